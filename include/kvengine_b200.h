@@ -1,0 +1,228 @@
+/*
+ * kvengine_b200 — C ABI of the B200 (sm_100a) speculative-decoding verify path.
+ *
+ * Every entry point takes raw device pointers, sizes and a cudaStream_t,
+ * launches asynchronously on that stream and returns an int status
+ * (KVE_OK == 0, negative on error; kve_last_error() has the message).
+ * Nothing here allocates device memory or throws: buffers and workspaces are
+ * owned by the caller. A workspace must be zero-filled once before its first
+ * use; the kernels leave it zeroed again when they finish.
+ *
+ * Device-side checks (an out-of-range slot or block id, a wait that ran out)
+ * never trap: the kernel skips the access and writes the first error code into
+ * `dev_status` (an int in device memory, may be NULL), which the caller reads.
+ *
+ * Each entry point names the reference code (kvengine, file:line) it replaces.
+ */
+#ifndef KVENGINE_B200_H
+#define KVENGINE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  KVE_OK = 0,
+  KVE_ERR_ARG = -1,        /* bad pointer, size or enum */
+  KVE_ERR_SHAPE = -2,      /* unsupported shape (e.g. head_dim not 64/128) */
+  KVE_ERR_DTYPE = -3,      /* unsupported dtype */
+  KVE_ERR_CUDA = -4,       /* a CUDA runtime/driver call failed */
+  KVE_ERR_TIMEOUT = -5,    /* a bounded device-side wait gave up */
+  KVE_ERR_WORKSPACE = -6,  /* workspace missing or too small */
+  KVE_ERR_BOUNDS = -7      /* device side: slot / block / token id out of range */
+};
+
+enum { KVE_F32 = 0, KVE_BF16 = 1 };
+
+/* GEMM epilogues: out[m, :] from acc[m, :] = sum_k x[m,k] * w[n,k].
+ *   STORE     out = round(acc)
+ *   BIAS      out = round(acc + bias[n])                (q/k/v projections)
+ *   RESIDUAL  out = round(residual + round(acc))        (o_proj, down_proj + residual add;
+ *                                                        out may alias residual)
+ *   SILU_MUL  w rows interleaved (2j = gate_j, 2j+1 = up_j); out has n/2 columns,
+ *             out[m, j] = round(round(silu(round(gate))) * round(up))   (Qwen2MLP) */
+enum { KVE_EPI_STORE = 0, KVE_EPI_BIAS = 1, KVE_EPI_RESIDUAL = 2, KVE_EPI_SILU_MUL = 3 };
+
+/* GEMM kernel selection for kve_gemm_ex: AUTO = tcgen05 for bf16, SIMT for fp32. */
+enum { KVE_GEMM_AUTO = 0, KVE_GEMM_SIMT = 1, KVE_GEMM_TCGEN05 = 2 };
+
+int kve_version(void);
+const char* kve_last_error(void);
+
+/* Fused greedy acceptance.
+ * Replaces kvengine/speculative.py:167-182: `target_preds = argmax(t_logits[u-1:])`
+ * over the k+1 verify rows, the longest prefix with preds[j] == drafts[j], and the
+ * emitted tokens drafts[:n] + [preds[n]] (preds[k] is the bonus when n == k).
+ * logits: [batch, k+1, vocab] rows `row_stride` elements apart (fp32 or bf16).
+ * drafts: int32, draft j of sequence b at drafts[b * draft_stride_b + j * draft_stride_j]
+ * ([batch, k] row-major is stride_b = k, stride_j = 1).
+ * Outputs (int32): preds [batch, k+1], n_accepted [batch], emitted [batch, k+1]
+ * (entries past n are -1). argmax ties resolve to the lowest index and NaN counts
+ * as the maximum, as torch.argmax does. 1 <= k <= 31. */
+size_t kve_greedy_accept_workspace_bytes(int batch);
+int kve_greedy_accept(const void* logits, int dtype, int64_t row_stride, const int32_t* drafts,
+                      int64_t draft_stride_b, int64_t draft_stride_j, int batch, int k, int vocab,
+                      int32_t* out_preds, int32_t* out_n_accepted, int32_t* out_emitted,
+                      void* workspace, size_t workspace_bytes, int* dev_status, cudaStream_t stream);
+
+/* Row argmax. Replaces the draft's `int(torch.argmax(logits[-1]))`
+ * (kvengine/speculative.py:155) and greedy decoding's argmax (kvengine/decode.py:303).
+ * x: [rows, cols] with `row_stride`; out: [rows] int32. Same tie/NaN rule as above. */
+int kve_argmax_rows(const void* x, int dtype, int rows, int cols, int64_t row_stride,
+                    int32_t* out, cudaStream_t stream);
+
+/* KV append: pool[slot_ids[t]] = new[t] for the K and V of one layer.
+ * Replaces `pool.k_flat[layer].index_copy_(0, slots, k_src)` and the V twin,
+ * kvengine/paged.py:310-311. k_new, v_new: [n_tokens, num_kv_heads, head_dim];
+ * pool_k, pool_v: the layer's flat view [num_slots, num_kv_heads, head_dim]
+ * (num_slots = num_blocks * block_size). Slots outside [0, num_slots) are skipped
+ * and reported as KVE_ERR_BOUNDS. */
+int kve_kv_append(const void* k_new, const void* v_new, int dtype, const int64_t* slot_ids,
+                  int n_tokens, int num_kv_heads, int head_dim, void* pool_k, void* pool_v,
+                  int64_t num_slots, int* dev_status, cudaStream_t stream);
+
+/* Fused rotary embedding + KV append for one layer.
+ * Replaces kvengine/forward.py:193-201: splitting the q/k/v projection output,
+ * `apply_rope` (forward.py:55-69, rotate-half pairing with cos/sin cast to the
+ * model dtype) and `cache.write`'s scatter (paged.py:310-311).
+ * qkv: [n_tokens, (num_heads + 2*num_kv_heads) * head_dim] (bias already added);
+ * positions, slots: [n_tokens] int32; rope_cos/sin: [rope_len, head_dim/2] fp32;
+ * q_out: [n_tokens, num_heads, head_dim]; pool_k/v as for kve_kv_append. */
+int kve_qkv_rope_append(const void* qkv, int dtype, int n_tokens, int num_heads, int num_kv_heads,
+                        int head_dim, const int32_t* positions, const int32_t* slots,
+                        const float* rope_cos, const float* rope_sin, int rope_len, void* q_out,
+                        void* pool_k, void* pool_v, int64_t num_slots, int* dev_status,
+                        cudaStream_t stream);
+
+/* Paged multi-query GQA verify attention, reading K/V blocks in place.
+ * Replaces the gather kvengine/paged.py:315-331 plus kvengine/forward.py:72-144
+ * (`repeat_kv`, `causal_mask`, `attend`): query row i of sequence b sits at
+ * position ctx_lens[b] - q_lens[b] + i and attends keys [0, position].
+ * q: [sum(q_lens), num_heads, head_dim] with sequence b's rows at q_offsets[b];
+ * pool_k/v: the layer's [num_blocks, block_size, num_kv_heads, head_dim];
+ * block_tables: [batch, table_stride] int32; out like q. head_dim in {64, 128}.
+ * Long contexts are split into fixed 512-key chunks combined in a fixed order
+ * (the result for a query depends only on its own keys, not on the batch). */
+size_t kve_paged_attn_workspace_bytes(int batch, int max_q_len, int max_ctx, int num_heads,
+                                      int num_kv_heads, int head_dim);
+int kve_paged_verify_attn(const void* q, int dtype, const void* pool_k, const void* pool_v,
+                          const int32_t* block_tables, int table_stride, const int32_t* ctx_lens,
+                          const int32_t* q_lens, const int32_t* q_offsets, int batch, int max_q_len,
+                          int max_ctx, int num_heads, int num_kv_heads, int head_dim, int block_size,
+                          int64_t num_blocks, float scale, void* out, void* workspace,
+                          size_t workspace_bytes, int* dev_status, cudaStream_t stream);
+
+/* Contiguous K/V history of one sequence: out[h, t, :] = pool[table[t / bs], t % bs, h, :]
+ * for t < length. Replaces kvengine/paged.py:315-331 (`_gather`) where a caller
+ * still wants the materialised history (the KVCacheLike `write` return value). */
+int kve_gather_kv(const void* pool, int dtype, const int32_t* block_table, int length,
+                  int num_kv_heads, int head_dim, int block_size, int64_t num_blocks, void* out,
+                  int* dev_status, cudaStream_t stream);
+
+/* Token embedding gather. Replaces `inner.embed_tokens(input_ids)`, kvengine/forward.py:176. */
+int kve_embed(const int32_t* ids, int n_tokens, const void* table, int dtype, int hidden, int vocab,
+              void* out, int* dev_status, cudaStream_t stream);
+
+/* RMSNorm (Qwen2RMSNorm): out = w * round(x * rsqrt(mean(x^2) + eps)), computed in fp32.
+ * Replaces input_layernorm / post_attention_layernorm / model.norm,
+ * kvengine/forward.py:191,207,212. Optional row_index [rows] gathers input rows
+ * (the final norm runs only on the rows whose logits are needed). */
+int kve_rmsnorm(const void* x, int dtype, const float* weight, int rows, int hidden, float eps,
+                const int32_t* row_index, void* out, cudaStream_t stream);
+
+/* Linear layer y = x w^T with a fused epilogue (see KVE_EPI_*).
+ * Replaces the nn.Linear calls of kvengine/forward.py:194-196 (q/k/v), :204 (o_proj),
+ * :207 (Qwen2MLP gate/up/down) and :215 (lm_head).
+ * x: [m, k]; w: [n, k] (row-major, k contiguous); out: [m, n] (or [m, n/2] for
+ * SILU_MUL) in out_dtype. bf16 runs on tcgen05 tensor cores (fp32 accumulate in
+ * TMEM), fp32 on a CUDA-core kernel whose per-element reduction order does not
+ * depend on m (draft and verify passes of the same model agree bit for bit). */
+size_t kve_gemm_workspace_bytes(int m, int n, int k, int dtype);
+int kve_gemm(const void* x, const void* w, int dtype, int m, int n, int k, int epilogue,
+             const float* bias, const void* residual, void* out, int out_dtype, void* workspace,
+             size_t workspace_bytes, int* dev_status, cudaStream_t stream);
+int kve_gemm_ex(const void* x, const void* w, int dtype, int m, int n, int k, int epilogue,
+                const float* bias, const void* residual, void* out, int out_dtype, void* workspace,
+                size_t workspace_bytes, int* dev_status, int algo, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Whole forward pass (one call launches every kernel of one model pass).
+ * Replaces kvengine/forward.py:147-215 (`forward_with_own_cache`) generalised
+ * to a ragged batch: sequence b feeds q_lens[b] new tokens that occupy
+ * positions [ctx_lens[b] - q_lens[b], ctx_lens[b]) of its paged cache.
+ * Order per layer: rmsnorm -> qkv GEMM (+bias) -> rope + KV append ->
+ * paged attention -> o_proj GEMM (+residual) -> rmsnorm -> gate/up GEMM
+ * (SwiGLU epilogue) -> down GEMM (+residual); then the final rmsnorm over the
+ * `out_rows` rows and the lm_head GEMM into `logits`.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  const void* w_qkv;   /* [q+2kv, hidden] */
+  const float* b_qkv;  /* [q+2kv] */
+  const void* w_o;     /* [hidden, q] */
+  const void* w_gu;    /* [2*inter, hidden], gate/up rows interleaved */
+  const void* w_down;  /* [hidden, inter] */
+  const float* ln1;    /* [hidden] */
+  const float* ln2;    /* [hidden] */
+  void* pool_k;        /* this layer's [num_blocks, block_size, kv_heads, head_dim] */
+  void* pool_v;
+} kve_layer_t;
+
+typedef struct {
+  int dtype;  /* KVE_F32 or KVE_BF16: weights, activations and cache */
+  int num_layers, hidden, num_heads, num_kv_heads, head_dim, intermediate, vocab;
+  float rms_eps;
+  const kve_layer_t* layers; /* host array [num_layers] */
+  const void* embed;         /* [vocab, hidden] */
+  const void* lm_head;       /* [vocab, hidden] */
+  const float* final_norm;   /* [hidden] */
+  const float* rope_cos;     /* [rope_len, head_dim/2] */
+  const float* rope_sin;
+  int rope_len;
+  int64_t num_blocks;
+  int block_size;
+} kve_model_t;
+
+typedef struct {
+  int n_tokens, n_seqs, max_q_len, max_ctx;
+  const int32_t* ids;        /* [n_tokens] */
+  const int32_t* positions;  /* [n_tokens] */
+  const int32_t* slots;      /* [n_tokens] flat slot = block * block_size + offset */
+  const int32_t* q_lens;     /* [n_seqs] */
+  const int32_t* q_offsets;  /* [n_seqs + 1] */
+  const int32_t* ctx_lens;   /* [n_seqs] */
+  const int32_t* block_tables; /* [n_seqs, table_stride] */
+  int table_stride;
+  int n_out;                 /* rows whose logits are computed */
+  const int32_t* out_rows;   /* [n_out] token rows, or NULL for rows 0..n_out-1 */
+  void* logits;              /* [n_out, vocab] in logits_dtype */
+  int logits_dtype;
+} kve_batch_t;
+
+typedef struct {
+  void* hidden;   /* [n_tokens, hidden] residual stream */
+  void* normed;   /* [n_tokens, hidden] */
+  void* qkv;      /* [n_tokens, q+2kv] */
+  void* q;        /* [n_tokens, q] */
+  void* attn;     /* [n_tokens, q] */
+  void* act;      /* [n_tokens, inter] */
+  void* out_normed; /* [n_out, hidden] */
+  void* gemm_ws; size_t gemm_ws_bytes;
+  void* attn_ws; size_t attn_ws_bytes;
+  int* dev_status;
+} kve_scratch_t;
+
+/* Bytes the two workspaces of kve_forward need for a batch of this size. */
+size_t kve_forward_gemm_ws_bytes(const kve_model_t* model, int n_tokens, int n_out);
+size_t kve_forward_attn_ws_bytes(const kve_model_t* model, int n_seqs, int max_q_len, int max_ctx);
+int kve_forward(const kve_model_t* model, const kve_batch_t* batch, const kve_scratch_t* scratch,
+                cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVENGINE_B200_H */

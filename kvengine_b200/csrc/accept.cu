@@ -1,0 +1,202 @@
+// Fused greedy acceptance (argmax over the vocab for every verify row, prefix
+// match against the drafts, emitted tokens) and a plain row-argmax kernel.
+//
+// One CTA scans one 151,936-wide logits row with 16-byte loads (HBM-bound:
+// the row is read exactly once). The last CTA to finish a sequence's k+1 rows
+// (per-sequence arrival counter in the workspace) runs the acceptance with a
+// warp ballot and resets the counter to zero, so the workspace stays clean.
+#include <math.h>
+
+#include "kve_common.cuh"
+
+namespace kve {
+namespace {
+
+constexpr int kArgmaxThreads = 512;
+
+// (v1, i1) beats (v2, i2): NaN is the maximum (torch.argmax semantics), larger
+// values win, equal values resolve to the lower index.
+__device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
+  bool n1 = isnan(v1), n2 = isnan(v2);
+  if (n1 || n2) return (n1 && n2) ? (i1 < i2) : n1;
+  if (v1 != v2) return v1 > v2;
+  return i1 < i2;
+}
+
+template <typename T> struct Vec;
+template <> struct Vec<float> {
+  static constexpr int N = 4;
+  static __device__ __forceinline__ void load(const float* p, float (&o)[4]) {
+    float4 v = __ldcs(reinterpret_cast<const float4*>(p));
+    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+  }
+};
+template <> struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&o)[8]) {
+    uint4 v = __ldcs(reinterpret_cast<const uint4*>(p));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      o[2 * j] = f.x; o[2 * j + 1] = f.y;
+    }
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ int row_argmax(const T* x, int cols, bool vec_ok) {
+  float best_v = -INFINITY;
+  int best_i = 0x7fffffff;
+  constexpr int N = Vec<T>::N;
+  int nvec = vec_ok ? cols / N : 0;
+  constexpr int U = 4;
+  int v = threadIdx.x;
+  for (; v + (U - 1) * kArgmaxThreads < nvec; v += U * kArgmaxThreads) {
+    float buf[U][N];
+#pragma unroll
+    for (int u = 0; u < U; ++u) Vec<T>::load(x + (size_t)(v + u * kArgmaxThreads) * N, buf[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      int base = (v + u * kArgmaxThreads) * N;
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+        if (better(buf[u][j], base + j, best_v, best_i)) { best_v = buf[u][j]; best_i = base + j; }
+    }
+  }
+  for (; v < nvec; v += kArgmaxThreads) {
+    float buf[N];
+    Vec<T>::load(x + (size_t)v * N, buf);
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+      if (better(buf[j], v * N + j, best_v, best_i)) { best_v = buf[j]; best_i = v * N + j; }
+  }
+  for (int i = nvec * N + threadIdx.x; i < cols; i += kArgmaxThreads) {
+    float f = Elem<T>::to_f(x[i]);
+    if (better(f, i, best_v, best_i)) { best_v = f; best_i = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+    int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    if (better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
+  }
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int si[kArgmaxThreads / 32];
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = best_v; si[warp] = best_i; }
+  __syncthreads();
+  if (warp == 0) {
+    best_v = lane < kArgmaxThreads / 32 ? sv[lane] : -INFINITY;
+    best_i = lane < kArgmaxThreads / 32 ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+      int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+      if (better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
+    }
+  }
+  return best_i;  // valid in thread 0
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kArgmaxThreads)
+accept_kernel(const T* __restrict__ logits, int64_t row_stride, const int32_t* __restrict__ drafts,
+              int64_t dsb, int64_t dsj, int k, int vocab, bool vec_ok, int32_t* __restrict__ preds, int32_t* __restrict__ n_acc,
+              int32_t* __restrict__ emitted, int32_t* __restrict__ counters) {
+  const int row = blockIdx.x;
+  const int b = row / (k + 1);
+  int best = row_argmax(logits + (size_t)row * row_stride, vocab, vec_ok);
+  __shared__ int is_last;
+  if (threadIdx.x == 0) {
+    preds[row] = best;
+    __threadfence();
+    int prev = atomicAdd(&counters[b], 1);
+    is_last = (prev == k);
+    if (is_last) counters[b] = 0;  // every row of b has arrived: leave the workspace zeroed
+  }
+  __syncthreads();
+  if (!is_last || threadIdx.x >= 32) return;
+  __threadfence();
+  const int lane = threadIdx.x;
+  int p = lane <= k ? __ldcg(preds + (size_t)b * (k + 1) + lane) : -1;
+  int d = lane < k ? drafts[b * dsb + lane * dsj] : -1;
+  unsigned mism = __ballot_sync(0xffffffffu, lane < k && p != d);
+  int n = mism ? (__ffs(mism) - 1) : k;
+  int pn = __shfl_sync(0xffffffffu, p, n);
+  if (lane <= k) {
+    int e = lane < n ? d : (lane == n ? pn : -1);
+    emitted[(size_t)b * (k + 1) + lane] = e;
+  }
+  if (lane == 0) n_acc[b] = n;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kArgmaxThreads)
+argmax_kernel(const T* __restrict__ x, int64_t row_stride, int cols, bool vec_ok, int32_t* __restrict__ out) {
+  int best = row_argmax(x + (size_t)blockIdx.x * row_stride, cols, vec_ok);
+  if (threadIdx.x == 0) out[blockIdx.x] = best;
+}
+
+bool vec_aligned(const void* p, int64_t row_stride, int elem) {
+  return ((uintptr_t)p % 16 == 0) && ((row_stride * elem) % 16 == 0);
+}
+
+}  // namespace
+}  // namespace kve
+
+using namespace kve;
+
+extern "C" size_t kve_greedy_accept_workspace_bytes(int batch) {
+  size_t b = (size_t)(batch > 0 ? batch : 0) * sizeof(int32_t);
+  return (b + 255) / 256 * 256;
+}
+
+extern "C" int kve_greedy_accept(const void* logits, int dtype, int64_t row_stride,
+                                 const int32_t* drafts, int64_t draft_stride_b, int64_t draft_stride_j, int batch, int k, int vocab,
+                                 int32_t* out_preds, int32_t* out_n_accepted, int32_t* out_emitted,
+                                 void* workspace, size_t workspace_bytes, int* dev_status,
+                                 cudaStream_t stream) {
+  (void)dev_status;
+  if (batch < 0 || k < 1 || k > 31 || vocab < 1 || row_stride < vocab)
+    return set_error(KVE_ERR_ARG, "kve_greedy_accept: bad sizes batch=%d k=%d vocab=%d stride=%lld",
+                     batch, k, vocab, (long long)row_stride);
+  if (batch == 0) return KVE_OK;
+  if (!logits || !drafts || !out_preds || !out_n_accepted || !out_emitted)
+    return set_error(KVE_ERR_ARG, "kve_greedy_accept: null pointer");
+  if (!workspace || workspace_bytes < kve_greedy_accept_workspace_bytes(batch))
+    return set_error(KVE_ERR_WORKSPACE, "kve_greedy_accept: workspace needs %zu bytes",
+                     kve_greedy_accept_workspace_bytes(batch));
+  dim3 grid(batch * (k + 1));
+  int32_t* counters = static_cast<int32_t*>(workspace);
+  if (dtype == KVE_F32) {
+    accept_kernel<float><<<grid, kArgmaxThreads, 0, stream>>>(
+        static_cast<const float*>(logits), row_stride, drafts, draft_stride_b, draft_stride_j, k, vocab,
+        vec_aligned(logits, row_stride, 4), out_preds, out_n_accepted, out_emitted, counters);
+  } else if (dtype == KVE_BF16) {
+    accept_kernel<__nv_bfloat16><<<grid, kArgmaxThreads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(logits), row_stride, drafts, draft_stride_b, draft_stride_j, k, vocab,
+        vec_aligned(logits, row_stride, 2), out_preds, out_n_accepted, out_emitted, counters);
+  } else {
+    return set_error(KVE_ERR_DTYPE, "kve_greedy_accept: dtype %d", dtype);
+  }
+  return check_launch("kve_greedy_accept");
+}
+
+extern "C" int kve_argmax_rows(const void* x, int dtype, int rows, int cols, int64_t row_stride,
+                               int32_t* out, cudaStream_t stream) {
+  if (rows < 0 || cols < 1 || row_stride < cols)
+    return set_error(KVE_ERR_ARG, "kve_argmax_rows: bad sizes");
+  if (rows == 0) return KVE_OK;
+  if (!x || !out) return set_error(KVE_ERR_ARG, "kve_argmax_rows: null pointer");
+  if (dtype == KVE_F32) {
+    argmax_kernel<float><<<rows, kArgmaxThreads, 0, stream>>>(
+        static_cast<const float*>(x), row_stride, cols, vec_aligned(x, row_stride, 4), out);
+  } else if (dtype == KVE_BF16) {
+    argmax_kernel<__nv_bfloat16><<<rows, kArgmaxThreads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), row_stride, cols, vec_aligned(x, row_stride, 2), out);
+  } else {
+    return set_error(KVE_ERR_DTYPE, "kve_argmax_rows: dtype %d", dtype);
+  }
+  return check_launch("kve_argmax_rows");
+}

@@ -1,0 +1,23 @@
+// Library-wide C ABI pieces: version and the thread-local error message.
+#include <cstdarg>
+#include <cstdio>
+
+#include "kve_common.cuh"
+
+namespace kve {
+
+static thread_local char g_last_error[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+}  // namespace kve
+
+extern "C" int kve_version(void) { return 1; }
+
+extern "C" const char* kve_last_error(void) { return kve::g_last_error; }

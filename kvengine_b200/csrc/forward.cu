@@ -1,0 +1,76 @@
+// kve_forward: the launch sequence of one model pass over a ragged batch.
+// Host code only; every kernel it launches is one of the library's entry points.
+#include "kve_common.cuh"
+
+namespace {
+
+inline size_t max3(size_t a, size_t b, size_t c) { return a > b ? (a > c ? a : c) : (b > c ? b : c); }
+
+#define KVE_TRY(expr)          \
+  do {                         \
+    int _rc = (expr);          \
+    if (_rc != KVE_OK) return _rc; \
+  } while (0)
+
+}  // namespace
+
+using namespace kve;
+
+extern "C" size_t kve_forward_gemm_ws_bytes(const kve_model_t* m, int n_tokens, int n_out) {
+  if (!m || n_tokens <= 0) return 0;
+  int qkv = (m->num_heads + 2 * m->num_kv_heads) * m->head_dim;
+  int q = m->num_heads * m->head_dim;
+  size_t a = kve_gemm_workspace_bytes(n_tokens, qkv, m->hidden, m->dtype);
+  size_t b = kve_gemm_workspace_bytes(n_tokens, m->hidden, q, m->dtype);
+  size_t c = kve_gemm_workspace_bytes(n_tokens, 2 * m->intermediate, m->hidden, m->dtype);
+  size_t d = kve_gemm_workspace_bytes(n_tokens, m->hidden, m->intermediate, m->dtype);
+  size_t e = n_out > 0 ? kve_gemm_workspace_bytes(n_out, m->vocab, m->hidden, m->dtype) : 0;
+  size_t r = max3(a, b, c);
+  return max3(r, d, e);
+}
+
+extern "C" size_t kve_forward_attn_ws_bytes(const kve_model_t* m, int n_seqs, int max_q_len, int max_ctx) {
+  if (!m) return 0;
+  return kve_paged_attn_workspace_bytes(n_seqs, max_q_len, max_ctx, m->num_heads, m->num_kv_heads, m->head_dim);
+}
+
+extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve_scratch_t* s,
+                           cudaStream_t stream) {
+  if (!m || !b || !s || !m->layers) return set_error(KVE_ERR_ARG, "kve_forward: null argument");
+  if (b->n_tokens < 0 || b->n_seqs < 0 || b->n_out < 0)
+    return set_error(KVE_ERR_ARG, "kve_forward: bad batch sizes");
+  if (b->n_tokens == 0) return KVE_OK;
+  const int dt = m->dtype;
+  const int H = m->hidden, M = b->n_tokens;
+  const int qsz = m->num_heads * m->head_dim;
+  const int qkv = qsz + 2 * m->num_kv_heads * m->head_dim;
+  const int64_t num_slots = m->num_blocks * m->block_size;
+  const float scale = 1.0f / sqrtf((float)m->head_dim);
+
+  KVE_TRY(kve_embed(b->ids, M, m->embed, dt, H, m->vocab, s->hidden, s->dev_status, stream));
+  for (int l = 0; l < m->num_layers; ++l) {
+    const kve_layer_t& L = m->layers[l];
+    KVE_TRY(kve_rmsnorm(s->hidden, dt, L.ln1, M, H, m->rms_eps, nullptr, s->normed, stream));
+    KVE_TRY(kve_gemm(s->normed, L.w_qkv, dt, M, qkv, H, KVE_EPI_BIAS, L.b_qkv, nullptr, s->qkv, dt,
+                     s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
+    KVE_TRY(kve_qkv_rope_append(s->qkv, dt, M, m->num_heads, m->num_kv_heads, m->head_dim, b->positions,
+                                b->slots, m->rope_cos, m->rope_sin, m->rope_len, s->q, L.pool_k, L.pool_v,
+                                num_slots, s->dev_status, stream));
+    KVE_TRY(kve_paged_verify_attn(s->q, dt, L.pool_k, L.pool_v, b->block_tables, b->table_stride, b->ctx_lens,
+                                  b->q_lens, b->q_offsets, b->n_seqs, b->max_q_len, b->max_ctx, m->num_heads,
+                                  m->num_kv_heads, m->head_dim, m->block_size, m->num_blocks, scale, s->attn,
+                                  s->attn_ws, s->attn_ws_bytes, s->dev_status, stream));
+    KVE_TRY(kve_gemm(s->attn, L.w_o, dt, M, H, qsz, KVE_EPI_RESIDUAL, nullptr, s->hidden, s->hidden, dt,
+                     s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
+    KVE_TRY(kve_rmsnorm(s->hidden, dt, L.ln2, M, H, m->rms_eps, nullptr, s->normed, stream));
+    KVE_TRY(kve_gemm(s->normed, L.w_gu, dt, M, 2 * m->intermediate, H, KVE_EPI_SILU_MUL, nullptr, nullptr,
+                     s->act, dt, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
+    KVE_TRY(kve_gemm(s->act, L.w_down, dt, M, H, m->intermediate, KVE_EPI_RESIDUAL, nullptr, s->hidden,
+                     s->hidden, dt, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
+  }
+  if (b->n_out == 0) return KVE_OK;
+  KVE_TRY(kve_rmsnorm(s->hidden, dt, m->final_norm, b->n_out, H, m->rms_eps, b->out_rows, s->out_normed, stream));
+  KVE_TRY(kve_gemm(s->out_normed, m->lm_head, dt, b->n_out, m->vocab, H, KVE_EPI_STORE, nullptr, nullptr,
+                   b->logits, b->logits_dtype, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
+  return KVE_OK;
+}

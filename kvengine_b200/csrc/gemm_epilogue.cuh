@@ -1,0 +1,65 @@
+// GEMM epilogues shared by the CUDA-core and tcgen05 kernels. Rounding points
+// follow the reference's module-by-module torch ops in the model dtype:
+// nn.Linear output rounded once (bias added before that rounding), the
+// residual add rounded again, SwiGLU as round(round(silu(round(g))) * round(u)).
+#pragma once
+
+#include <math.h>
+
+#include "kve_common.cuh"
+
+namespace kve {
+
+struct EpiArgs {
+  int mode;           // KVE_EPI_*
+  int out_dtype;      // KVE_F32 / KVE_BF16 (the dtype rounding happens in)
+  int ld_out;         // leading dimension of out (n, or n/2 for SILU_MUL)
+  const float* bias;  // [n] (BIAS)
+  const void* residual;  // [m, n] in out_dtype (RESIDUAL); may alias out
+  void* out;
+};
+
+__device__ __forceinline__ float round_to(int dtype, float v) {
+  return dtype == KVE_BF16 ? Elem<__nv_bfloat16>::round(v) : v;
+}
+
+__device__ __forceinline__ void write_out(const EpiArgs& e, int row, int col, float v) {
+  size_t idx = (size_t)row * e.ld_out + col;
+  if (e.out_dtype == KVE_BF16) static_cast<__nv_bfloat16*>(e.out)[idx] = __float2bfloat16_rn(v);
+  else static_cast<float*>(e.out)[idx] = v;
+}
+
+__device__ __forceinline__ float read_res(const EpiArgs& e, int row, int col) {
+  size_t idx = (size_t)row * e.ld_out + col;
+  if (e.out_dtype == KVE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(e.residual)[idx]);
+  return static_cast<const float*>(e.residual)[idx];
+}
+
+// STORE / BIAS / RESIDUAL for one element.
+__device__ __forceinline__ void epi_store(const EpiArgs& e, int row, int col, float acc) {
+  float v = acc;
+  if (e.mode == KVE_EPI_BIAS) {
+    v = __fadd_rn(acc, e.bias[col]);
+  } else if (e.mode == KVE_EPI_RESIDUAL) {
+    v = __fadd_rn(read_res(e, row, col), round_to(e.out_dtype, acc));
+  }
+  write_out(e, row, col, v);
+}
+
+__device__ __forceinline__ float silu_ref(float g) { return g / (1.0f + expf(-g)); }
+
+// SwiGLU pair: gate and up accumulators of output column j.
+__device__ __forceinline__ void epi_silu_mul(const EpiArgs& e, int row, int j, float gate, float up) {
+  float g = round_to(e.out_dtype, gate);
+  float u = round_to(e.out_dtype, up);
+  float s = round_to(e.out_dtype, silu_ref(g));
+  write_out(e, row, j, __fmul_rn(s, u));
+}
+
+int gemm_simt(const void* x, const void* w, int dtype, int m, int n, int k, const EpiArgs& e,
+              cudaStream_t stream);
+int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e, void* workspace,
+            size_t workspace_bytes, int* status, cudaStream_t stream);
+size_t gemm_tc_workspace_bytes(int m, int n, int k);
+
+}  // namespace kve

@@ -1,0 +1,185 @@
+"""Torch-tensor wrappers over the C ABI, one per kernel entry point.
+
+Each wrapper checks shapes, dtypes and devices on the host, then launches on
+the current CUDA stream. Workspaces are plain zero-filled uint8 tensors the
+caller keeps (the kernels leave them zeroed).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+    return torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def status_tensor(device) -> torch.Tensor:
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def check_status(status: torch.Tensor) -> None:
+    """Raise if a kernel recorded a device-side error (syncs on `status`)."""
+    code = int(status.item())
+    if code != 0:
+        status.zero_()
+        raise L.KveError(code, "device-side check failed (see the op that wrote dev_status)")
+
+
+class Workspace:
+    """A grow-only zero-filled device scratch buffer."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.buf = _ws(256, self.device)
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if nbytes > self.buf.numel():
+            self.buf = _ws(int(nbytes * 1.25) + 4096, self.device)
+        return self.buf
+
+
+def greedy_accept(logits: torch.Tensor, drafts: torch.Tensor, workspace: Workspace | None = None,
+                  status: torch.Tensor | None = None):
+    """logits [B, k+1, V] (fp32/bf16), drafts [B, k] (any int strides) ->
+    (preds [B, k+1], n_accepted [B], emitted [B, k+1]) int32."""
+    lib = L.load()
+    L.require_cuda(logits, drafts)
+    B, kp1, V = logits.shape
+    k = kp1 - 1
+    if drafts.dtype != torch.int32 or tuple(drafts.shape) != (B, k):
+        raise ValueError("drafts must be int32 [B, k]")
+    if logits.stride(2) != 1 or logits.stride(0) != kp1 * logits.stride(1):
+        raise ValueError("logits rows must be evenly strided with unit column stride")
+    dev = logits.device
+    preds = torch.empty(B, kp1, dtype=torch.int32, device=dev)
+    n_acc = torch.empty(B, dtype=torch.int32, device=dev)
+    emitted = torch.empty(B, kp1, dtype=torch.int32, device=dev)
+    ws = (workspace or Workspace(dev)).get(lib.kve_greedy_accept_workspace_bytes(B))
+    L.check(lib.kve_greedy_accept(
+        logits.data_ptr(), L.dtype_code(logits.dtype), logits.stride(1), drafts.data_ptr(),
+        drafts.stride(0), drafts.stride(1), B, k, V, preds.data_ptr(), n_acc.data_ptr(),
+        emitted.data_ptr(), ws.data_ptr(), ws.numel(), L.ptr(status), L.stream_handle(dev)))
+    return preds, n_acc, emitted
+
+
+def argmax_rows(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    lib = L.load()
+    L.require_cuda(x)
+    rows, cols = x.shape
+    if x.stride(1) != 1:
+        raise ValueError("argmax_rows needs unit column stride")
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=x.device)
+    L.check(lib.kve_argmax_rows(x.data_ptr(), L.dtype_code(x.dtype), rows, cols, x.stride(0),
+                                out.data_ptr(), L.stream_handle(x.device)))
+    return out
+
+
+def kv_append(k_new, v_new, slot_ids, pool_k_layer, pool_v_layer, status=None) -> None:
+    """pool[slot] = new rows; pool_*_layer: [num_blocks, bs, nkv, hd] (one layer)."""
+    lib = L.load()
+    L.require_cuda(k_new, v_new, slot_ids, pool_k_layer, pool_v_layer)
+    n, nkv, hd = k_new.shape
+    num_slots = pool_k_layer.shape[0] * pool_k_layer.shape[1]
+    for t in (k_new, v_new, pool_k_layer, pool_v_layer):
+        if not t.is_contiguous() or t.dtype != k_new.dtype:
+            raise ValueError("kv_append operands must be contiguous and share a dtype")
+    if slot_ids.dtype != torch.int64:
+        raise ValueError("slot_ids must be int64 (as index_copy_ takes)")
+    L.check(lib.kve_kv_append(k_new.data_ptr(), v_new.data_ptr(), L.dtype_code(k_new.dtype),
+                              slot_ids.data_ptr(), n, nkv, hd, pool_k_layer.data_ptr(),
+                              pool_v_layer.data_ptr(), num_slots, L.ptr(status),
+                              L.stream_handle(k_new.device)))
+
+
+def qkv_rope_append(qkv, positions, slots, rope_cos, rope_sin, q_out, pool_k_layer, pool_v_layer,
+                    num_heads, num_kv_heads, head_dim, status=None) -> None:
+    lib = L.load()
+    n = qkv.shape[0]
+    num_slots = pool_k_layer.shape[0] * pool_k_layer.shape[1]
+    L.check(lib.kve_qkv_rope_append(qkv.data_ptr(), L.dtype_code(qkv.dtype), n, num_heads, num_kv_heads,
+                                    head_dim, positions.data_ptr(), slots.data_ptr(), rope_cos.data_ptr(),
+                                    rope_sin.data_ptr(), rope_cos.shape[0], q_out.data_ptr(),
+                                    pool_k_layer.data_ptr(), pool_v_layer.data_ptr(), num_slots,
+                                    L.ptr(status), L.stream_handle(qkv.device)))
+
+
+def paged_attention(q, pool_k_layer, pool_v_layer, block_tables, ctx_lens, q_lens, q_offsets,
+                    max_q_len: int, max_ctx: int, scale: float, out=None, workspace: Workspace | None = None,
+                    status=None) -> torch.Tensor:
+    """q [sum q_lens, nq, hd]; pools [num_blocks, bs, nkv, hd]; int32 tables/lengths."""
+    lib = L.load()
+    L.require_cuda(q, pool_k_layer, pool_v_layer, block_tables, ctx_lens, q_lens, q_offsets)
+    _, nq, hd = q.shape
+    num_blocks, bs, nkv, _ = pool_k_layer.shape
+    B = ctx_lens.shape[0]
+    for t in (block_tables, ctx_lens, q_lens, q_offsets):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError("tables and lengths must be contiguous int32")
+    if out is None:
+        out = torch.empty_like(q)
+    need = lib.kve_paged_attn_workspace_bytes(B, max_q_len, max_ctx, nq, nkv, hd)
+    ws = (workspace or Workspace(q.device)).get(need) if need else None
+    L.check(lib.kve_paged_verify_attn(
+        q.data_ptr(), L.dtype_code(q.dtype), pool_k_layer.data_ptr(), pool_v_layer.data_ptr(),
+        block_tables.data_ptr(), block_tables.shape[1], ctx_lens.data_ptr(), q_lens.data_ptr(),
+        q_offsets.data_ptr(), B, max_q_len, max_ctx, nq, nkv, hd, bs, num_blocks, scale, out.data_ptr(),
+        L.ptr(ws), 0 if ws is None else ws.numel(), L.ptr(status), L.stream_handle(q.device)))
+    return out
+
+
+def gather_kv(pool_layer, block_table, length: int, status=None) -> torch.Tensor:
+    """[nkv, length, hd] history of one sequence (pool_layer [num_blocks, bs, nkv, hd])."""
+    lib = L.load()
+    num_blocks, bs, nkv, hd = pool_layer.shape
+    out = torch.empty(nkv, length, hd, dtype=pool_layer.dtype, device=pool_layer.device)
+    L.check(lib.kve_gather_kv(pool_layer.data_ptr(), L.dtype_code(pool_layer.dtype), block_table.data_ptr(),
+                              length, nkv, hd, bs, num_blocks, out.data_ptr(), L.ptr(status),
+                              L.stream_handle(pool_layer.device)))
+    return out
+
+
+def embed(ids, table, out=None, status=None):
+    lib = L.load()
+    n = ids.shape[0]
+    vocab, hidden = table.shape
+    if out is None:
+        out = torch.empty(n, hidden, dtype=table.dtype, device=table.device)
+    L.check(lib.kve_embed(ids.data_ptr(), n, table.data_ptr(), L.dtype_code(table.dtype), hidden, vocab,
+                          out.data_ptr(), L.ptr(status), L.stream_handle(table.device)))
+    return out
+
+
+def rmsnorm(x, weight, eps: float, row_index=None, out=None):
+    lib = L.load()
+    rows = x.shape[0] if row_index is None else row_index.shape[0]
+    hidden = x.shape[1]
+    if out is None:
+        out = torch.empty(rows, hidden, dtype=x.dtype, device=x.device)
+    L.check(lib.kve_rmsnorm(x.data_ptr(), L.dtype_code(x.dtype), weight.data_ptr(), rows, hidden, eps,
+                            L.ptr(row_index), out.data_ptr(), L.stream_handle(x.device)))
+    return out
+
+
+def gemm(x, w, epilogue: int = L.EPI_STORE, bias=None, residual=None, out=None, out_dtype=None,
+         workspace: Workspace | None = None, status=None, algo: int = L.GEMM_AUTO) -> torch.Tensor:
+    lib = L.load()
+    L.require_cuda(x, w)
+    m, k = x.shape
+    n = w.shape[0]
+    if w.shape[1] != k or x.dtype != w.dtype or not x.is_contiguous() or not w.is_contiguous():
+        raise ValueError("gemm: x [m,k] and w [n,k] must be contiguous and share a dtype")
+    out_dtype = out_dtype or x.dtype
+    n_out = n // 2 if epilogue == L.EPI_SILU_MUL else n
+    if out is None:
+        out = torch.empty(m, n_out, dtype=out_dtype, device=x.device)
+    dc = L.dtype_code(x.dtype)
+    need = lib.kve_gemm_workspace_bytes(m, n, k, dc)
+    ws = (workspace or Workspace(x.device)).get(need) if need else None
+    L.check(lib.kve_gemm_ex(x.data_ptr(), w.data_ptr(), dc, m, n, k, epilogue, L.ptr(bias), L.ptr(residual),
+                            out.data_ptr(), L.dtype_code(out_dtype), L.ptr(ws), 0 if ws is None else ws.numel(),
+                            L.ptr(status), algo, L.stream_handle(x.device)))
+    return out

@@ -1,0 +1,263 @@
+"""Greedy speculative decoding with draft, verify and accept on the device.
+
+Same API and result type as kvengine/speculative.py:53-216:
+`speculative_greedy(target_model, draft_model, input_ids, target_cache,
+draft_cache, k=4, max_new_tokens=32, eos_token_id=AUTO_EOS) -> SpecDecodeResult`,
+with identical bookkeeping (u unseen target tokens + k drafts fed in one
+verify pass, rows u-1 .. u-1+k predict drafts[0..k-1] and the bonus, the
+longest matching prefix is accepted and the first disagreement resolved in
+the target's favour, both caches truncated to len(tokens)-1, trims at EOS and
+at the budget).
+
+What differs is where it runs. `speculative_greedy_batch` advances many
+requests together: per iteration one ragged draft pass (each request's unseen
+tokens), k-1 one-token draft passes whose inputs are the previous argmax
+kernel's outputs (no host sync between draft tokens), one verify pass over
+B*(u+k) rows, and the fused accept kernel. The host sees one small
+device->host copy per iteration (accepted counts and emitted tokens) and
+does the block-table bookkeeping. `speculative_greedy` is the batch of one.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import ops
+from .decode import AUTO_EOS, _resolve_eos, _sync
+from .forward import runner_for
+from .model import ForwardPlan, SeqSpec, as_model
+
+
+@dataclass
+class SpecDecodeResult:
+    prompt_token_ids: list[int]
+    new_token_ids: list[int]
+    elapsed_s: float
+    stopped_on_eos: bool
+    iterations: int = 0
+    tokens_drafted: int = 0
+    tokens_accepted: int = 0
+    accepted_per_iter: list[int] = field(default_factory=list)
+    target_forwards: int = 0
+    draft_forwards: int = 0
+
+    @property
+    def tokens_per_s(self) -> float:
+        return len(self.new_token_ids) / self.elapsed_s if self.elapsed_s else 0.0
+
+    @property
+    def acceptance_rate(self) -> float:
+        return self.tokens_accepted / self.tokens_drafted if self.tokens_drafted else 0.0
+
+    @property
+    def tokens_per_target_forward(self) -> float:
+        return len(self.new_token_ids) / self.target_forwards if self.target_forwards else 0.0
+
+    def summary(self) -> dict:
+        return {
+            "new_tokens": len(self.new_token_ids),
+            "elapsed_s": round(self.elapsed_s, 3),
+            "tokens_per_s": round(self.tokens_per_s, 2),
+            "iterations": self.iterations,
+            "tokens_drafted": self.tokens_drafted,
+            "tokens_accepted": self.tokens_accepted,
+            "acceptance_rate": round(self.acceptance_rate, 4),
+            "tokens_per_target_forward": round(self.tokens_per_target_forward, 3),
+            "target_forwards": self.target_forwards,
+            "draft_forwards": self.draft_forwards,
+            "stopped_on_eos": self.stopped_on_eos,
+        }
+
+
+class _Request:
+    __slots__ = ("tokens", "t_seq", "d_seq", "res", "max_new", "done", "u_d", "u_t")
+
+    def __init__(self, prompt, t_seq, d_seq, max_new):
+        self.tokens = list(prompt)
+        self.t_seq = t_seq
+        self.d_seq = d_seq
+        self.res = SpecDecodeResult(list(prompt), [], 0.0, False)
+        self.max_new = max_new
+        self.done = max_new <= 0
+        self.u_d = self.u_t = 0
+
+
+class SpecEngine:
+    """Batched draft/verify/accept loop over one target and one draft model."""
+
+    def __init__(self, target, draft, target_pool, draft_pool, k: int):
+        assert k >= 1, "k must be at least 1"
+        self.target = as_model(target)
+        self.draft = as_model(draft)
+        if self.target.cfg.vocab_size != self.draft.cfg.vocab_size:
+            raise ValueError("draft and target must share a vocabulary")
+        self.k = k
+        self.t_pool, self.d_pool = target_pool, draft_pool
+        self.tr = runner_for(self.target, target_pool)
+        self.dr = runner_for(self.draft, draft_pool)
+        self.device = self.target.device
+        self.V = self.target.cfg.vocab_size
+        self._cap = 0
+        self.stats = {"iterations": 0, "verify_rows": 0}
+
+    def _ensure(self, S: int):
+        if S <= self._cap:
+            return
+        dev, k = self.device, self.k
+        self._cap = S
+        self.dlog = torch.empty(S, self.V, dtype=self.draft.dtype, device=dev)
+        self.tlog = torch.empty(S * (k + 1), self.V, dtype=self.target.dtype, device=dev)
+        self.drafts = torch.empty(k, S, dtype=torch.int32, device=dev)
+        self.accept_ws = ops.Workspace(dev)
+
+    def step(self, reqs: list[_Request], eos: set[int]) -> None:
+        """One draft/verify/accept iteration for every request in `reqs`."""
+        k, S = self.k, len(reqs)
+        self._ensure(S)
+        # --- block reservation, in the reference's order: draft feeds, then the verify feed.
+        for r in reqs:
+            r.u_d = len(r.tokens) - r.d_seq.length
+            r.u_t = len(r.tokens) - r.t_seq.length
+            r.d_seq.reserve(r.u_d + k - 1)
+        for r in reqs:
+            r.t_seq.reserve(r.u_t + k)
+        bs_d, bs_t = self.d_pool.block_size, self.t_pool.block_size
+        plans = [ForwardPlan([SeqSpec(r.d_seq.length, r.u_d, r.d_seq.blocks, 1) for r in reqs], bs_d)]
+        for j in range(1, k):
+            plans.append(ForwardPlan([SeqSpec(r.d_seq.length + r.u_d + j - 1, 1, r.d_seq.blocks, 1)
+                                      for r in reqs], bs_d))
+        vplan = ForwardPlan([SeqSpec(r.t_seq.length, r.u_t + k, r.t_seq.blocks, k + 1) for r in reqs], bs_t)
+        d_ids = [t for r in reqs for t in r.tokens[len(r.tokens) - r.u_d:]]
+        v_ids, dst = [], np.empty((k, S), dtype=np.int64)
+        for i, r in enumerate(reqs):
+            base = len(v_ids) + r.u_t
+            v_ids.extend(r.tokens[len(r.tokens) - r.u_t:])
+            v_ids.extend([0] * k)
+            dst[:, i] = base + np.arange(k)
+        # --- one host->device copy for every plan and input of this iteration
+        host = [p.host for p in plans] + [vplan.host, np.asarray(d_ids, np.int32), np.asarray(v_ids, np.int32),
+                                          dst.reshape(-1).astype(np.int32)]
+        offs = np.cumsum([0] + [h.shape[0] for h in host])
+        dev_all = torch.from_numpy(np.concatenate(host)).to(self.device)
+        views = [dev_all[offs[i]:offs[i + 1]] for i in range(len(host))]
+        d_ids_dev, v_ids_dev, dst_dev = views[-3], views[-2], views[-1].long()
+        # --- draft: k passes, argmax feeding the next pass on the device
+        self.dr.forward(plans[0], d_ids_dev, self.dlog[:S], plan_dev=views[0])
+        ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S])
+        for j in range(1, k):
+            self.dr.forward(plans[j], self.drafts[j - 1, :S], self.dlog[:S], plan_dev=views[j])
+            ops.argmax_rows(self.dlog[:S], out=self.drafts[j, :S])
+        # --- verify: one target pass over every request's u+k rows
+        drafts = self.drafts[:, :S]
+        v_ids_dev.index_copy_(0, dst_dev, drafts.reshape(-1))
+        tlog = self.tlog[: S * (k + 1)]
+        self.tr.forward(vplan, v_ids_dev, tlog, plan_dev=views[k])
+        # --- accept (fused argmax + prefix match + bonus)
+        _, n_acc, emitted = ops.greedy_accept(tlog.view(S, k + 1, self.V), drafts.t(), self.accept_ws)
+        n_host = n_acc.cpu().tolist()
+        em_host = emitted.cpu().tolist()
+        self.stats["iterations"] += 1
+        self.stats["verify_rows"] += vplan.n_tokens
+        for i, r in enumerate(reqs):
+            n = n_host[i]
+            em = em_host[i][: n + 1]
+            res = r.res
+            res.iterations += 1
+            res.tokens_drafted += k
+            res.tokens_accepted += n
+            res.accepted_per_iter.append(n)
+            res.draft_forwards += k
+            res.target_forwards += 1
+            r.d_seq.commit(r.u_d + k - 1)
+            r.t_seq.commit(r.u_t + k)
+            r.tokens.extend(em)
+            res.new_token_ids.extend(em)
+            keep = len(r.tokens) - 1
+            r.t_seq.truncate(min(r.t_seq.length, keep))
+            r.d_seq.truncate(min(r.d_seq.length, keep))
+            if eos and any(t in eos for t in em):
+                first = next(j for j, t in enumerate(em) if t in eos)
+                trim = len(em) - (first + 1)
+                if trim:
+                    res.new_token_ids = res.new_token_ids[:-trim]
+                res.stopped_on_eos = True
+                r.done = True
+            elif len(res.new_token_ids) >= r.max_new:
+                r.done = True
+
+    def check(self) -> None:
+        self.tr.check_status()
+        self.dr.check_status()
+
+    def run(self, reqs: list[_Request], eos: set[int], t0: float | None = None) -> None:
+        t0 = time.perf_counter() if t0 is None else t0
+        active = [r for r in reqs if not r.done]
+        while active:
+            self.step(active, eos)
+            now = None
+            for r in active:
+                if r.done:
+                    now = now or time.perf_counter()
+                    r.res.elapsed_s = now - t0
+            active = [r for r in active if not r.done]
+        self.check()
+        _sync(self.device)
+        end = time.perf_counter()
+        for r in reqs:
+            if r.res.elapsed_s == 0.0:
+                r.res.elapsed_s = end - t0
+            new = r.res.new_token_ids
+            if len(new) > r.max_new:
+                r.res.new_token_ids = new[: r.max_new]
+                r.res.stopped_on_eos = r.res.new_token_ids[-1] in eos if r.res.new_token_ids else False
+
+
+@torch.no_grad()
+def speculative_greedy(target_model, draft_model, input_ids: torch.Tensor, target_cache, draft_cache,
+                       k: int = 4, max_new_tokens: int = 32, eos_token_id=AUTO_EOS) -> SpecDecodeResult:
+    """Greedy speculative decoding of one request; output equals greedy decoding of the target."""
+    assert input_ids.dim() == 2 and input_ids.shape[0] == 1, "one request at a time"
+    assert k >= 1, "k must be at least 1"
+    assert target_cache.length == 0 and draft_cache.length == 0, "caches must be empty"
+    eos = _resolve_eos(target_model, eos_token_id)
+    eng = SpecEngine(target_model, draft_model, target_cache.pool, draft_cache.pool, k)
+    req = _Request(input_ids[0].tolist(), target_cache, draft_cache, max_new_tokens)
+    _sync(eng.device)
+    t0 = time.perf_counter()
+    req.done = False
+    if max_new_tokens <= 0:
+        req.done = True
+    eng.run([req], eos, t0)
+    req.res.elapsed_s = time.perf_counter() - t0
+    return req.res
+
+
+@torch.no_grad()
+def speculative_greedy_batch(target_model, draft_model, prompts: list[list[int]], target_pool, draft_pool,
+                             k: int = 4, max_new_tokens=32, eos_token_id=AUTO_EOS,
+                             free_on_finish: bool = True, engine: SpecEngine | None = None):
+    """Batched greedy speculative decoding. `max_new_tokens` is an int or a per-request list.
+
+    Returns (results, wall_seconds). Token output per request is identical to
+    `speculative_greedy` on that request alone (greedy output depends only on
+    the request's own tokens)."""
+    eos = _resolve_eos(target_model, eos_token_id)
+    eng = engine or SpecEngine(target_model, draft_model, target_pool, draft_pool, k)
+    budgets = max_new_tokens if isinstance(max_new_tokens, (list, tuple)) else [max_new_tokens] * len(prompts)
+    reqs = [_Request(p, target_pool.new_sequence(f"t{i}"), draft_pool.new_sequence(f"d{i}"), budgets[i])
+            for i, p in enumerate(prompts)]
+    _sync(eng.device)
+    t0 = time.perf_counter()
+    try:
+        eng.run(reqs, eos, t0)
+    finally:
+        if free_on_finish:
+            for r in reqs:
+                r.t_seq.free()
+                r.d_seq.free()
+    wall = time.perf_counter() - t0
+    return [r.res for r in reqs], wall

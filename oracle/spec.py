@@ -1,0 +1,104 @@
+"""Oracle: greedy speculative decoding and plain greedy. TEST INFRASTRUCTURE ONLY.
+
+`oracle_speculative_greedy` restates kvengine/speculative.py:111-216 step for
+step (draft k tokens with one forward each, verify u+k in one target forward,
+accept the longest matching prefix plus the bonus/correction token, truncate
+both caches to len(tokens)-1, trim at EOS and at the budget).
+`oracle_greedy_paged` restates kvengine/decode.py:261-332 (prefill, then one
+token per forward; blocks freed at the end).
+
+Both take an optional `logits_log` list that receives, per emitted decision,
+the fp32 logits row the argmax was taken over, so tests can compare logits and
+measure top-1/top-2 margins (near-tie reporting).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .model import OracleModel, oracle_forward
+
+
+def oracle_speculative_greedy(target: OracleModel, draft: OracleModel, prompt: list[int],
+                              t_cache, d_cache, k: int = 4, max_new_tokens: int = 32,
+                              eos_ids=(), use_sdpa: bool = True, verify_log: list | None = None):
+    assert k >= 1
+    assert t_cache.length == 0 and d_cache.length == 0
+    eos_ids = set(eos_ids or ())
+    tokens = list(prompt)
+    res = {"new_token_ids": [], "stopped_on_eos": False, "iterations": 0,
+           "tokens_drafted": 0, "tokens_accepted": 0, "accepted_per_iter": [],
+           "target_forwards": 0, "draft_forwards": 0}
+
+    def feed(model, cache, ids):
+        return oracle_forward(model, ids, cache, all_logits=True, use_sdpa=use_sdpa)
+
+    while len(res["new_token_ids"]) < max_new_tokens:
+        unseen = tokens[d_cache.length:]
+        logits = feed(draft, d_cache, unseen)
+        res["draft_forwards"] += 1
+        drafts = []
+        for j in range(k):
+            drafts.append(int(torch.argmax(logits[-1])))
+            if j < k - 1:
+                logits = feed(draft, d_cache, [drafts[-1]])
+                res["draft_forwards"] += 1
+        unseen_t = tokens[t_cache.length:]
+        u = len(unseen_t)
+        t_logits = feed(target, t_cache, unseen_t + drafts)
+        res["target_forwards"] += 1
+        rows = t_logits[u - 1:]
+        if verify_log is not None:
+            verify_log.append({"drafts": list(drafts), "rows": rows.float().clone(),
+                               "position": len(tokens)})
+        preds = torch.argmax(rows, dim=-1).tolist()
+        n = 0
+        for j in range(k):
+            if preds[j] != drafts[j]:
+                break
+            n += 1
+        emitted = drafts + [preds[k]] if n == k else drafts[:n] + [preds[n]]
+        res["iterations"] += 1
+        res["tokens_drafted"] += k
+        res["tokens_accepted"] += n
+        res["accepted_per_iter"].append(n)
+        tokens.extend(emitted)
+        res["new_token_ids"].extend(emitted)
+        keep = len(tokens) - 1
+        t_cache.truncate(min(t_cache.length, keep))
+        d_cache.truncate(min(d_cache.length, keep))
+        if any(t in eos_ids for t in emitted):
+            first = next(i for i, t in enumerate(emitted) if t in eos_ids)
+            trim = len(emitted) - (first + 1)
+            if trim:
+                res["new_token_ids"] = res["new_token_ids"][:-trim]
+            res["stopped_on_eos"] = True
+            break
+    if len(res["new_token_ids"]) > max_new_tokens:
+        res["new_token_ids"] = res["new_token_ids"][:max_new_tokens]
+        res["stopped_on_eos"] = res["new_token_ids"][-1] in eos_ids
+    return res
+
+
+def oracle_greedy_paged(model: OracleModel, prompt: list[int], cache, max_new_tokens: int = 32,
+                        eos_ids=(), use_sdpa: bool = True, logits_log: list | None = None):
+    eos_ids = set(eos_ids or ())
+    new = []
+    stopped = False
+    logits = oracle_forward(model, list(prompt), cache, use_sdpa=use_sdpa)
+    nxt = logits[-1]
+    for _ in range(max_new_tokens):
+        if logits_log is not None:
+            logits_log.append(nxt.float().clone())
+        tok = int(torch.argmax(nxt))
+        new.append(tok)
+        if tok in eos_ids:
+            stopped = True
+            break
+        nxt = oracle_forward(model, [tok], cache, use_sdpa=use_sdpa)[-1]
+    return {"new_token_ids": new, "stopped_on_eos": stopped, "blocks_held": len(cache.blocks)}
+
+
+def top2_margin(row: torch.Tensor) -> float:
+    v = row.float().topk(2).values
+    return float(v[0] - v[1])
