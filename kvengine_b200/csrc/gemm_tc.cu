@@ -166,7 +166,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   const int split = blockIdx.z;
   const int kb0 = (int)((long long)split * a.k_blocks / a.splits);
   const int kb1 = (int)((long long)(split + 1) * a.k_blocks / a.splits);
-  const int n_iter = kb1 - kb0;
+  // After a timeout anywhere in this launch, later CTAs skip their work instead
+  // of each waiting out the limit again.
+  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
+  const int n_iter = aborted ? 0 : kb1 - kb0;
   uint32_t tmem_cols = 32;
   while ((int)tmem_cols < a.nt) tmem_cols <<= 1;
 
@@ -234,7 +237,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     const int quad = warp & 3;  // TMEM lane quarter this warp may access
     const int col_feat = feat0 + quad * 32 + lane;
     const bool feat_ok = col_feat < a.n;
-    const bool waited = mbar_wait(smem_u32(tmem_full), 0, a.status);
+    const bool waited = !aborted && mbar_wait(smem_u32(tmem_full), 0, a.status);
     fence_after();
     const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);
     if (a.splits == 1) {

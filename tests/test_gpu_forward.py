@@ -1,0 +1,180 @@
+"""End-to-end parity on the GPU: model passes, plain greedy and speculative
+decoding through the sm_100a path against the reference's golden outputs and
+the CPU oracle. Tolerances: logits within 1e-3 (fp32) / 2e-2 (bf16); token
+sequences identical, with argmax near-ties (top-2 margin below the tolerance
+in the oracle) reported rather than failed."""
+
+import pytest
+import torch
+
+from conftest import load_golden
+from kvengine_b200 import (Model, PagedKVCache, forward_with_own_cache, greedy_batch, greedy_paged,
+                           speculative_greedy, speculative_greedy_batch)
+from oracle.model import OracleModel, oracle_forward
+from oracle.paged import OraclePool
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-3, torch.bfloat16: 2e-2}
+
+
+@pytest.fixture(scope="module")
+def tiny_golden():
+    return load_golden("tiny")
+
+
+def _models(tiny_state_dicts, name, dtype, dev):
+    cfg, sd = tiny_state_dicts[name]
+    return cfg, Model(cfg, sd, dtype, dev), Model(cfg, sd, dtype, dev, roll_lm_head=1)
+
+
+@pytest.mark.parametrize("name,dtype", [("tiny", torch.float32), ("tiny", torch.bfloat16),
+                                        ("tiny_hd128", torch.float32)])
+def test_forward_logits_match_oracle(cuda_device, tiny_state_dicts, name, dtype):
+    cfg, m, _ = _models(tiny_state_dicts, name, dtype, cuda_device)
+    om = OracleModel(cfg, tiny_state_dicts[name][1], dtype)
+    g = torch.Generator().manual_seed(3)
+    pool = PagedKVCache.for_model(m, num_blocks=64, block_size=16)
+    opool = OraclePool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, 64, 16, dtype)
+    seq, oseq = pool.new_sequence("a"), opool.new_sequence()
+    for T in (37, 1, 5, 16, 2):  # prefill, decode, verify-sized chunks
+        ids = torch.randint(0, cfg.vocab_size, (1, T), generator=g)
+        got = forward_with_own_cache(m, ids.to(cuda_device), seq, all_logits=True)[0].float().cpu()
+        ref = oracle_forward(om, ids[0].tolist(), oseq, all_logits=True).float()
+        err = (got - ref).abs().max().item()
+        assert err <= TOL[dtype], (T, err)
+    assert seq.blocks == oseq.blocks and seq.length == oseq.length
+
+
+@pytest.mark.parametrize("name,dt_name,dtype", [("tiny", "f32", torch.float32), ("tiny", "bf16", torch.bfloat16),
+                                                ("tiny_hd128", "f32", torch.float32)])
+def test_spec_and_greedy_match_reference_tokens(cuda_device, tiny_state_dicts, tiny_golden, name, dt_name, dtype):
+    rec = tiny_golden[f"{name}_{dt_name}"]
+    cfg, m, hostile = _models(tiny_state_dicts, name, dtype, cuda_device)
+    for i, p in enumerate(rec["prompts"]):
+        pool = PagedKVCache.for_model(m, num_blocks=256, block_size=16)
+        g = greedy_paged(m, torch.tensor([p], device=cuda_device), pool, max_new_tokens=20, eos_token_id=None)
+        assert g.new_token_ids == rec["greedy"][i]
+        assert pool.manager.num_allocated == 0
+    for k in (1, 2, 4, 8):
+        for i, p in enumerate(rec["prompts"]):
+            for draft, key in ((m, "spec_self"), (hostile, "spec_hostile")):
+                pool = PagedKVCache.for_model(m, num_blocks=256, block_size=16)
+                s = speculative_greedy(m, draft, torch.tensor([p], device=cuda_device), pool.new_sequence("t"),
+                                       pool.new_sequence("d"), k=k, max_new_tokens=20, eos_token_id=None)
+                want = rec[key][str(k)][i]
+                assert s.new_token_ids == want["tokens"], (key, k, i)
+                assert s.accepted_per_iter == want["accepted_per_iter"], (key, k, i)
+                assert (s.target_forwards, s.draft_forwards) == (want["target_forwards"], want["draft_forwards"])
+
+
+def test_budgets_eos_block_sizes_and_rollback_tables(cuda_device, tiny_state_dicts, tiny_golden):
+    rec = tiny_golden["tiny_f32"]
+    cfg, m, hostile = _models(tiny_state_dicts, "tiny", torch.float32, cuda_device)
+    p = torch.tensor([rec["prompts"][1]], device=cuda_device)
+    for budget, want in rec["budgets"].items():
+        pool = PagedKVCache.for_model(m, num_blocks=256, block_size=16)
+        s = speculative_greedy(m, m, p, pool.new_sequence("t"), pool.new_sequence("d"), k=4,
+                               max_new_tokens=int(budget), eos_token_id=None)
+        assert s.new_token_ids == want and len(s.new_token_ids) == int(budget)
+    for bs, want in rec["block_sizes"].items():
+        pool = PagedKVCache.for_model(m, num_blocks=512, block_size=int(bs))
+        assert greedy_paged(m, p, pool, max_new_tokens=16, eos_token_id=None).new_token_ids == want
+    e = rec["eos"]
+    pool = PagedKVCache.for_model(m, num_blocks=256, block_size=16)
+    s = speculative_greedy(m, m, p, pool.new_sequence("t"), pool.new_sequence("d"), k=4, max_new_tokens=20,
+                           eos_token_id=e["eos_id"])
+    assert s.new_token_ids == e["tokens"] and s.stopped_on_eos == e["stopped"]
+    assert s.new_token_ids.count(e["eos_id"]) == 1
+    rb = rec["rollback"]
+    pool = PagedKVCache.for_model(m, num_blocks=64, block_size=4)
+    t_seq, d_seq = pool.new_sequence("target"), pool.new_sequence("draft")
+    s = speculative_greedy(m, hostile, p, t_seq, d_seq, k=8, max_new_tokens=16, eos_token_id=None)
+    assert s.new_token_ids == rb["tokens"]
+    assert (t_seq.blocks, d_seq.blocks, t_seq.length, d_seq.length) == (
+        rb["t_blocks"], rb["d_blocks"], rb["t_len"], rb["d_len"])
+    assert pool.manager._free == rb["free_list"]
+    assert len(t_seq.blocks) == pool.manager.blocks_needed(t_seq.length)
+    t_seq.free()
+    d_seq.free()
+    assert pool.manager.num_allocated == 0
+    pool.manager.check_invariants()
+
+
+def test_truncate_then_continue_matches_uninterrupted(cuda_device, tiny_state_dicts):
+    """kvengine tests/test_phase5.py:240-265: junk K/V written then rolled back leaves no trace."""
+    cfg, m, _ = _models(tiny_state_dicts, "tiny", torch.float32, cuda_device)
+    ids = torch.randint(0, cfg.vocab_size, (1, 9), generator=torch.Generator().manual_seed(0)).to(cuda_device)
+    pool = PagedKVCache.for_model(m, num_blocks=64, block_size=4)
+    straight = greedy_paged(m, ids, pool, max_new_tokens=12, eos_token_id=None).new_token_ids
+    cache = pool.new_sequence("x")
+    logits = forward_with_own_cache(m, ids, cache)
+    produced = []
+    for step in range(12):
+        tok = int(torch.argmax(logits[0, -1]))
+        produced.append(tok)
+        if step == 5:
+            mark = cache.length
+            forward_with_own_cache(m, torch.tensor([[tok, tok, tok]], device=cuda_device), cache)
+            cache.truncate(mark)
+        logits = forward_with_own_cache(m, torch.tensor([[tok]], device=cuda_device), cache)
+    assert produced == straight
+
+
+def test_batched_spec_equals_per_request(cuda_device, tiny_state_dicts, tiny_golden):
+    rec = tiny_golden["tiny_bf16"]
+    cfg, m, hostile = _models(tiny_state_dicts, "tiny", torch.bfloat16, cuda_device)
+    prompts = rec["prompts"]
+    for draft, key in ((m, "spec_self"), (hostile, "spec_hostile")):
+        tp = PagedKVCache.for_model(m, num_blocks=512, block_size=16)
+        dp = PagedKVCache.for_model(m, num_blocks=512, block_size=16)
+        res, _ = speculative_greedy_batch(m, draft, prompts, tp, dp, k=4, max_new_tokens=[20, 13, 20],
+                                          eos_token_id=None)
+        for i, r in enumerate(res):
+            want = rec[key]["4"][i]["tokens"]
+            assert r.new_token_ids == want[: len(r.new_token_ids)]
+            assert len(r.new_token_ids) == (13 if i == 1 else 20)
+        assert tp.manager.num_allocated == 0 and dp.manager.num_allocated == 0
+
+
+@pytest.fixture(scope="module")
+def cfg1_model(cuda_device):
+    from kvengine_b200.config import QWEN2_0_5B
+
+    return Model.random_init(QWEN2_0_5B, seed=0, dtype=torch.float32, device=cuda_device, init_device="cpu")
+
+
+def test_config1_self_spec_full_acceptance_and_greedy_identity(cuda_device, cfg1_model):
+    """Config 1: 0.5B arch, seed 0, fp32, 4 requests x 64 random ids, 64 new tokens, k=4, bs=16:
+    acceptance exactly 100% and tokens identical to the reference's spec and greedy output."""
+    g = load_golden("cfg1")
+    m = cfg1_model
+    tp = PagedKVCache.for_model(m, num_blocks=512, block_size=16)
+    dp = PagedKVCache.for_model(m, num_blocks=512, block_size=16)
+    res, _ = speculative_greedy_batch(m, m, g["prompts"], tp, dp, k=4, max_new_tokens=64, eos_token_id=None)
+    for i, r in enumerate(res):
+        assert r.acceptance_rate == 1.0, (i, r.accepted_per_iter)
+        assert r.new_token_ids == g["spec"][i]["tokens"] == g["greedy"][i]
+    pool = PagedKVCache.for_model(m, num_blocks=512, block_size=16)
+    gr = greedy_batch(m, g["prompts"], pool, 64, eos_token_id=None, collect_logits=True)
+    for i, r in enumerate(gr):
+        assert r.new_token_ids == g["greedy"][i]
+        top = torch.tensor(g["greedy_top2"][i]["values"])
+        got = r.step_logits.topk(2, dim=-1).values
+        assert (got - top).abs().max().item() <= 1e-3
+
+
+def test_config1_logits_within_1e3_of_oracle(cuda_device, cfg1_model):
+    """Teacher-forced prompt + generated tokens: every row of our fp32 logits within 1e-3 of the oracle."""
+    from kvengine_b200.config import QWEN2_0_5B
+    from kvengine_b200.weights import init_state_dict
+
+    g = load_golden("cfg1")
+    seqv = g["prompts"][0] + g["greedy"][0][:20]
+    om = OracleModel(QWEN2_0_5B, init_state_dict(QWEN2_0_5B, seed=0), torch.float32)
+    opool = OraclePool(24, 2, 64, 64, 16, torch.float32)
+    ref = oracle_forward(om, seqv, opool.new_sequence(), all_logits=True)
+    pool = PagedKVCache.for_model(cfg1_model, num_blocks=64, block_size=16)
+    got = forward_with_own_cache(cfg1_model, torch.tensor([seqv], device=cuda_device), pool.new_sequence("x"),
+                                 all_logits=True)[0].cpu()
+    assert (got - ref).abs().max().item() <= 1e-3
