@@ -1,0 +1,529 @@
+"""Benchmark: accepted tokens/s of greedy speculative decoding, 0.5B-arch draft -> 3B-arch target, k=4.
+
+Workload (BASELINE config 4 at k=4): draft Qwen2.5-0.5B architecture (seed 1),
+target Qwen2.5-3B architecture (seed 2), random-init bf16, 64 requests per
+GPU with 128 uniform-random prompt ids each, 64 new tokens per request, KV
+block size 16. One step = one full batched speculative decode of those
+requests (prefill fused into the first verify pass, as the reference does).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+`value`: accepted (emitted) tokens/s over all ranks with the weights and the
+request token lists resident before the timed region; `e2e`: the same through
+the public API `speculative_greedy_batch` from a pinned host prompt tensor,
+with every host<->device copy inside the timed region. `roofline`: the verify
+step (one target pass over B*(k+1) rows), timed with CUDA events on its
+stream during the timed steps. `--impl reference` times the CPU oracle port
+of the reference's path on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+K_SPEC = 4
+N_REQ = 64
+PROMPT = 128
+NEW = 64
+BLOCK = 16
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p["bf16_tflops_sustained"], "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def verify_algorithmic(plans, target_cfg, weight_bytes: int):
+    """Bytes and FLOPs one verify pass must move/do (per launch, averaged)."""
+    kv_tok = target_cfg.kv_bytes_per_token(2)
+    V, H = target_cfg.vocab_size, target_cfg.hidden_size
+    L, nq, hd = target_cfg.num_layers, target_cfg.num_heads, target_cfg.head_dim
+    tot_b = tot_f = 0.0
+    for plan in plans:
+        rows = plan.n_tokens
+        off = plan.offsets
+        q = plan.host[off["q_lens"][0]: off["q_lens"][0] + off["q_lens"][1]]
+        ctx = plan.host[off["ctx_lens"][0]: off["ctx_lens"][0] + off["ctx_lens"][1]]
+        hist = float((ctx - q).sum())
+        n_out = plan.n_out
+        b = weight_bytes + hist * kv_tok + rows * kv_tok + n_out * V * 2 + rows * H * 2
+        params = weight_bytes / 2
+        attn = 4.0 * float((q.astype("float64") * ctx).sum()) * nq * hd * L
+        f = 2.0 * rows * (params - V * H) + 2.0 * n_out * V * H + attn
+        tot_b += b
+        tot_f += f
+    n = max(1, len(plans))
+    return tot_b / n, tot_f / n
+
+
+def run_gpu(args):
+    import torch.distributed as dist
+
+    from kvengine_b200 import Model, PagedKVCache, SpecEngine, speculative_greedy_batch
+    from kvengine_b200 import _lib as L
+    from kvengine_b200.config import QWEN2_0_5B, QWEN2_3B
+    from kvengine_b200.speculative import _Request
+    from kvengine_b200.workloads import random_prompts
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=600))
+    draft = Model.random_init(QWEN2_0_5B, seed=1, dtype=torch.bfloat16, device=dev, init_device=dev)
+    target = Model.random_init(QWEN2_3B, seed=2, dtype=torch.bfloat16, device=dev, init_device=dev)
+    # Requests are sharded by rank: rank r decodes requests [r*64, (r+1)*64) of a seeded set.
+    prompts_all = random_prompts(N_REQ * world, PROMPT, seed=4)
+    prompts = prompts_all[rank * N_REQ:(rank + 1) * N_REQ].tolist()
+    blocks_per_seq = -(-(PROMPT + NEW + 2 * K_SPEC + 2) // BLOCK)
+    t_pool = PagedKVCache.for_model(target, num_blocks=N_REQ * blocks_per_seq + 64, block_size=BLOCK)
+    d_pool = PagedKVCache.for_model(draft, num_blocks=N_REQ * blocks_per_seq + 64, block_size=BLOCK)
+    eng = SpecEngine(target, draft, t_pool, d_pool, K_SPEC)
+    lib = L.load()
+
+    def one_step(collect=None):
+        reqs = [_Request(p, t_pool.new_sequence(f"t{i}"), d_pool.new_sequence(f"d{i}"), NEW)
+                for i, p in enumerate(prompts)]
+        eng.run(reqs, set())
+        toks = sum(len(r.res.new_token_ids) for r in reqs)
+        if collect is not None:
+            collect.append(reqs)
+        for r in reqs:
+            r.t_seq.free()
+            r.d_seq.free()
+        return toks
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+
+    # ---------------------------------------------------------------- value
+    props = torch.cuda.get_device_properties(dev)
+    bus = getattr(props, "pci_bus_id", None)
+    smi_id = f"{getattr(props, 'pci_domain_id', 0):08x}:{bus:02x}:{getattr(props, 'pci_device_id', 0):02x}.0" \
+        if bus is not None else str(local)
+    sampler = ClockSampler(smi_id)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    eng.verify_events = []
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = lib.kve_launch_count()
+    stats0 = dict(eng.stats)
+    collected = []
+    ev0.record()
+    tokens = 0
+    for _ in range(args.steps):
+        tokens += one_step(collected)
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = lib.kve_launch_count() - launches0
+    clocks = sampler.stop()
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    verify_ev = eng.verify_events
+    eng.verify_events = None
+    t = torch.tensor([ms], device=dev)
+    tok_t = torch.tensor([float(tokens)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tok_t, op=dist.ReduceOp.SUM)
+    ms_max = float(t.item())
+    total_tokens = float(tok_t.item())
+    value = total_tokens / (ms_max / 1e3)
+    accepted = sum(r.res.tokens_accepted for reqs in collected for r in reqs)
+    drafted = sum(r.res.tokens_drafted for reqs in collected for r in reqs)
+    iters = eng.stats["iterations"] - stats0["iterations"]
+
+    # ------------------------------------------------------------ roofline
+    steady = [(a, b, p) for a, b, p in verify_ev if p.max_q_len == K_SPEC + 1]
+    prefill = [(a, b, p) for a, b, p in verify_ev if p.max_q_len != K_SPEC + 1]
+    v_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in steady) if steady else float("nan")
+    wb = target.weights.weight_bytes()
+    alg_b, alg_f = verify_algorithmic([p for _, _, p in steady], QWEN2_3B, wb)
+    pk = peaks()
+    t_hbm = alg_b / (pk["hbm_gbs"] * 1e9)
+    t_tc = alg_f / (pk["bf16_tflops_sustained"] * 1e12)
+    bound = "tensor" if t_tc > t_hbm else "hbm"
+    if bound == "tensor":
+        achieved = alg_f / (v_ms / 1e3) / 1e12
+        peak = pk["bf16_tflops_sustained"]
+        unit = "TFLOP/s"
+    else:
+        achieved = alg_b / (v_ms / 1e3) / 1e9
+        peak = pk["hbm_gbs"]
+        unit = "GB/s"
+    roofline = {
+        "kernel": "verify step: kve_forward of the 3B target over B*(k+1)=320 rows (36 layers + lm_head)",
+        "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+        "frac": round(achieved / peak, 4), "peak_src": pk["src"] + (" sustained" if bound == "tensor" else ""),
+        "traffic": None,
+        "verify_ms": round(v_ms, 4), "verify_launches": len(steady),
+        "alg_bytes_per_launch": round(alg_b), "alg_flops_per_launch": round(alg_f),
+        "hbm_gbs_achieved": round(alg_b / (v_ms / 1e3) / 1e9, 1),
+        "hbm_frac": round(alg_b / (v_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+        "roofline_ms": round(max(t_hbm, t_tc) * 1e3, 4),
+        "frac_of_roofline_time": round(max(t_hbm, t_tc) * 1e3 / v_ms, 4),
+        "prefill_verify_ms": round(statistics.mean(a.elapsed_time(b) for a, b, _ in prefill), 3) if prefill else None,
+    }
+
+    # ----------------------------------------------------------------- e2e
+    pinned = torch.tensor(prompts, dtype=torch.int64).pin_memory()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h2d0, d2h0 = eng.stats["h2d_bytes"], eng.stats["d2h_bytes"]
+    e_tokens = 0
+    out_bytes = 0
+    e0.record()
+    for _ in range(args.steps):
+        res, _wall = speculative_greedy_batch(target, draft, pinned, t_pool, d_pool, k=K_SPEC,
+                                              max_new_tokens=NEW, eos_token_id=None, engine=eng)
+        out = torch.tensor([r.new_token_ids for r in res], dtype=torch.int32)
+        out_bytes += out.numel() * 4
+        e_tokens += int(out.numel())
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    e_tok = torch.tensor([float(e_tokens)], device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(e_tok, op=dist.ReduceOp.SUM)
+    h2d = (eng.stats["h2d_bytes"] - h2d0) / args.steps
+    d2h = (eng.stats["d2h_bytes"] - d2h0) / args.steps
+    e2e = {"value": round(float(e_tok.item()) / (float(e_ms.item()) / 1e3), 2), "unit": "accepted tokens/s",
+           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+           "api": "kvengine_b200.speculative_greedy_batch(pinned host prompt tensor) -> host token lists; "
+                  "counted bytes = every plan/token upload and every accept readback"}
+
+    # ------------------------------------------------- results to rank 0 (NCCL, untimed)
+    if world > 1:
+        mine = torch.tensor([r.res.new_token_ids for r in collected[-1]], dtype=torch.int32, device=dev)
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+        dist.barrier()
+        dist.destroy_process_group()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(oracle_models(target, draft), prompts[0])
+
+    if rank == 0:
+        line = {
+            "metric": "accepted tokens/s (0.5B->3B, k=4)",
+            "value": round(value, 2), "unit": "accepted tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random ids, random-init weights)",
+            "config": {"workload": "config 4 at k=4: 0.5B-arch draft (seed 1) -> 3B-arch target (seed 2), bf16",
+                       "requests_per_gpu": N_REQ, "prompt_len": PROMPT, "new_tokens": NEW, "k": K_SPEC,
+                       "block_size": BLOCK, "global_requests": N_REQ * world, "parallelism": f"dp{world} (requests sharded)",
+                       "l2": "inputs larger than L2 (6.2 GB target + 1.0 GB draft weights streamed per pass)"},
+            "acceptance_rate": round(accepted / drafted, 4) if drafted else None,
+            "iterations_per_step": iters / args.steps,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "roofline": roofline,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+CPU_SAMPLE_TOKENS = 24
+
+
+def oracle_models(target=None, draft=None):
+    """CPU oracle models holding the benchmark's weights (copied from the GPU
+    models when given, else the same seeded init generated on the GPU if one
+    is present, else on the CPU)."""
+    from kvengine_b200.config import QWEN2_0_5B, QWEN2_3B
+    from kvengine_b200.weights import init_state_dict
+    from oracle.model import OracleModel
+
+    def from_device(m):
+        w, cfg, i = m.weights, m.cfg, m.cfg.intermediate_size
+        sd = {"model.embed_tokens.weight": w.embed.cpu(), "model.norm.weight": w.norm.cpu().to(m.dtype),
+              "lm_head.weight": w.lm_head.cpu()}
+        qs, ks = cfg.q_size, cfg.kv_size
+        for li, lw in enumerate(w.layers):
+            p = f"model.layers.{li}."
+            qkv, b = lw["w_qkv"].cpu(), lw["b_qkv"].cpu().to(m.dtype)
+            for n, a, z in (("q", 0, qs), ("k", qs, qs + ks), ("v", qs + ks, qs + 2 * ks)):
+                sd[p + f"self_attn.{n}_proj.weight"] = qkv[a:z]
+                sd[p + f"self_attn.{n}_proj.bias"] = b[a:z]
+            sd[p + "self_attn.o_proj.weight"] = lw["w_o"].cpu()
+            gu = lw["w_gu"].cpu().view(i, 2, -1)
+            sd[p + "mlp.gate_proj.weight"], sd[p + "mlp.up_proj.weight"] = gu[:, 0], gu[:, 1]
+            sd[p + "mlp.down_proj.weight"] = lw["w_down"].cpu()
+            sd[p + "input_layernorm.weight"] = lw["ln1"].cpu().to(m.dtype)
+            sd[p + "post_attention_layernorm.weight"] = lw["ln2"].cpu().to(m.dtype)
+        return sd
+
+    if target is not None:
+        t_sd, d_sd = from_device(target), from_device(draft)
+    else:
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+        t_sd = {k: v.cpu() for k, v in init_state_dict(QWEN2_3B, 2, dtype=torch.bfloat16, device=dev).items()}
+        d_sd = {k: v.cpu() for k, v in init_state_dict(QWEN2_0_5B, 1, dtype=torch.bfloat16, device=dev).items()}
+    return OracleModel(QWEN2_3B, t_sd, torch.bfloat16), OracleModel(QWEN2_0_5B, d_sd, torch.bfloat16)
+
+
+def cpu_baseline(models, prompt):
+    """The CPU oracle (a port of the reference's speculative_greedy path) on a
+    bounded sample of the same workload: one request of the benchmark, the
+    prefill-fused first verify plus spec iterations until CPU_SAMPLE_TOKENS new
+    tokens, bf16, on every host thread."""
+    from oracle.paged import OraclePool
+    from oracle.spec import oracle_speculative_greedy
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    tm, dm = models
+    tp = OraclePool(36, 2, 128, 64, BLOCK, torch.bfloat16)
+    dp = OraclePool(24, 2, 64, 64, BLOCK, torch.bfloat16)
+    t0 = time.perf_counter()
+    res = oracle_speculative_greedy(tm, dm, prompt, tp.new_sequence(), dp.new_sequence(), k=K_SPEC,
+                                    max_new_tokens=CPU_SAMPLE_TOKENS)
+    dt = time.perf_counter() - t0
+    n = len(res["new_token_ids"])
+    return {"value": round(n / dt, 3), "unit": "accepted tokens/s", "cores": cores, "kind": "port",
+            "sample": f"1 request (prompt {PROMPT} ids), k={K_SPEC}, {n} new tokens in {res['iterations']} "
+                      f"iterations incl. the prefill-fused first verify; CPU oracle port of kvengine's "
+                      f"speculative_greedy in bf16; {dt:.1f} s"}
+
+
+def run_reference(args):
+    from kvengine_b200.workloads import random_prompts
+
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    models = oracle_models()
+    prompt = random_prompts(N_REQ, PROMPT, seed=4)[0].tolist()
+    vals, info = [], None
+    for i in range(args.warmup + args.steps):
+        info = cpu_baseline(models, prompt)
+        if i >= args.warmup:
+            vals.append(info["value"])
+    v = statistics.mean(vals)
+    line = {"impl": "reference", "metric": "accepted tokens/s (0.5B->3B, k=4)", "value": round(v, 3),
+            "unit": "accepted tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random ids, random-init weights)",
+            "config": {"workload": "config 4 at k=4: 0.5B-arch draft (seed 1) -> 3B-arch target (seed 2), bf16",
+                       "sample_per_step": info["sample"]},
+            "cpu_baseline": {"value": round(v, 3), "unit": "accepted tokens/s", "cores": info["cores"],
+                             "kind": "port", "sample": info["sample"]},
+            "e2e": {"value": round(v, 3), "unit": "accepted tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _time_launches(fn, iters: int, flush: torch.Tensor | None = None) -> float:
+    """Mean ms per call of `fn` with CUDA events on the current stream; the L2
+    is flushed (a write larger than L2) between calls when `flush` is given."""
+    for _ in range(3):
+        fn()
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.add_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    return statistics.mean(times)
+
+
+def run_micro(args):
+    """Per-kernel microbenchmarks (one JSON line each) on the BASELINE configs
+    2 (attention), 3 (accept) and the verify GEMM shapes, timed with CUDA events."""
+    from kvengine_b200 import ops, workloads
+
+    dev = torch.device("cuda", 0)
+    pk = peaks()
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)  # 256 MB > L2
+    out = []
+    which = args.micro.split(",")
+    if "accept" in which:
+        for k in (1, 2, 4, 8):
+            w = workloads.accept_workload(k)
+            lg, dr = w.logits.to(dev), w.drafts.to(torch.int32).to(dev)
+            ws = ops.Workspace(dev)
+            ms = _time_launches(lambda: ops.greedy_accept(lg, dr, ws), args.steps, flush)
+            nbytes = lg.numel() * 4
+            out.append({"micro": "greedy_accept (config 3)", "k": k, "batch": 256, "ms": round(ms, 4),
+                        "alg_bytes": nbytes, "gbs": round(nbytes / ms / 1e6, 1),
+                        "frac_hbm": round(nbytes / ms / 1e6 / pk["hbm_gbs"], 4)})
+            del lg
+    if "attention" in which:
+        w = workloads.attention_workload()
+        shape = (w.num_blocks, w.block_size, w.k_new.shape[1], w.k_new.shape[2])
+        dk = torch.randn(shape, device=dev).to(torch.bfloat16)  # timing only: any finite contents
+        dv = torch.randn(shape, device=dev).to(torch.bfloat16)
+        B = w.num_seqs
+        width = max(len(t) for t in w.tables)
+        tables = torch.zeros(B, width, dtype=torch.int32)
+        for b, t in enumerate(w.tables):
+            tables[b, : len(t)] = torch.tensor(t, dtype=torch.int32)
+        tables = tables.to(dev)
+        ctx = torch.tensor(w.ctx_lens, dtype=torch.int32, device=dev)
+        ql = torch.full((B,), w.q_len, dtype=torch.int32, device=dev)
+        qo = (torch.arange(B + 1, dtype=torch.int32) * w.q_len).to(dev)
+        q = w.q.to(dev)
+        o = torch.empty_like(q)
+        ws = ops.Workspace(dev)
+        mc = max(w.ctx_lens)
+        ms = _time_launches(lambda: ops.paged_attention(q, dk, dv, tables, ctx, ql, qo, w.q_len, mc, w.scale, out=o,
+                                                        workspace=ws), args.steps, flush)
+        kvb = sum(w.ctx_lens) * 2 * 64 * 2 * 2
+        qob = q.numel() * 2 * 2
+        out.append({"micro": "paged_verify_attention (config 2)", "seqs": B, "q_len": w.q_len,
+                    "mean_ctx": round(sum(w.ctx_lens) / B, 1), "ms": round(ms, 4), "alg_bytes": kvb + qob,
+                    "gbs": round((kvb + qob) / ms / 1e6, 1), "frac_hbm": round((kvb + qob) / ms / 1e6 / pk["hbm_gbs"], 4)})
+    if "gemm" in which:
+        g = torch.Generator(device=dev).manual_seed(0)
+        for name, m, n, k in (("qkv", 320, 2560, 2048), ("o_proj", 320, 2048, 2048), ("gate_up", 320, 22016, 2048),
+                              ("down", 320, 2048, 11008), ("lm_head", 320, 151936, 2048),
+                              ("draft_gate_up", 64, 9728, 896), ("draft_lm_head", 64, 151936, 896)):
+            if args.gemm_case and name not in args.gemm_case.split(","):
+                continue
+            x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+            wt = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            ws = ops.Workspace(dev)
+            y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+            ms = _time_launches(lambda: ops.gemm(x, wt, out=y, workspace=ws), args.steps, flush)
+            bts = (n * k + m * k + m * n) * 2
+            fl = 2.0 * m * n * k
+            out.append({"micro": f"gemm_tcgen05 {name}", "m": m, "n": n, "k": k, "ms": round(ms, 4),
+                        "gbs": round(bts / ms / 1e6, 1), "frac_hbm": round(bts / ms / 1e6 / pk["hbm_gbs"], 4),
+                        "tflops": round(fl / ms / 1e9, 1), "frac_tensor": round(fl / ms / 1e9 / pk["bf16_tflops"], 4)})
+            del wt
+    for line in out:
+        print(json.dumps(line), flush=True)
+
+
+def run_profile_iteration(args):
+    """Warm up on the benchmark workload, then run exactly one steady-state spec
+    iteration between cudaProfilerStart/Stop (for `ncu --profile-from-start off`)."""
+    from kvengine_b200 import Model, PagedKVCache, SpecEngine
+    from kvengine_b200.config import QWEN2_0_5B, QWEN2_3B
+    from kvengine_b200.speculative import _Request
+    from kvengine_b200.workloads import random_prompts
+
+    dev = torch.device("cuda", 0)
+    draft = Model.random_init(QWEN2_0_5B, seed=1, dtype=torch.bfloat16, device=dev, init_device=dev)
+    target = Model.random_init(QWEN2_3B, seed=2, dtype=torch.bfloat16, device=dev, init_device=dev)
+    prompts = random_prompts(N_REQ, PROMPT, seed=4).tolist()
+    nb = N_REQ * (-(-(PROMPT + NEW + 2 * K_SPEC + 2) // BLOCK)) + 64
+    t_pool = PagedKVCache.for_model(target, num_blocks=nb, block_size=BLOCK)
+    d_pool = PagedKVCache.for_model(draft, num_blocks=nb, block_size=BLOCK)
+    eng = SpecEngine(target, draft, t_pool, d_pool, K_SPEC)
+    reqs = [_Request(p, t_pool.new_sequence(f"t{i}"), d_pool.new_sequence(f"d{i}"), NEW)
+            for i, p in enumerate(prompts)]
+    for _ in range(4):  # prefill-fused first iteration + 3 steady iterations
+        eng.step(reqs, set())
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    eng.step(reqs, set())
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({"profiled": "one steady-state spec iteration", "requests": N_REQ, "k": K_SPEC}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="kvengine_b200", choices=["kvengine_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", default=None, help="comma list of accept,attention,gemm microbenchmarks")
+    ap.add_argument("--gemm-case", default=None, help="restrict --micro gemm to these shapes (comma list)")
+    ap.add_argument("--profile-iteration", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.micro:
+        run_micro(args)
+    elif args.profile_iteration:
+        run_profile_iteration(args)
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

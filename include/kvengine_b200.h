@@ -52,6 +52,8 @@ enum { KVE_GEMM_AUTO = 0, KVE_GEMM_SIMT = 1, KVE_GEMM_TCGEN05 = 2 };
 
 int kve_version(void);
 const char* kve_last_error(void);
+/* Number of kernels this library has launched in this process (for launch accounting). */
+unsigned long long kve_launch_count(void);
 
 /* Fused greedy acceptance.
  * Replaces kvengine/speculative.py:167-182: `target_preds = argmax(t_logits[u-1:])`

@@ -61,6 +61,7 @@ class ScratchT(C.Structure):
 _SIGNATURES = {
     "kve_version": (i32, []),
     "kve_last_error": (C.c_char_p, []),
+    "kve_launch_count": (C.c_ulonglong, []),
     "kve_greedy_accept_workspace_bytes": (sz, [i32]),
     "kve_greedy_accept": (i32, [vp, i32, i64, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp, sz, vp, vp]),
     "kve_argmax_rows": (i32, [vp, i32, i32, i32, i64, vp, vp]),

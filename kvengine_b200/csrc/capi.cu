@@ -1,4 +1,5 @@
 // Library-wide C ABI pieces: version and the thread-local error message.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -16,8 +17,14 @@ int set_error(int code, const char* fmt, ...) {
   return code;
 }
 
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 }  // namespace kve
 
 extern "C" int kve_version(void) { return 1; }
+
+extern "C" unsigned long long kve_launch_count(void) { return kve::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" const char* kve_last_error(void) { return kve::g_last_error; }

@@ -13,8 +13,11 @@ namespace kve {
 
 // Sets the thread-local message returned by kve_last_error() and returns `code`.
 int set_error(int code, const char* fmt, ...);
+void count_launch();
 
+// Called right after every kernel launch of this library.
 inline int check_launch(const char* what) {
+  count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(KVE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return KVE_OK;

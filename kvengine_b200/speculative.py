@@ -102,7 +102,10 @@ class SpecEngine:
         self.device = self.target.device
         self.V = self.target.cfg.vocab_size
         self._cap = 0
-        self.stats = {"iterations": 0, "verify_rows": 0}
+        self.stats = {"iterations": 0, "verify_rows": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+        # When a list, every verify pass appends (start_event, end_event, plan) so a
+        # caller can time the verify step on the stream it runs on.
+        self.verify_events: list | None = None
 
     def _ensure(self, S: int):
         if S <= self._cap:
@@ -142,7 +145,9 @@ class SpecEngine:
         host = [p.host for p in plans] + [vplan.host, np.asarray(d_ids, np.int32), np.asarray(v_ids, np.int32),
                                           dst.reshape(-1).astype(np.int32)]
         offs = np.cumsum([0] + [h.shape[0] for h in host])
-        dev_all = torch.from_numpy(np.concatenate(host)).to(self.device)
+        packed = np.concatenate(host)
+        dev_all = torch.from_numpy(packed).to(self.device)
+        self.stats["h2d_bytes"] += packed.nbytes
         views = [dev_all[offs[i]:offs[i + 1]] for i in range(len(host))]
         d_ids_dev, v_ids_dev, dst_dev = views[-3], views[-2], views[-1].long()
         # --- draft: k passes, argmax feeding the next pass on the device
@@ -155,11 +160,18 @@ class SpecEngine:
         drafts = self.drafts[:, :S]
         v_ids_dev.index_copy_(0, dst_dev, drafts.reshape(-1))
         tlog = self.tlog[: S * (k + 1)]
+        if self.verify_events is not None:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
         self.tr.forward(vplan, v_ids_dev, tlog, plan_dev=views[k])
+        if self.verify_events is not None:
+            ev1.record()
+            self.verify_events.append((ev0, ev1, vplan))
         # --- accept (fused argmax + prefix match + bonus)
         _, n_acc, emitted = ops.greedy_accept(tlog.view(S, k + 1, self.V), drafts.t(), self.accept_ws)
         n_host = n_acc.cpu().tolist()
         em_host = emitted.cpu().tolist()
+        self.stats["d2h_bytes"] += (n_acc.numel() + emitted.numel()) * 4
         self.stats["iterations"] += 1
         self.stats["verify_rows"] += vplan.n_tokens
         for i, r in enumerate(reqs):
@@ -240,12 +252,15 @@ def speculative_greedy(target_model, draft_model, input_ids: torch.Tensor, targe
 def speculative_greedy_batch(target_model, draft_model, prompts: list[list[int]], target_pool, draft_pool,
                              k: int = 4, max_new_tokens=32, eos_token_id=AUTO_EOS,
                              free_on_finish: bool = True, engine: SpecEngine | None = None):
-    """Batched greedy speculative decoding. `max_new_tokens` is an int or a per-request list.
+    """Batched greedy speculative decoding. `prompts`: list of token lists or a host
+    int tensor [B, P]; `max_new_tokens`: an int or a per-request list.
 
     Returns (results, wall_seconds). Token output per request is identical to
     `speculative_greedy` on that request alone (greedy output depends only on
     the request's own tokens)."""
     eos = _resolve_eos(target_model, eos_token_id)
+    if isinstance(prompts, torch.Tensor):
+        prompts = prompts.tolist()
     eng = engine or SpecEngine(target_model, draft_model, target_pool, draft_pool, k)
     budgets = max_new_tokens if isinstance(max_new_tokens, (list, tuple)) else [max_new_tokens] * len(prompts)
     reqs = [_Request(p, target_pool.new_sequence(f"t{i}"), draft_pool.new_sequence(f"d{i}"), budgets[i])
