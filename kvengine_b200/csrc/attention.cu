@@ -12,6 +12,9 @@
 // accumulator all fp32), masked keys contribute exact zeros.
 #include <math.h>
 
+#include <mutex>
+#include <type_traits>
+
 #include "kve_common.cuh"
 
 namespace kve {
@@ -177,6 +180,295 @@ paged_attn_kernel(AttnParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// bf16 tensor-core variant (mma.sync m16n8k16, fp32 accumulate). Same CTA
+// decomposition, key tiles, chunking and partial format as the kernel above;
+// each of the 4 warps owns 16 query rows. K/V tiles of 32 keys are staged with
+// 16-byte cp.async (double-buffered, rows padded by 16 bytes so ldmatrix is
+// conflict-free); S = Q K^T and O += P V run on the tensor cores, the online
+// softmax in registers. Every row's arithmetic depends only on that row and on
+// keys at fixed absolute positions, so results do not depend on the batch.
+constexpr int kMmaKeyTile = 32;
+constexpr int kMmaStages = 4;
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+template <int HD, int BS>
+__global__ void __launch_bounds__(kAttnThreads)
+paged_attn_mma_kernel(AttnParams p) {
+  constexpr int ROW = HD * 2 + 16;             // padded smem row (bytes)
+  constexpr int TILE = kMmaKeyTile * ROW;      // one K or V tile
+  constexpr int KSTEPS = HD / 16;              // k16 steps over the head dim
+  constexpr int NT = kMmaKeyTile / 8;          // n8 tiles of keys per tile
+  constexpr int DT = HD / 8;                   // n8 tiles of the output
+  constexpr int CPR = HD * 2 / 16;             // 16-byte chunks per key row
+  extern __shared__ __align__(128) uint8_t smem_attn[];
+  const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem_attn));
+  // buffers: [stage][K|V] tiles, then the chunk's block table
+
+  const int c = blockIdx.x, bh = blockIdx.y, qtile = blockIdx.z;
+  const int b = bh / p.nkv, h = bh % p.nkv;
+  const int ctx = p.ctx_lens[b], ql = p.q_lens[b], qoff = p.q_offsets[b];
+  if (ql < 0 || ctx < ql || ctx > p.table_stride * p.bs) {
+    if (threadIdx.x == 0 && c == 0 && qtile == 0) report(p.status, KVE_ERR_BOUNDS);
+    return;
+  }
+  const int t0 = qtile * p.qt;
+  if (t0 >= ql) return;
+  const int nt = min(p.qt, ql - t0);
+  const int rows = nt * p.group;
+  const int first_pos = ctx - ql + t0;
+  const int last_pos = first_pos + nt - 1;
+  const int key_lo = c * kChunk;
+  if (key_lo > last_pos) return;
+  const int key_hi = min(min(ctx, key_lo + kChunk), last_pos + 1);
+  const int n_tiles = (key_hi - key_lo + kMmaKeyTile - 1) / kMmaKeyTile;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.q);
+  const __nv_bfloat16* pk = static_cast<const __nv_bfloat16*>(p.pool_k);
+  const __nv_bfloat16* pv = static_cast<const __nv_bfloat16*>(p.pool_v);
+  const int32_t* table = p.tables + (size_t)b * p.table_stride;
+
+  // The chunk's block-table entries, staged once (512 keys / block size).
+  int* tab = reinterpret_cast<int*>(smem_attn + kMmaStages * 2 * TILE);
+  const int blk_lo = BS > 0 ? key_lo / BS : key_lo / p.bs;
+  const int n_blk = (BS > 0 ? (key_hi - 1) / BS : (key_hi - 1) / p.bs) - blk_lo + 1;
+  for (int i = threadIdx.x; i < n_blk; i += kAttnThreads) {
+    int64_t blk = table[blk_lo + i];
+    if (blk < 0 || blk >= p.num_blocks) {
+      report(p.status, KVE_ERR_BOUNDS);
+      blk = -1;
+    }
+    tab[i] = (int)blk;
+  }
+  __syncthreads();
+
+  // Each thread copies the same (key-in-tile, 16-byte chunk) slots of every tile.
+  constexpr int SLOTS = 2 * kMmaKeyTile * CPR / kAttnThreads;  // K and V chunks per thread per tile
+  static_assert(2 * kMmaKeyTile * CPR % kAttnThreads == 0, "tile copy must divide evenly");
+  const size_t head_off = (size_t)h * HD;
+  const size_t row_stride = (size_t)p.nkv * HD;  // elements between consecutive tokens
+  auto load_tile = [&](int tile, int stage) {
+    const int kt = key_lo + tile * kMmaKeyTile;
+#pragma unroll
+    for (int u = 0; u < SLOTS; ++u) {
+      const int i = threadIdx.x + u * kAttnThreads;
+      const bool is_v = i >= kMmaKeyTile * CPR;
+      const int j = is_v ? i - kMmaKeyTile * CPR : i;
+      const int kk = j / CPR, ch = j % CPR;
+      const int key = kt + kk;
+      const __nv_bfloat16* src = pk;
+      uint32_t bytes = 0;
+      if (key < key_hi) {
+        int blk, off;
+        if constexpr (BS > 0) {
+          blk = tab[key / BS - blk_lo];
+          off = key % BS;
+        } else {
+          blk = tab[key / p.bs - blk_lo];
+          off = key % p.bs;
+        }
+        if (blk >= 0) {
+          const int bsz = BS > 0 ? BS : p.bs;
+          src = (is_v ? pv : pk) + ((size_t)blk * bsz + off) * row_stride + head_off + ch * 8;
+          bytes = 16;
+        }
+      }
+      const uint32_t dst = sbase + (uint32_t)(stage * 2 * TILE + (is_v ? TILE : 0) + kk * ROW + ch * 16);
+      cp_async16(dst, src, bytes);
+    }
+  };
+
+  // Prologue: keep kMmaStages - 1 tiles in flight (one commit group per tile, empty groups past the end).
+#pragma unroll
+  for (int t = 0; t < kMmaStages - 1; ++t) {
+    if (t < n_tiles) load_tile(t, t);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+
+  // Q fragments for this warp's 16 rows (rows >= `rows` are zero).
+  const int r_lo = warp * 16 + g, r_hi = r_lo + 8;
+  uint32_t qa[KSTEPS][4];
+  {
+    const __nv_bfloat16* q_lo = nullptr;
+    const __nv_bfloat16* q_hi = nullptr;
+    if (r_lo < rows) q_lo = q + ((size_t)(qoff + t0 + r_lo / p.group) * p.nq + h * p.group + r_lo % p.group) * HD;
+    if (r_hi < rows) q_hi = q + ((size_t)(qoff + t0 + r_hi / p.group) * p.nq + h * p.group + r_hi % p.group) * HD;
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      const int d0 = kk * 16 + 2 * tq;
+      qa[kk][0] = q_lo ? *reinterpret_cast<const uint32_t*>(q_lo + d0) : 0u;
+      qa[kk][1] = q_hi ? *reinterpret_cast<const uint32_t*>(q_hi + d0) : 0u;
+      qa[kk][2] = q_lo ? *reinterpret_cast<const uint32_t*>(q_lo + d0 + 8) : 0u;
+      qa[kk][3] = q_hi ? *reinterpret_cast<const uint32_t*>(q_hi + d0 + 8) : 0u;
+    }
+  }
+  const int pos_lo = first_pos + (r_lo < rows ? r_lo / p.group : 0);
+  const int pos_hi = first_pos + (r_hi < rows ? r_hi / p.group : 0);
+
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+  float acc[DT][4];
+#pragma unroll
+  for (int j = 0; j < DT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int stage = tile % kMmaStages;
+    // Tile `tile` is the oldest outstanding group once kMmaStages - 2 newer ones may remain.
+    asm volatile("cp.async.wait_group %0;" ::"n"(kMmaStages - 2) : "memory");
+    __syncthreads();
+    // Refill the stage freed by the previous iteration (everyone passed the barrier above).
+    if (tile + kMmaStages - 1 < n_tiles) load_tile(tile + kMmaStages - 1, (tile + kMmaStages - 1) % kMmaStages);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint32_t kbase = sbase + stage * 2 * TILE;
+    const uint32_t vbase = kbase + TILE;
+    const int kt = key_lo + tile * kMmaKeyTile;
+    if (warp * 16 < rows) {
+      // S = Q K^T over this tile's 32 keys.
+      float sc[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < KSTEPS; ++kk) {
+#pragma unroll
+        for (int j2 = 0; j2 < NT; j2 += 2) {
+          // 4 matrices: keys [8*j2, 8*j2+8) dims k0..k0+7 / k0+8..k0+15, keys [8*j2+8, ...) same dims
+          const int mat = lane >> 3, rr = lane & 7;
+          const int key_row = 8 * j2 + ((mat >> 1) << 3) + rr;
+          const int dim = kk * 16 + ((mat & 1) << 3);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kbase + key_row * ROW + dim * 2, b0, b1, b2, b3);
+          mma_bf16_16816(sc[j2], qa[kk], b0, b1);
+          mma_bf16_16816(sc[j2 + 1], qa[kk], b2, b3);
+        }
+      }
+      // scale, causal mask, online softmax (rows g and g+8 of this warp)
+      float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = kt + 8 * j + 2 * tq + e;
+          const bool ok = key < key_hi;
+          sc[j][e] = (ok && key <= pos_lo) ? sc[j][e] * p.scale : -INFINITY;
+          sc[j][2 + e] = (ok && key <= pos_hi) ? sc[j][2 + e] * p.scale : -INFINITY;
+          mx_lo = fmaxf(mx_lo, sc[j][e]);
+          mx_hi = fmaxf(mx_hi, sc[j][2 + e]);
+        }
+      }
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+      const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+      // Rows whose tile is fully masked keep their state exactly (factor 1, p = 0).
+      const float f_lo = mx_lo == -INFINITY ? 1.f : expf(m_lo - mn_lo);
+      const float f_hi = mx_hi == -INFINITY ? 1.f : expf(m_hi - mn_hi);
+      float s_lo = 0.f, s_hi = 0.f;
+      uint32_t pa[NT / 2][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const float p0 = sc[j][0] == -INFINITY ? 0.f : expf(sc[j][0] - mn_lo);
+        const float p1 = sc[j][1] == -INFINITY ? 0.f : expf(sc[j][1] - mn_lo);
+        const float p2 = sc[j][2] == -INFINITY ? 0.f : expf(sc[j][2] - mn_hi);
+        const float p3 = sc[j][3] == -INFINITY ? 0.f : expf(sc[j][3] - mn_hi);
+        s_lo += p0 + p1;
+        s_hi += p2 + p3;
+        pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16(p0, p1);
+        pa[j >> 1][(j & 1) * 2 + 1] = pack_bf16(p2, p3);
+      }
+      s_lo += __shfl_xor_sync(0xffffffffu, s_lo, 1);
+      s_lo += __shfl_xor_sync(0xffffffffu, s_lo, 2);
+      s_hi += __shfl_xor_sync(0xffffffffu, s_hi, 1);
+      s_hi += __shfl_xor_sync(0xffffffffu, s_hi, 2);
+      if (mx_lo != -INFINITY) { l_lo = l_lo * f_lo + s_lo; m_lo = mn_lo; }
+      if (mx_hi != -INFINITY) { l_hi = l_hi * f_hi + s_hi; m_hi = mn_hi; }
+#pragma unroll
+      for (int j = 0; j < DT; ++j) {
+        acc[j][0] *= f_lo; acc[j][1] *= f_lo;
+        acc[j][2] *= f_hi; acc[j][3] *= f_hi;
+      }
+      // O += P V: P (16 x 32 keys) as two k16 A fragments, V via transposed ldmatrix.
+#pragma unroll
+      for (int s16 = 0; s16 < NT / 2; ++s16) {
+        // A fragment order: (row g, keys 2t..), (row g+8, keys 2t..), (row g, keys 8+2t..), (row g+8, keys 8+2t..)
+        const uint32_t a[4] = {pa[s16][0], pa[s16][1], pa[s16][2], pa[s16][3]};
+#pragma unroll
+        for (int j2 = 0; j2 < DT; j2 += 2) {
+          const int mat = lane >> 3, rr = lane & 7;
+          const int key_row = s16 * 16 + ((mat & 1) << 3) + rr;
+          const int dim = 8 * j2 + ((mat >> 1) << 3);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vbase + key_row * ROW + dim * 2, b0, b1, b2, b3);
+          mma_bf16_16816(acc[j2], a, b0, b1);
+          mma_bf16_16816(acc[j2 + 1], a, b2, b3);
+        }
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+
+  // Write the normalised output, or this chunk's partial for the combine kernel.
+  if (warp * 16 >= rows) return;
+  if (p.ws == nullptr) {
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = half ? r_hi : r_lo;
+      if (r >= rows) continue;
+      const float l = half ? l_hi : l_lo;
+      __nv_bfloat16* o = out + ((size_t)(qoff + t0 + r / p.group) * p.nq + h * p.group + r % p.group) * HD;
+#pragma unroll
+      for (int j = 0; j < DT; ++j) {
+        const float v0 = acc[j][half * 2] / l, v1 = acc[j][half * 2 + 1] / l;
+        *reinterpret_cast<uint32_t*>(o + 8 * j + 2 * tq) = pack_bf16(v0, v1);
+      }
+    }
+  } else {
+    float* part = p.ws + ((((size_t)bh * p.n_qtiles + qtile) * p.n_chunks) + c) * partial_floats(HD);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = half ? r_hi : r_lo;
+      if (r >= rows) continue;
+      float* pr = part + (size_t)r * (HD + 2);
+#pragma unroll
+      for (int j = 0; j < DT; ++j) {
+        pr[8 * j + 2 * tq] = acc[j][half * 2];
+        pr[8 * j + 2 * tq + 1] = acc[j][half * 2 + 1];
+      }
+      if (tq == 0) {
+        pr[HD] = half ? m_hi : m_lo;
+        pr[HD + 1] = half ? l_hi : l_lo;
+      }
+    }
+  }
+}
+
 // Merge chunk partials in chunk order. A row at position pos reads chunks
 // 0 .. pos / kChunk; with a single chunk this reproduces acc / l exactly.
 template <typename T, int HD>
@@ -219,14 +511,25 @@ attn_combine_kernel(AttnParams p) {
 
 template <typename T, int HD>
 int launch(AttnParams& p, int batch, cudaStream_t stream) {
-  size_t smem = sizeof(float) * ((size_t)kMaxRows * HD + kKeyTile * (HD + 1) + kKeyTile * HD);
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(paged_attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    configured = true;
-  }
   dim3 grid(p.n_chunks, batch * p.nkv, p.n_qtiles);
-  paged_attn_kernel<T, HD><<<grid, kAttnThreads, smem, stream>>>(p);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    // stages x (K + V) tiles, then the chunk's block table (<= 512 entries for block size >= 1)
+    const size_t smem = (size_t)kMmaStages * 2 * kMmaKeyTile * (HD * 2 + 16) + kChunk * sizeof(int);
+    static std::once_flag once;
+    std::call_once(once, [smem] {
+      cudaFuncSetAttribute(paged_attn_mma_kernel<HD, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaFuncSetAttribute(paged_attn_mma_kernel<HD, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    });
+    if (p.bs == 16) paged_attn_mma_kernel<HD, 16><<<grid, kAttnThreads, smem, stream>>>(p);
+    else paged_attn_mma_kernel<HD, 0><<<grid, kAttnThreads, smem, stream>>>(p);
+  } else {
+    const size_t smem = sizeof(float) * ((size_t)kMaxRows * HD + kKeyTile * (HD + 1) + kKeyTile * HD);
+    static std::once_flag once;
+    std::call_once(once, [smem] {
+      cudaFuncSetAttribute(paged_attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    });
+    paged_attn_kernel<T, HD><<<grid, kAttnThreads, smem, stream>>>(p);
+  }
   int rc = check_launch("kve_paged_verify_attn");
   if (rc || !p.ws) return rc;
   attn_combine_kernel<T, HD><<<dim3(batch * p.nkv, p.n_qtiles), kAttnThreads, 0, stream>>>(p);

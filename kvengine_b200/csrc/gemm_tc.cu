@@ -2,25 +2,31 @@
 //
 // Weight-streaming shape (m = batch * (k+1) tokens is small, n = features is
 // large), so the MMA's M dimension runs over FEATURES: one CTA owns 128 weight
-// rows x `nt` tokens (nt <= 256) and accumulates D^T[128, nt] in TMEM.
-// Weights are read from HBM once per token tile; CTAs of the same feature tile
-// are adjacent in launch order, so a second token tile re-reads them from L2.
+// rows x `mt` tokens and accumulates D^T[128, mt] in TMEM. Weights are read
+// from HBM once per token tile; CTAs of the same feature tile are adjacent in
+// launch order, so further token tiles re-read them from L2.
 //
 //   warp 0      TMA producer: 128x64 weight tile + nt x 64 token tile per
 //               stage (SWIZZLE_128B, K-major), mbarrier expect-tx
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //               (kind::f16, bf16 x bf16 -> fp32), tcgen05.commit frees stages
 //   warps 2-5   epilogue: tcgen05.ld 32x32b (one feature row per thread),
-//               fused bias / residual / SwiGLU, store
+//               fused bias / residual / SwiGLU, staged 16-byte stores
 //
-// Small grids split K across CTAs. The split count depends only on (n, k), and
-// the last-arriving CTA of a tile sums the fp32 partials in split order, so a
-// row's result never depends on m (draft and verify passes agree bit for bit).
-// Every mbarrier wait is bounded; a timeout is reported through `status`.
+// Up to 384 tokens share one CTA (two MMAs per k-step into two TMEM column
+// ranges); larger batches tile tokens by 256. Small grids split K over a thread-
+// block cluster of up to 8 CTAs: each CTA parks its fp32 partial in its own
+// shared memory and the cluster sums them in rank order through distributed
+// shared memory, each CTA finishing a slice of the tokens (no global
+// workspace). The split count depends only on (n, k), so a row's result never
+// depends on m (draft and verify passes agree bit for bit). The epilogue stages
+// each 64-token chunk in shared memory and writes whole rows with 16-byte
+// stores. Every mbarrier wait is bounded; a timeout is reported via `status`.
 #include <cuda.h>
 #include <math.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "gemm_epilogue.cuh"
 
@@ -31,17 +37,22 @@ constexpr int BM = 128;          // features per tile (MMA M)
 constexpr int BK = 64;           // K per stage: one 128-byte swizzle row of bf16
 constexpr int UMMA_K = 16;       // K per tcgen05.mma for 16-bit inputs
 constexpr int kThreads = 192;    // 6 warps
-constexpr int kMaxNT = 256;
+constexpr int kMaxNG = 256;      // tokens per MMA (N of one tcgen05.mma)
 constexpr int kMaxStages = 8;
-constexpr size_t kSmemLimit = 232448;  // 227 KB opt-in
+constexpr int kMaxSplits = 8;    // portable cluster size
+constexpr int kRows = 32;                    // tokens per staged output chunk
+constexpr int kStageBytes = 2 * kRows * 128 * 4;  // double-buffered output staging (fp32 worst case)
+constexpr size_t kSmemLimit = 232448;       // 227 KB opt-in
 
 struct TcArgs {
   int m, n, k;
-  int nt, k_blocks, splits, stages;
+  int mt, ng, n_g;       // tokens per CTA = ng groups of n_g tokens (one MMA each)
+  int k_blocks, splits, stages;
   uint32_t stage_bytes;
+  int rch;               // split-K: tokens reduced per round (the receive buffer holds rch tokens)
+  int stg_off;           // byte offset of the output staging buffer in the drained stage area
+  int out_vec_ok;        // output rows start on 16-byte boundaries
   EpiArgs e;
-  float* ws;        // [splits, m, n] fp32 partials (splits > 1)
-  int* counters;    // [tiles] arrival counters (splits > 1)
   int* status;
 };
 
@@ -55,6 +66,10 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -102,9 +117,9 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16: D fp32, A/B bf16, both K-major, M=128, N=nt.
-__device__ __forceinline__ uint32_t umma_idesc(int nt) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor, kind::f16: D fp32, A/B bf16, both K-major, M=128, N=n.
+__device__ __forceinline__ uint32_t umma_idesc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
@@ -136,20 +151,134 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
 
-// One accumulator value for (token row, feature col): final epilogue. SwiGLU
-// pairs live in adjacent lanes (features 2j, 2j+1), so every lane calls this.
-__device__ __forceinline__ void finish(const TcArgs& a, int row, int col, float v, bool valid) {
-  if (a.e.mode == KVE_EPI_SILU_MUL) {
-    float other = __shfl_xor_sync(0xffffffffu, v, 1);
-    if (valid && (col & 1) == 0 && col + 1 < a.n) epi_silu_mul(a.e, row, col >> 1, v, other);
-  } else if (valid) {
-    epi_store(a.e, row, col, v);
+// Up to 32 TMEM columns (n is 16 or 32) of this thread's lane into v.
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, int n, bool have, float* v) {
+  if (!have) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    return;
+  }
+  if (n == 32) {
+    tmem_ld32(taddr, v);
+  } else {
+    float h[16];
+    tmem_ld16(taddr, h);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = h[i];
   }
 }
 
+template <int MODE, bool BF>
+struct Epi {
+  using T = typename std::conditional<BF, __nv_bfloat16, float>::type;
+  static constexpr int ES = BF ? 2 : 4;
+  static constexpr int W = MODE == KVE_EPI_SILU_MUL ? BM / 2 : BM;  // output columns per tile
+  static constexpr int VE = 16 / ES;                                 // elements per 16-byte vector
+  static constexpr int VPR = W / VE;                                 // vectors per staged row
+
+  static __device__ __forceinline__ float rnd(float v) { return BF ? __bfloat162float(__float2bfloat16_rn(v)) : v; }
+  static __device__ __forceinline__ T cvt(float v) {
+    if constexpr (BF) return __float2bfloat16_rn(v);
+    else return v;
+  }
+
+  // Staged row r of a dense [kRows][W] buffer: this thread's feature of one token.
+  // SwiGLU pairs sit in adjacent lanes (features 2j, 2j+1), so all lanes call this.
+  static __device__ __forceinline__ void stage(uint8_t* buf, int r, int f_local, float v, float bias_f) {
+    T* b = reinterpret_cast<T*>(buf);
+    if constexpr (MODE == KVE_EPI_SILU_MUL) {
+      float other = __shfl_xor_sync(0xffffffffu, v, 1);
+      if ((f_local & 1) == 0) {
+        float g = rnd(v), u = rnd(other);
+        b[r * W + (f_local >> 1)] = cvt(__fmul_rn(rnd(silu_ref(g)), u));
+      }
+    } else if constexpr (MODE == KVE_EPI_BIAS) {
+      b[r * W + f_local] = cvt(__fadd_rn(v, bias_f));
+    } else {
+      b[r * W + f_local] = cvt(v);  // RESIDUAL adds the residual while copying out
+    }
+  }
+
+  // Write staged rows [0, nr) (tokens tok_base ...) with 16-byte stores. Thread
+  // etid always handles the same column vector; 128 / VPR rows per pass.
+  static __device__ __forceinline__ void copy_out(const TcArgs& a, const uint8_t* buf, int tok_base, int nr,
+                                                  int col0, int etid) {
+    constexpr int RPP = 128 / VPR;  // rows per pass
+    const int nvalid = min(W, a.e.ld_out - col0);
+    const int c = (etid % VPR) * VE;
+    const int r_first = etid / VPR;
+    if (c >= nvalid) return;
+    const bool vec = a.out_vec_ok && c + VE <= nvalid;
+    const T* src0 = reinterpret_cast<const T*>(buf) + c;
+    T* dst0 = static_cast<T*>(a.e.out) + (size_t)col0 + c;
+    const T* res0 = static_cast<const T*>(a.e.residual) + (size_t)col0 + c;
+#pragma unroll 4
+    for (int r = r_first; r < nr; r += RPP) {
+      const int t = tok_base + r;
+      if (t >= a.m) break;
+      const T* src = src0 + r * W;
+      T* dst = dst0 + (size_t)t * a.e.ld_out;
+      if (vec) {
+        uint4 val = *reinterpret_cast<const uint4*>(src);
+        if constexpr (MODE == KVE_EPI_RESIDUAL) {
+          uint4 res = *reinterpret_cast<const uint4*>(res0 + (size_t)t * a.e.ld_out);
+          T* y = reinterpret_cast<T*>(&val);
+          const T* q = reinterpret_cast<const T*>(&res);
+#pragma unroll
+          for (int j = 0; j < VE; ++j) y[j] = cvt(__fadd_rn((float)q[j], (float)y[j]));
+        }
+        *reinterpret_cast<uint4*>(dst) = val;
+      } else {
+        for (int j = 0; j < VE && c + j < nvalid; ++j) {
+          float y = (float)src[j];
+          if constexpr (MODE == KVE_EPI_RESIDUAL) y = __fadd_rn((float)res0[(size_t)t * a.e.ld_out + j], y);
+          dst[j] = cvt(y);
+        }
+      }
+    }
+  }
+};
+
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                  uint32_t mbar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst_cluster), "r"(src_cta), "r"(bytes), "r"(mbar_cluster)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t map_to(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+template <int MODE, bool BF, int NG>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, TcArgs a) {
+  using E = Epi<MODE, BF>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Stage buffers need 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -157,11 +286,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxStages;
   uint64_t* tmem_full = bars + 2 * kMaxStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 1);
-  int& s_last = *reinterpret_cast<int*>(tmem_slot + 1);
+  uint64_t* epi_done = bars + 2 * kMaxStages + 1;
+  uint64_t* recv_bar = bars + 2 * kMaxStages + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 3);
+  // After the main loop the drained stage buffers hold the split-K exchange
+  // buffers (offset 0) and the output staging (offset stg_off).
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tok0 = blockIdx.x * a.nt;
+  const int tok0 = blockIdx.x * a.mt;
   const int feat0 = blockIdx.y * BM;
   const int split = blockIdx.z;
   const int kb0 = (int)((long long)split * a.k_blocks / a.splits);
@@ -171,7 +303,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
   const int n_iter = aborted ? 0 : kb1 - kb0;
   uint32_t tmem_cols = 32;
-  while ((int)tmem_cols < a.nt) tmem_cols <<= 1;
+  while ((int)tmem_cols < a.mt) tmem_cols <<= 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -179,8 +311,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       mbar_init(smem_u32(&empty[s]), 1);
     }
     mbar_init(smem_u32(tmem_full), 1);
+    mbar_init(smem_u32(epi_done), 4);  // one arrival per epilogue warp
+    mbar_init(smem_u32(recv_bar), 1);  // this CTA's expect-tx arrival per split-K round
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  __syncwarp();
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(tmem_cols)
@@ -195,105 +330,194 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------- producer
-      const uint32_t tx_bytes = a.stage_bytes;
-      int issued = 0;
+      int issued = 0, s = 0;
+      uint32_t ph = 0;
+      uint8_t* sa = smem;
+      int kx = kb0 * BK;
       for (int it = 0; it < n_iter; ++it) {
-        const int s = it % a.stages;
-        const uint32_t ph = (uint32_t)(it / a.stages) & 1u;
         if (it >= a.stages && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, a.status)) break;
-        uint8_t* sa = smem + (size_t)s * a.stage_bytes;
+        const uint32_t fb = smem_u32(&full[s]);
+        mbar_expect_tx(fb, a.stage_bytes);
+        tma_load_2d(smem_u32(sa), &map_w, kx, feat0, fb);
         uint8_t* sb = sa + BM * BK * 2;
-        mbar_expect_tx(smem_u32(&full[s]), tx_bytes);
-        tma_load_2d(smem_u32(sa), &map_w, (kb0 + it) * BK, feat0, smem_u32(&full[s]));
-        tma_load_2d(smem_u32(sb), &map_x, (kb0 + it) * BK, tok0, smem_u32(&full[s]));
+        tma_load_2d(smem_u32(sb), &map_x, kx, tok0, fb);
+        if (NG == 2) tma_load_2d(smem_u32(sb + a.n_g * BK * 2), &map_x, kx, tok0 + a.n_g, fb);
         ++issued;
+        kx += BK;
+        if (++s == a.stages) {
+          s = 0;
+          ph ^= 1u;
+          sa = smem;
+        } else {
+          sa += a.stage_bytes;
+        }
       }
       // Do not leave while a bulk copy may still be writing this CTA's shared memory.
       for (int it = issued - a.stages < 0 ? 0 : issued - a.stages; it < issued; ++it)
         mbar_wait(smem_u32(&full[it % a.stages]), (uint32_t)(it / a.stages) & 1u, a.status);
     }
+    __syncwarp();
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    // One thread issues every MMA; its ALU latency is fully exposed, so the
+    // loop only adds precomputed descriptor deltas (the 14-bit start-address
+    // field counts 16-byte units; stages, k-steps and N groups are offsets).
     if (lane == 0) {
-      // ------------------------------------------------------------ MMA issue
-      const uint32_t idesc = umma_idesc(a.nt);
+      const uint32_t idesc = umma_idesc(a.n_g);
+      const uint64_t a0 = umma_desc(smem_u32(smem));
+      const uint64_t b0 = umma_desc(smem_u32(smem) + BM * BK * 2);
+      const uint64_t stage_step = (uint64_t)(a.stage_bytes >> 4);
+      const uint64_t grp_step = (uint64_t)((a.n_g * BK * 2) >> 4);
+      constexpr uint64_t kstep = (UMMA_K * 2) >> 4;  // 32 bytes along K
+      const uint32_t t1 = tmem_base + a.n_g;
+      int s = 0;
+      uint32_t ph = 0;
+      uint64_t soff = 0;
       for (int it = 0; it < n_iter; ++it) {
-        const int s = it % a.stages;
-        const uint32_t ph = (uint32_t)(it / a.stages) & 1u;
         if (!mbar_wait(smem_u32(&full[s]), ph, a.status)) break;
         fence_after();
-        const uint32_t sa = smem_u32(smem + (size_t)s * a.stage_bytes);
-        const uint32_t sb = sa + BM * BK * 2;
+        const uint64_t ad = a0 + soff, bd = b0 + soff;
+        umma_bf16(tmem_base, ad, bd, idesc, it > 0 ? 1u : 0u);
+        if (NG == 2) umma_bf16(t1, ad, bd + grp_step, idesc, it > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-          umma_bf16(tmem_base, umma_desc(sa + kk * UMMA_K * 2), umma_desc(sb + kk * UMMA_K * 2), idesc,
-                    (it > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 1; kk < BK / UMMA_K; ++kk) {
+          umma_bf16(tmem_base, ad + kk * kstep, bd + kk * kstep, idesc, 1u);
+          if (NG == 2) umma_bf16(t1, ad + kk * kstep, bd + grp_step + kk * kstep, idesc, 1u);
         }
         umma_commit(smem_u32(&empty[s]));
+        if (++s == a.stages) {
+          s = 0;
+          ph ^= 1u;
+          soff = 0;
+        } else {
+          soff += stage_step;
+        }
       }
       umma_commit(smem_u32(tmem_full));  // fires once every issued MMA has completed
     }
-  } else {
-    // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;  // TMEM lane quarter this warp may access
-    const int col_feat = feat0 + quad * 32 + lane;
-    const bool feat_ok = col_feat < a.n;
-    const bool waited = !aborted && mbar_wait(smem_u32(tmem_full), 0, a.status);
+    __syncwarp();
+  }
+
+  // ---------------------------------------------------------------- epilogue
+  // Warps 2-5 own TMEM lane quarters (warp w reads lanes 32*(w%4) ...), i.e.
+  // feature rows; tokens are TMEM columns. Output is staged 32 tokens at a time
+  // in a dense [32][W] buffer (double-buffered) and written as whole rows.
+  const bool epi = warp >= 2;
+  const int quad = warp & 3;
+  const int f_local = quad * 32 + lane;
+  const int feat = feat0 + f_local;
+  const int col0 = MODE == KVE_EPI_SILU_MUL ? feat0 / 2 : feat0;
+  const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);
+  const int etid = threadIdx.x - 64;
+  const float bias_f = (MODE == KVE_EPI_BIAS && epi && feat < a.n) ? a.e.bias[feat] : 0.f;
+  bool have = false;
+  if (epi) {
+    have = !aborted && mbar_wait(smem_u32(tmem_full), 0, a.status);
     fence_after();
-    const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);
-    if (a.splits == 1) {
-      if (waited) {
-        for (int c0 = 0; c0 < a.nt; c0 += 16) {
-          float v[16];
-          tmem_ld16(t_lane + c0, v);
+  }
+  const int S = a.splits;
+  uint8_t* stg = smem + a.stg_off;
+  constexpr int kStgBuf = kRows * BM * 4;  // one staging buffer (fp32 worst case)
+  if (S == 1) {
+    if (epi) {
+      int it = 0;
+      for (int c0 = 0; c0 < a.mt; c0 += kRows, ++it) {
+        const int n = min(kRows, a.mt - c0);
+        uint8_t* buf = stg + (it & 1) * kStgBuf;
+        float v[32];
+        tmem_load_cols(t_lane + c0, n, have, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int row = tok0 + c0 + j;
-            finish(a, row, col_feat, v[j], feat_ok && row < a.m);
-          }
+        for (int j = 0; j < 32; ++j)
+          if (j < n) E::stage(buf, j, f_local, v[j], bias_f);
+        epi_bar();
+        E::copy_out(a, buf, tok0 + c0, n, col0, etid);
+      }
+    }
+  } else {
+    // Split-K over the cluster: each CTA writes its fp32 partial, grouped by the
+    // CTA that owns each token (contiguous slices of the round), and sends every
+    // peer its group with one bulk shared-memory copy; the owner then sums the
+    // S partials of its tokens in rank order from its own shared memory.
+    const uint32_t rank = cluster_rank();
+    const int slm = (a.rch + S - 1) / S;               // max tokens per slice
+    float* pout = reinterpret_cast<float*>(smem);      // [rch][128] this CTA's partial, token-major
+    float* recv = pout + (size_t)a.rch * BM;           // [S][slm][128] received slices, by sender
+    int round = 0;
+    for (int r0 = 0; r0 < a.mt; r0 += a.rch, ++round) {
+      const int ch = min(a.rch, a.mt - r0);
+      // Peers write into this CTA's drained stage buffers: wait until every CTA of
+      // the cluster has finished its main loop (and, in later rounds, its reads).
+      cluster_sync();
+      const int my_lo = (int)((long long)rank * ch / S), my_hi = (int)((long long)(rank + 1) * ch / S);
+      if (epi) {
+        // Owner u's tokens [lo_u, hi_u) are contiguous rows of pout.
+        float* prow = pout + f_local;
+        for (int c = 0; c < ch; c += kRows) {
+          const int n = min(kRows, ch - c);
+          float v[32];
+          tmem_load_cols(t_lane + r0 + c, n, have, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < n) prow[(c + j) * BM] = v[j];
         }
-      }
-    } else {
-      if (waited) {
-        for (int c0 = 0; c0 < a.nt; c0 += 16) {
-          float v[16];
-          tmem_ld16(t_lane + c0, v);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int row = tok0 + c0 + j;
-            if (feat_ok && row < a.m) a.ws[((size_t)split * a.m + row) * a.n + col_feat] = v[j];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        epi_bar();
+        if (etid == 0) {
+          const uint32_t mine = (uint32_t)(my_hi - my_lo);
+          mbar_expect_tx(smem_u32(recv_bar), (uint32_t)(S - 1) * mine * BM * 4);
+          for (int u = 0; u < S; ++u) {
+            if (u == (int)rank) continue;
+            const int lo = (int)((long long)u * ch / S), hi = (int)((long long)(u + 1) * ch / S);
+            if (hi <= lo) continue;
+            bulk_copy_to_peer(map_to(smem_u32(recv + (size_t)rank * slm * BM), (uint32_t)u),
+                              smem_u32(pout + (size_t)lo * BM), (uint32_t)(hi - lo) * BM * 4,
+                              map_to(smem_u32(recv_bar), (uint32_t)u));
           }
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
-      }
-      __threadfence();
-      epi_bar();
-      if (threadIdx.x == 64) {
-        int* ctr = a.counters + (blockIdx.y * gridDim.x + blockIdx.x);
-        int prev = atomicAdd(ctr, 1);
-        s_last = (prev == a.splits - 1);
-        if (s_last) *ctr = 0;
-      }
-      epi_bar();
-      if (s_last) {
-        __threadfence();
-        for (int c0 = 0; c0 < a.nt; c0 += 16) {
+        mbar_wait(smem_u32(recv_bar), (uint32_t)(round & 1), a.status);
+        // Sum the S partials of each owned token in rank order (own slice from pout).
+        const float* src[kMaxSplits];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int row = tok0 + c0 + j;
-            const bool valid = feat_ok && row < a.m;
-            float acc = 0.f;
-            if (valid) {
-              const float* p = a.ws + (size_t)row * a.n + col_feat;
-              for (int s = 0; s < a.splits; ++s) acc += __ldcg(p + (size_t)s * a.m * a.n);
+        for (int u = 0; u < kMaxSplits; ++u)
+          src[u] = (u == (int)rank ? pout + (size_t)my_lo * BM : recv + (size_t)u * slm * BM) + f_local;
+        const int mine = my_hi - my_lo;
+        int it = 0;
+        for (int t0 = 0; t0 < mine; t0 += kRows, ++it) {
+          const int n = min(kRows, mine - t0);
+          uint8_t* buf = stg + (it & 1) * kStgBuf;
+          for (int j0 = 0; j0 < n; j0 += 4) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int u = 0; u < kMaxSplits; ++u) {
+              if (u < S) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  if (j0 + q < n) acc[q] += src[u][(t0 + j0 + q) * BM];
+              }
             }
-            finish(a, row, col_feat, acc, valid);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (j0 + q < n) E::stage(buf, j0 + q, f_local, acc[q], bias_f);
           }
+          epi_bar();
+          E::copy_out(a, buf, tok0 + r0 + my_lo + t0, n, col0, etid);
         }
+        if (etid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        epi_bar();
       }
     }
   }
-  fence_before();
-  __syncthreads();
-  if (warp == 1) {
+
+  if (epi) {
+    // Every tcgen05.ld of this warp has completed (wait::ld); tell warp 1 it may free TMEM.
+    fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(epi_done));
+  } else if (warp == 1) {
+    // Free TMEM only after the epilogue is done with it (bounded wait; freed either way
+    // so a later CTA on this SM can always allocate).
+    mbar_wait(smem_u32(epi_done), 0, a.status);
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
                  : "memory");
@@ -333,75 +557,176 @@ int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int box_rows) {
 }
 
 struct Plan {
-  int nt, token_tiles, feat_tiles, k_blocks, splits, stages;
+  int mt, ng, n_g, token_tiles, feat_tiles, k_blocks, splits, stages, rch, stg_off;
   uint32_t stage_bytes;
 };
 
+inline int round16(int x) { return (x + 15) / 16 * 16; }
+
+typedef void (*GemmKernel)(CUtensorMap, CUtensorMap, TcArgs);
+
+template <int NG>
+GemmKernel kernel_for_ng(int mode, bool bf) {
+  switch (mode) {
+    case KVE_EPI_BIAS: return bf ? gemm_tc_kernel<KVE_EPI_BIAS, true, NG> : gemm_tc_kernel<KVE_EPI_BIAS, false, NG>;
+    case KVE_EPI_RESIDUAL:
+      return bf ? gemm_tc_kernel<KVE_EPI_RESIDUAL, true, NG> : gemm_tc_kernel<KVE_EPI_RESIDUAL, false, NG>;
+    case KVE_EPI_SILU_MUL:
+      return bf ? gemm_tc_kernel<KVE_EPI_SILU_MUL, true, NG> : gemm_tc_kernel<KVE_EPI_SILU_MUL, false, NG>;
+    default: return bf ? gemm_tc_kernel<KVE_EPI_STORE, true, NG> : gemm_tc_kernel<KVE_EPI_STORE, false, NG>;
+  }
+}
+
+GemmKernel kernel_for(int mode, int out_dtype, int ng) {
+  const bool bf = out_dtype == KVE_BF16;
+  return ng == 2 ? kernel_for_ng<2>(mode, bf) : kernel_for_ng<1>(mode, bf);
+}
+
+void configure_kernel() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    for (int mode = KVE_EPI_STORE; mode <= KVE_EPI_SILU_MUL; ++mode)
+      for (int dt : {KVE_F32, KVE_BF16})
+        for (int ng : {1, 2})
+          cudaFuncSetAttribute(kernel_for(mode, dt, ng), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)(kSmemLimit - 512));
+  });
+}
+
+// Concurrent CTAs for each cluster size with one CTA per SM (queried once).
+const int* cluster_capacity() {
+  static int cap[kMaxSplits + 1];
+  static std::once_flag once;
+  std::call_once(once, [] {
+    configure_kernel();
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    for (int s = 1; s <= kMaxSplits; ++s) {
+      cap[s] = (sms / s) * s;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, 1, s);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = kSmemLimit - 512;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 1;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = s;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(KVE_EPI_STORE, KVE_BF16, 1), &cfg) == cudaSuccess && n > 0)
+        cap[s] = n * s;
+    }
+    cudaGetLastError();
+  });
+  return cap;
+}
+
+// Split-K factor: a function of (n, k) only, so a row's reduction order never
+// depends on how many tokens are in the batch. Picks the cluster size that
+// minimises (waves x k-blocks per split + fixed per-CTA cost).
+int choose_splits(int feat_tiles, int k_blocks) {
+  const int* cap = cluster_capacity();
+  int best = 1;
+  double best_t = 1e30;
+  for (int s = 1; s <= kMaxSplits; ++s) {
+    if (s > 1 && k_blocks / s < 2) break;
+    int ctas = feat_tiles * s;
+    int waves = (ctas + cap[s] - 1) / cap[s];
+    double t = waves * ((k_blocks + s - 1) / s + 3.0);
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
 Plan make_plan(int m, int n, int k) {
   Plan p{};
-  p.token_tiles = (m + kMaxNT - 1) / kMaxNT;
-  if (p.token_tiles < 1) p.token_tiles = 1;
-  int per = (m + p.token_tiles - 1) / p.token_tiles;
-  p.nt = ((per + 15) / 16) * 16;
-  if (p.nt < 16) p.nt = 16;
   p.feat_tiles = (n + BM - 1) / BM;
   p.k_blocks = (k + BK - 1) / BK;
-  // Split K only to fill the machine; depends on (n, k) alone.
-  int want = (148 + p.feat_tiles - 1) / p.feat_tiles;
-  int max_splits = p.k_blocks / 4;
-  if (max_splits < 1) max_splits = 1;
-  p.splits = want < max_splits ? want : max_splits;
-  if (p.splits < 1) p.splits = 1;
-  p.stage_bytes = (uint32_t)(BM * BK * 2 + p.nt * BK * 2);
+  if (m <= kMaxNG) {
+    p.token_tiles = 1; p.ng = 1; p.n_g = round16(m < 16 ? 16 : m);
+  } else if (m <= 384) {
+    p.token_tiles = 1; p.ng = 2; p.n_g = round16((m + 1) / 2);
+  } else {
+    p.token_tiles = (m + kMaxNG - 1) / kMaxNG; p.ng = 1; p.n_g = round16((m + p.token_tiles - 1) / p.token_tiles);
+  }
+  p.mt = p.ng * p.n_g;
+  p.stage_bytes = (uint32_t)(BM * BK * 2 + p.mt * BK * 2);
   size_t avail = kSmemLimit - 2048 /*align slack + barriers + margin*/;
   p.stages = (int)(avail / p.stage_bytes);
   if (p.stages > kMaxStages) p.stages = kMaxStages;
+  p.splits = choose_splits(p.feat_tiles, p.k_blocks);
+  p.rch = p.mt;
+  p.stg_off = 0;
+  if (p.splits > 1) {
+    // Largest round whose exchange buffers (outgoing [rch][128] + incoming
+    // [S][ceil(rch/S)][128] fp32) fit in the drained stage area next to the staging.
+    const size_t area = (size_t)p.stages * p.stage_bytes;
+    p.rch = 0;
+    for (int ch = p.mt; ch >= 16; ch -= 16) {
+      size_t slm = (ch + p.splits - 1) / p.splits;
+      size_t xbuf = ((size_t)ch + (size_t)p.splits * slm) * BM * 4;
+      size_t off = (xbuf + 1023) / 1024 * 1024;
+      if (off + kStageBytes <= area) {
+        p.rch = ch;
+        p.stg_off = (int)off;
+        break;
+      }
+    }
+  }
   return p;
 }
 
 }  // namespace
 
-size_t gemm_tc_workspace_bytes(int m, int n, int k) {
-  Plan p = make_plan(m, n, k);
-  if (p.splits <= 1) return 0;
-  size_t part = (size_t)p.splits * m * n * sizeof(float);
-  size_t ctr = (size_t)p.token_tiles * p.feat_tiles * sizeof(int);
-  return ((ctr + 255) / 256) * 256 + part;
-}
+size_t gemm_tc_workspace_bytes(int, int, int) { return 0; }
 
-int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e, void* workspace,
-            size_t workspace_bytes, int* status, cudaStream_t stream) {
+int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e, void*, size_t, int* status,
+            cudaStream_t stream) {
   if (k % 8) return set_error(KVE_ERR_SHAPE, "kve_gemm(tcgen05): k=%d must be a multiple of 8", k);
   if ((uintptr_t)x % 16 || (uintptr_t)w % 16)
     return set_error(KVE_ERR_ARG, "kve_gemm(tcgen05): x and w must be 16-byte aligned");
   if (e.mode == KVE_EPI_SILU_MUL && (n % 2))
     return set_error(KVE_ERR_SHAPE, "kve_gemm: SILU_MUL needs an even n");
+  configure_kernel();
   Plan p = make_plan(m, n, k);
-  if (p.stages < 2) return set_error(KVE_ERR_SHAPE, "kve_gemm(tcgen05): tile does not fit shared memory");
+  if (p.stages < 2 || (p.splits > 1 && p.rch == 0))
+    return set_error(KVE_ERR_SHAPE, "kve_gemm(tcgen05): tile does not fit shared memory");
   TcArgs a{};
-  a.m = m; a.n = n; a.k = k; a.nt = p.nt; a.k_blocks = p.k_blocks; a.splits = p.splits; a.stages = p.stages;
-  a.stage_bytes = p.stage_bytes; a.e = e; a.status = status;
-  if (p.splits > 1) {
-    size_t need = gemm_tc_workspace_bytes(m, n, k);
-    if (!workspace || workspace_bytes < need)
-      return set_error(KVE_ERR_WORKSPACE, "kve_gemm(tcgen05): workspace needs %zu bytes", need);
-    size_t ctr = (size_t)p.token_tiles * p.feat_tiles * sizeof(int);
-    a.counters = static_cast<int*>(workspace);
-    a.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((ctr + 255) / 256) * 256);
-  }
+  a.m = m; a.n = n; a.k = k; a.mt = p.mt; a.ng = p.ng; a.n_g = p.n_g; a.k_blocks = p.k_blocks;
+  a.splits = p.splits; a.stages = p.stages; a.stage_bytes = p.stage_bytes; a.e = e; a.status = status;
+  a.rch = p.rch; a.stg_off = p.stg_off;
+  const int es = e.out_dtype == KVE_BF16 ? 2 : 4;
+  a.out_vec_ok = ((uintptr_t)e.out % 16 == 0) && ((size_t)e.ld_out * es % 16 == 0) &&
+                 (e.mode != KVE_EPI_RESIDUAL || (uintptr_t)e.residual % 16 == 0);
   CUtensorMap mw, mx;
   int rc = make_map(&mw, w, n, k, BM);
   if (rc) return rc;
-  rc = make_map(&mx, x, m, k, p.nt);
+  rc = make_map(&mx, x, m, k, p.n_g);
   if (rc) return rc;
-  size_t smem = (size_t)p.stages * p.stage_bytes + 1024 + 512;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
-    configured = true;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.token_tiles, p.feat_tiles, p.splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)p.stages * p.stage_bytes + 1024 + 512;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = p.splits;
+  cfg.attrs = &attr;
+  cfg.numAttrs = p.splits > 1 ? 1 : 0;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel_for(e.mode, e.out_dtype, p.ng), mw, mx, a);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    count_launch();
+    return set_error(KVE_ERR_CUDA, "kve_gemm(tcgen05): launch failed: %s", cudaGetErrorString(err));
   }
-  dim3 grid(p.token_tiles, p.feat_tiles, p.splits);
-  gemm_tc_kernel<<<grid, kThreads, smem, stream>>>(mw, mx, a);
   return check_launch("kve_gemm(tcgen05)");
 }
 
