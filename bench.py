@@ -264,11 +264,13 @@ def run_gpu(args):
            "api": "kvengine_b200.speculative_greedy_batch(pinned host prompt tensor) -> host token lists; "
                   "counted bytes = every plan/token upload and every accept readback"}
 
-    # ------------------------------------------------- results to rank 0 (NCCL, untimed)
+    # ------------------------------------------------- results to every rank (NCCL, untimed)
     if world > 1:
-        mine = torch.tensor([r.res.new_token_ids for r in collected[-1]], dtype=torch.int32, device=dev)
-        gathered = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(gathered, mine)
+        from kvengine_b200.distributed import gather_tokens
+
+        local = {rank * N_REQ + i: r.res.new_token_ids for i, r in enumerate(collected[-1])}
+        everything = gather_tokens(local, device=dev)
+        assert len(everything) == N_REQ * world
         dist.barrier()
         dist.destroy_process_group()
 
@@ -469,17 +471,29 @@ def run_micro(args):
                     "gbs": round((kvb + qob) / ms / 1e6, 1), "frac_hbm": round((kvb + qob) / ms / 1e6 / pk["hbm_gbs"], 4)})
     if "gemm" in which:
         g = torch.Generator(device=dev).manual_seed(0)
-        for name, m, n, k in (("qkv", 320, 2560, 2048), ("o_proj", 320, 2048, 2048), ("gate_up", 320, 22016, 2048),
-                              ("down", 320, 2048, 11008), ("lm_head", 320, 151936, 2048),
-                              ("draft_gate_up", 64, 9728, 896), ("draft_lm_head", 64, 151936, 896)):
+        from kvengine_b200 import _lib as L
+
+        # Each shape with the epilogue the forward pass uses on it (verify pass of
+        # 64 requests x 5 rows on the 3B target; one-token draft pass on the 0.5B).
+        cases = (("qkv", 320, 2560, 2048, L.EPI_BIAS), ("o_proj", 320, 2048, 2048, L.EPI_RESIDUAL),
+                 ("gate_up", 320, 22016, 2048, L.EPI_SILU_MUL), ("down", 320, 2048, 11008, L.EPI_RESIDUAL),
+                 ("lm_head", 320, 151936, 2048, L.EPI_STORE),
+                 ("draft_qkv", 64, 1152, 896, L.EPI_BIAS), ("draft_o_proj", 64, 896, 896, L.EPI_RESIDUAL),
+                 ("draft_gate_up", 64, 9728, 896, L.EPI_SILU_MUL), ("draft_down", 64, 896, 4864, L.EPI_RESIDUAL),
+                 ("draft_lm_head", 64, 151936, 896, L.EPI_STORE))
+        for name, m, n, k, epi in cases:
             if args.gemm_case and name not in args.gemm_case.split(","):
                 continue
             x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
             copies = max(1, -(-2 * L2_BYTES // (n * k * 2)))  # cold weights on every call
             wts = [(torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16) for _ in range(copies)]
-            y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-            ms = _time_launches([(lambda wt=wt: ops.gemm(x, wt, out=y)) for wt in wts], args.steps)
-            bts = (n * k + m * k + m * n) * 2
+            n_out = n // 2 if epi == L.EPI_SILU_MUL else n
+            y = torch.randn(m, n_out, device=dev, generator=g).to(torch.bfloat16)
+            bias = torch.randn(n, device=dev, generator=g) if epi == L.EPI_BIAS else None
+            res = y if epi == L.EPI_RESIDUAL else None  # in place, as the forward pass does
+            ms = _time_launches([(lambda wt=wt: ops.gemm(x, wt, epilogue=epi, bias=bias, residual=res, out=y))
+                                 for wt in wts], args.steps)
+            bts = (n * k + m * k + m * n_out * (2 if res is not None else 1)) * 2
             fl = 2.0 * m * n * k
             out.append({"micro": f"gemm_tcgen05 {name}", "m": m, "n": n, "k": k, "ms": round(ms, 4),
                         "weight_copies": copies,
