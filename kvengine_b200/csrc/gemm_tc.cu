@@ -26,6 +26,7 @@
 #include <math.h>
 
 #include <mutex>
+#include <unordered_map>
 #include <type_traits>
 
 #include "gemm_epilogue.cuh"
@@ -205,28 +206,64 @@ struct Epi {
     else return v;
   }
 
-  // Staged row r of a dense [kRows][W] buffer: this thread's feature of one token.
-  // SwiGLU pairs sit in adjacent lanes (features 2j, 2j+1), so all lanes call this.
-  static __device__ __forceinline__ void stage(uint8_t* buf, int r, int f_local, float v, float bias_f) {
+  // Stage values v[0..CNT) of this thread's feature for tokens r0 .. r0+CNT-1 into
+  // the dense [kRows][W] buffer (rows >= nr are skipped). Every lane of the warp
+  // calls this. SwiGLU pairs sit in adjacent lanes (gate 2j, up 2j+1): the pair
+  // trades one value per two tokens, so the even lane finishes token r and the
+  // odd lane token r+1 and no lane idles.
+  template <int CNT>
+  static __device__ __forceinline__ void stage(uint8_t* buf, int r0, int nr, int f_local, const float* v,
+                                               float bias_f) {
     T* b = reinterpret_cast<T*>(buf);
     if constexpr (MODE == KVE_EPI_SILU_MUL) {
-      float other = __shfl_xor_sync(0xffffffffu, v, 1);
-      if ((f_local & 1) == 0) {
-        float g = rnd(v), u = rnd(other);
-        b[r * W + (f_local >> 1)] = cvt(__fmul_rn(rnd(silu_ref(g)), u));
+      const int odd = f_local & 1;
+      T* col = b + (f_local >> 1);
+#pragma unroll
+      for (int j = 0; j < CNT; j += 2) {
+        const float recv = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
+        const float g = rnd(odd ? recv : v[j]);
+        const float u = rnd(odd ? v[j + 1] : recv);
+        const int r = r0 + j + odd;
+        if (r < nr) col[r * W] = cvt(__fmul_rn(rnd(silu_ref(g)), u));
       }
-    } else if constexpr (MODE == KVE_EPI_BIAS) {
-      b[r * W + f_local] = cvt(__fadd_rn(v, bias_f));
     } else {
-      b[r * W + f_local] = cvt(v);  // RESIDUAL adds the residual while copying out
+#pragma unroll
+      for (int j = 0; j < CNT; ++j) {
+        const int r = r0 + j;
+        if (r < nr) {
+          if constexpr (MODE == KVE_EPI_BIAS) b[r * W + f_local] = cvt(__fadd_rn(v[j], bias_f));
+          else b[r * W + f_local] = cvt(v[j]);  // RESIDUAL adds the residual while copying out
+        }
+      }
+    }
+  }
+
+  // Residual vectors of rows [0, nr) for copy_out, loaded ahead of the stores so
+  // that all of them are in flight at once (out may alias the residual: each
+  // element is read and then written by the same thread).
+  static constexpr int RPP = 128 / VPR;       // rows per copy_out pass
+  static constexpr int NPASS = kRows / RPP;   // passes per staged chunk
+  static __device__ __forceinline__ void load_res(const TcArgs& a, int tok_base, int nr, int col0, int etid,
+                                                  uint4 (&res)[NPASS]) {
+    if constexpr (MODE == KVE_EPI_RESIDUAL) {
+      const int nvalid = min(W, a.e.ld_out - col0);
+      const int c = (etid % VPR) * VE;
+      const int r_first = etid / VPR;
+      const bool vec = a.out_vec_ok && c + VE <= nvalid;
+      const T* res0 = static_cast<const T*>(a.e.residual) + (size_t)col0 + c;
+#pragma unroll
+      for (int i = 0; i < NPASS; ++i) {
+        const int r = r_first + i * RPP;
+        const int t = tok_base + r;
+        if (vec && r < nr && t < a.m) res[i] = *reinterpret_cast<const uint4*>(res0 + (size_t)t * a.e.ld_out);
+      }
     }
   }
 
   // Write staged rows [0, nr) (tokens tok_base ...) with 16-byte stores. Thread
-  // etid always handles the same column vector; 128 / VPR rows per pass.
+  // etid always handles the same column vector; RPP rows per pass.
   static __device__ __forceinline__ void copy_out(const TcArgs& a, const uint8_t* buf, int tok_base, int nr,
-                                                  int col0, int etid) {
-    constexpr int RPP = 128 / VPR;  // rows per pass
+                                                  int col0, int etid, const uint4 (&res)[NPASS]) {
     const int nvalid = min(W, a.e.ld_out - col0);
     const int c = (etid % VPR) * VE;
     const int r_first = etid / VPR;
@@ -235,18 +272,18 @@ struct Epi {
     const T* src0 = reinterpret_cast<const T*>(buf) + c;
     T* dst0 = static_cast<T*>(a.e.out) + (size_t)col0 + c;
     const T* res0 = static_cast<const T*>(a.e.residual) + (size_t)col0 + c;
-#pragma unroll 4
-    for (int r = r_first; r < nr; r += RPP) {
+#pragma unroll
+    for (int i = 0; i < NPASS; ++i) {
+      const int r = r_first + i * RPP;
       const int t = tok_base + r;
-      if (t >= a.m) break;
+      if (r >= nr || t >= a.m) break;
       const T* src = src0 + r * W;
       T* dst = dst0 + (size_t)t * a.e.ld_out;
       if (vec) {
         uint4 val = *reinterpret_cast<const uint4*>(src);
         if constexpr (MODE == KVE_EPI_RESIDUAL) {
-          uint4 res = *reinterpret_cast<const uint4*>(res0 + (size_t)t * a.e.ld_out);
           T* y = reinterpret_cast<T*>(&val);
-          const T* q = reinterpret_cast<const T*>(&res);
+          const T* q = reinterpret_cast<const T*>(&res[i]);
 #pragma unroll
           for (int j = 0; j < VE; ++j) y[j] = cvt(__fadd_rn((float)q[j], (float)y[j]));
         }
@@ -424,13 +461,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       for (int c0 = 0; c0 < a.mt; c0 += kRows, ++it) {
         const int n = min(kRows, a.mt - c0);
         uint8_t* buf = stg + (it & 1) * kStgBuf;
+        uint4 res[E::NPASS];
+        E::load_res(a, tok0 + c0, n, col0, etid, res);
         float v[32];
         tmem_load_cols(t_lane + c0, n, have, v);
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (j < n) E::stage(buf, j, f_local, v[j], bias_f);
+        E::template stage<32>(buf, 0, n, f_local, v, bias_f);
         epi_bar();
-        E::copy_out(a, buf, tok0 + c0, n, col0, etid);
+        E::copy_out(a, buf, tok0 + c0, n, col0, etid, res);
       }
     }
   } else {
@@ -486,6 +523,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
         for (int t0 = 0; t0 < mine; t0 += kRows, ++it) {
           const int n = min(kRows, mine - t0);
           uint8_t* buf = stg + (it & 1) * kStgBuf;
+          uint4 res[E::NPASS];
+          E::load_res(a, tok0 + r0 + my_lo + t0, n, col0, etid, res);
           for (int j0 = 0; j0 < n; j0 += 4) {
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -496,12 +535,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
                   if (j0 + q < n) acc[q] += src[u][(t0 + j0 + q) * BM];
               }
             }
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              if (j0 + q < n) E::stage(buf, j0 + q, f_local, acc[q], bias_f);
+            E::template stage<4>(buf, j0, n, f_local, acc, bias_f);
           }
           epi_bar();
-          E::copy_out(a, buf, tok0 + r0 + my_lo + t0, n, col0, etid);
+          E::copy_out(a, buf, tok0 + r0 + my_lo + t0, n, col0, etid, res);
         }
         if (etid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         epi_bar();
@@ -556,12 +593,12 @@ int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int box_rows) {
   return KVE_OK;
 }
 
+inline int round16(int x) { return (x + 15) / 16 * 16; }
+
 struct Plan {
   int mt, ng, n_g, token_tiles, feat_tiles, k_blocks, splits, stages, rch, stg_off;
   uint32_t stage_bytes;
 };
-
-inline int round16(int x) { return (x + 15) / 16 * 16; }
 
 typedef void (*GemmKernel)(CUtensorMap, CUtensorMap, TcArgs);
 
@@ -624,18 +661,70 @@ const int* cluster_capacity() {
   return cap;
 }
 
-// Split-K factor: a function of (n, k) only, so a row's reduction order never
-// depends on how many tokens are in the batch. Picks the cluster size that
-// minimises (waves x k-blocks per split + fixed per-CTA cost).
-int choose_splits(int feat_tiles, int k_blocks) {
+// Launch-time model (microseconds) used to pick split-K and token tiling, fitted
+// to B200 measurements of this kernel. One CTA per SM streams k-blocks at a rate
+// set by its stage size (latency x bytes in flight); a cluster exchange costs a
+// fixed part plus a part per token of the CTA's tile.
+double kblock_us(int m_cta) { return 0.1 + (double)(BM + m_cta) * BK * 2 / 130000.0; }
+double exchange_us(int m_cta, int s) { return s > 1 ? 2.5 + 0.25 * s + 0.04 * m_cta : 0.0; }
+double epilogue_us(int m_cta) { return 1.0 + 0.01 * m_cta; }
+
+double model_us(int feat_tiles, int k_blocks, int s, int token_tiles, int m_cta) {
   const int* cap = cluster_capacity();
+  const long long ctas = (long long)feat_tiles * token_tiles * s;
+  const long long waves = (ctas + cap[s] - 1) / cap[s];
+  return waves * (((k_blocks + s - 1) / s) * kblock_us(m_cta) + exchange_us(m_cta, s) + epilogue_us(m_cta));
+}
+
+// Token tiling: tokens are cut into token_tiles tiles of n_g (ng == 1) or
+// 2 x n_g (ng == 2, up to 384 tokens) so that small feature counts still fill the
+// SMs. Splitting tokens never changes a row's reduction order.
+struct TokenTiling {
+  int token_tiles, ng, n_g;
+  double us;
+};
+
+TokenTiling tiling_for(int m, int t) {
+  TokenTiling tt{};
+  const int per = (m + t - 1) / t;
+  tt.token_tiles = t;
+  if (per <= kMaxNG) {
+    tt.ng = 1;
+    tt.n_g = round16(per < 16 ? 16 : per);
+  } else {
+    tt.ng = 2;
+    tt.n_g = round16((per + 1) / 2);
+  }
+  return tt;
+}
+
+// Fewest token tiles that keep every tile within 384 tokens, then more while the
+// model gains clearly.
+TokenTiling best_tiling(int m, int feat_tiles, int k_blocks, int s) {
+  int t_min = (m + 383) / 384;
+  if (t_min < 1) t_min = 1;
+  TokenTiling best = tiling_for(m, t_min);
+  best.us = 1e30;
+  for (int t = t_min; t <= (m + 15) / 16; ++t) {
+    TokenTiling tt = tiling_for(m, t);
+    const int m_cta = tt.ng * tt.n_g;
+    if ((long long)(t - 1) * m_cta >= m) continue;  // an empty trailing tile
+    tt.us = model_us(feat_tiles, k_blocks, s, t, m_cta);
+    if (tt.us < best.us * 0.97) best = tt;
+  }
+  return best;
+}
+
+// Split-K factor: a function of (n, k) only, so a row's reduction order never
+// depends on how many tokens are in the batch. It minimises the modelled time
+// summed over small, medium and large batches, each with its best token tiling.
+int choose_splits(int feat_tiles, int k_blocks) {
   int best = 1;
   double best_t = 1e30;
   for (int s = 1; s <= kMaxSplits; ++s) {
     if (s > 1 && k_blocks / s < 2) break;
-    int ctas = feat_tiles * s;
-    int waves = (ctas + cap[s] - 1) / cap[s];
-    double t = waves * ((k_blocks + s - 1) / s + 3.0);
+    double t = 0;
+    for (int m_ref : {16, 64, 256}) t += best_tiling(m_ref, feat_tiles, k_blocks, s).us;
     if (t < best_t - 1e-9) {
       best_t = t;
       best = s;
@@ -644,23 +733,20 @@ int choose_splits(int feat_tiles, int k_blocks) {
   return best;
 }
 
-Plan make_plan(int m, int n, int k) {
+Plan make_plan_uncached(int m, int n, int k) {
   Plan p{};
   p.feat_tiles = (n + BM - 1) / BM;
   p.k_blocks = (k + BK - 1) / BK;
-  if (m <= kMaxNG) {
-    p.token_tiles = 1; p.ng = 1; p.n_g = round16(m < 16 ? 16 : m);
-  } else if (m <= 384) {
-    p.token_tiles = 1; p.ng = 2; p.n_g = round16((m + 1) / 2);
-  } else {
-    p.token_tiles = (m + kMaxNG - 1) / kMaxNG; p.ng = 1; p.n_g = round16((m + p.token_tiles - 1) / p.token_tiles);
-  }
+  p.splits = choose_splits(p.feat_tiles, p.k_blocks);
+  const TokenTiling tt = best_tiling(m, p.feat_tiles, p.k_blocks, p.splits);
+  p.token_tiles = tt.token_tiles;
+  p.ng = tt.ng;
+  p.n_g = tt.n_g;
   p.mt = p.ng * p.n_g;
   p.stage_bytes = (uint32_t)(BM * BK * 2 + p.mt * BK * 2);
   size_t avail = kSmemLimit - 2048 /*align slack + barriers + margin*/;
   p.stages = (int)(avail / p.stage_bytes);
   if (p.stages > kMaxStages) p.stages = kMaxStages;
-  p.splits = choose_splits(p.feat_tiles, p.k_blocks);
   p.rch = p.mt;
   p.stg_off = 0;
   if (p.splits > 1) {
@@ -678,6 +764,27 @@ Plan make_plan(int m, int n, int k) {
         break;
       }
     }
+  }
+  return p;
+}
+
+// Plans are cached per (m, n, k): a forward pass asks for the same few shapes on
+// every layer.
+Plan make_plan(int m, int n, int k) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, Plan> cache;
+  const bool key_ok = m < (1 << 20) && n < (1 << 24) && k < (1 << 20);
+  const uint64_t key = ((uint64_t)m << 44) | ((uint64_t)n << 20) | (uint64_t)k;
+  if (key_ok) {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  Plan p = make_plan_uncached(m, n, k);
+  if (key_ok) {
+    std::lock_guard<std::mutex> g(mu);
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, p);
   }
   return p;
 }
