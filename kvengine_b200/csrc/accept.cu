@@ -104,6 +104,8 @@ __global__ void __launch_bounds__(kArgmaxThreads)
 accept_kernel(const T* __restrict__ logits, int64_t row_stride, const int32_t* __restrict__ drafts,
               int64_t dsb, int64_t dsj, int k, int vocab, bool vec_ok, int32_t* __restrict__ preds, int32_t* __restrict__ n_acc,
               int32_t* __restrict__ emitted, int32_t* __restrict__ counters) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int row = blockIdx.x;
   const int b = row / (k + 1);
   int best = row_argmax(logits + (size_t)row * row_stride, vocab, vec_ok);
@@ -134,6 +136,8 @@ accept_kernel(const T* __restrict__ logits, int64_t row_stride, const int32_t* _
 template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads)
 argmax_kernel(const T* __restrict__ x, int64_t row_stride, int cols, bool vec_ok, int32_t* __restrict__ out) {
+  grid_dep_wait();
+  grid_dep_launch();
   int best = row_argmax(x + (size_t)blockIdx.x * row_stride, cols, vec_ok);
   if (threadIdx.x == 0) out[blockIdx.x] = best;
 }
@@ -170,11 +174,11 @@ extern "C" int kve_greedy_accept(const void* logits, int dtype, int64_t row_stri
   dim3 grid(batch * (k + 1));
   int32_t* counters = static_cast<int32_t*>(workspace);
   if (dtype == KVE_F32) {
-    accept_kernel<float><<<grid, kArgmaxThreads, 0, stream>>>(
+    launch_kernel(accept_kernel<float>, dim3(grid), dim3(kArgmaxThreads), 0, stream,
         static_cast<const float*>(logits), row_stride, drafts, draft_stride_b, draft_stride_j, k, vocab,
         vec_aligned(logits, row_stride, 4), out_preds, out_n_accepted, out_emitted, counters);
   } else if (dtype == KVE_BF16) {
-    accept_kernel<__nv_bfloat16><<<grid, kArgmaxThreads, 0, stream>>>(
+    launch_kernel(accept_kernel<__nv_bfloat16>, dim3(grid), dim3(kArgmaxThreads), 0, stream,
         static_cast<const __nv_bfloat16*>(logits), row_stride, drafts, draft_stride_b, draft_stride_j, k, vocab,
         vec_aligned(logits, row_stride, 2), out_preds, out_n_accepted, out_emitted, counters);
   } else {
@@ -190,10 +194,10 @@ extern "C" int kve_argmax_rows(const void* x, int dtype, int rows, int cols, int
   if (rows == 0) return KVE_OK;
   if (!x || !out) return set_error(KVE_ERR_ARG, "kve_argmax_rows: null pointer");
   if (dtype == KVE_F32) {
-    argmax_kernel<float><<<rows, kArgmaxThreads, 0, stream>>>(
+    launch_kernel(argmax_kernel<float>, dim3(rows), dim3(kArgmaxThreads), 0, stream,
         static_cast<const float*>(x), row_stride, cols, vec_aligned(x, row_stride, 4), out);
   } else if (dtype == KVE_BF16) {
-    argmax_kernel<__nv_bfloat16><<<rows, kArgmaxThreads, 0, stream>>>(
+    launch_kernel(argmax_kernel<__nv_bfloat16>, dim3(rows), dim3(kArgmaxThreads), 0, stream,
         static_cast<const __nv_bfloat16*>(x), row_stride, cols, vec_aligned(x, row_stride, 2), out);
   } else {
     return set_error(KVE_ERR_DTYPE, "kve_argmax_rows: dtype %d", dtype);

@@ -51,6 +51,8 @@ __host__ __device__ inline size_t partial_floats(int hd) { return (size_t)kMaxRo
 template <typename T, int HD>
 __global__ void __launch_bounds__(kAttnThreads)
 paged_attn_kernel(AttnParams p) {
+  grid_dep_wait();
+  grid_dep_launch();
   constexpr int DPL = HD / 32;  // output dims per lane
   constexpr int VEC = 16 / sizeof(T);
   constexpr int VPR = HD / VEC;  // 16-byte vectors per key row
@@ -220,6 +222,8 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
 template <int HD, int BS>
 __global__ void __launch_bounds__(kAttnThreads)
 paged_attn_mma_kernel(AttnParams p) {
+  grid_dep_wait();
+  grid_dep_launch();
   constexpr int ROW = HD * 2 + 16;             // padded smem row (bytes)
   constexpr int TILE = kMmaKeyTile * ROW;      // one K or V tile
   constexpr int KSTEPS = HD / 16;              // k16 steps over the head dim
@@ -474,6 +478,8 @@ paged_attn_mma_kernel(AttnParams p) {
 template <typename T, int HD>
 __global__ void __launch_bounds__(kAttnThreads)
 attn_combine_kernel(AttnParams p) {
+  grid_dep_wait();
+  grid_dep_launch();
   constexpr int DPL = HD / 32;
   const int bh = blockIdx.x, qtile = blockIdx.y;
   const int b = bh / p.nkv, h = bh % p.nkv;
@@ -520,19 +526,19 @@ int launch(AttnParams& p, int batch, cudaStream_t stream) {
       cudaFuncSetAttribute(paged_attn_mma_kernel<HD, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       cudaFuncSetAttribute(paged_attn_mma_kernel<HD, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     });
-    if (p.bs == 16) paged_attn_mma_kernel<HD, 16><<<grid, kAttnThreads, smem, stream>>>(p);
-    else paged_attn_mma_kernel<HD, 0><<<grid, kAttnThreads, smem, stream>>>(p);
+    if (p.bs == 16) launch_kernel(paged_attn_mma_kernel<HD, 16>, dim3(grid), dim3(kAttnThreads), smem, stream, p);
+    else launch_kernel(paged_attn_mma_kernel<HD, 0>, dim3(grid), dim3(kAttnThreads), smem, stream, p);
   } else {
     const size_t smem = sizeof(float) * ((size_t)kMaxRows * HD + kKeyTile * (HD + 1) + kKeyTile * HD);
     static std::once_flag once;
     std::call_once(once, [smem] {
       cudaFuncSetAttribute(paged_attn_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     });
-    paged_attn_kernel<T, HD><<<grid, kAttnThreads, smem, stream>>>(p);
+    launch_kernel(paged_attn_kernel<T, HD>, dim3(grid), dim3(kAttnThreads), smem, stream, p);
   }
   int rc = check_launch("kve_paged_verify_attn");
   if (rc || !p.ws) return rc;
-  attn_combine_kernel<T, HD><<<dim3(batch * p.nkv, p.n_qtiles), kAttnThreads, 0, stream>>>(p);
+  launch_kernel(attn_combine_kernel<T, HD>, dim3(batch * p.nkv, p.n_qtiles), dim3(kAttnThreads), 0, stream, p);
   return check_launch("kve_paged_verify_attn(combine)");
 }
 

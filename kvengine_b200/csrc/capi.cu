@@ -2,6 +2,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 
 #include "kve_common.cuh"
 
@@ -20,6 +21,14 @@ int set_error(int code, const char* fmt, ...) {
 static std::atomic<unsigned long long> g_launches{0};
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("KVE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 }  // namespace kve
 

@@ -19,6 +19,8 @@ constexpr int kThreads = 256;
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 gemm_simt_kernel(const T* __restrict__ x, const T* __restrict__ w, int m, int n, int k, EpiArgs e) {
+  grid_dep_wait();
+  grid_dep_launch();
   __shared__ float xs[BK][BM + 4];
   __shared__ float ws[BK][BN + 4];
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
@@ -77,10 +79,10 @@ int gemm_simt(const void* x, const void* w, int dtype, int m, int n, int k, cons
               cudaStream_t stream) {
   dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM);
   if (dtype == KVE_F32) {
-    gemm_simt_kernel<float><<<grid, kThreads, 0, stream>>>(static_cast<const float*>(x),
+    launch_kernel(gemm_simt_kernel<float>, dim3(grid), dim3(kThreads), 0, stream, static_cast<const float*>(x),
                                                            static_cast<const float*>(w), m, n, k, e);
   } else if (dtype == KVE_BF16) {
-    gemm_simt_kernel<__nv_bfloat16><<<grid, kThreads, 0, stream>>>(
+    launch_kernel(gemm_simt_kernel<__nv_bfloat16>, dim3(grid), dim3(kThreads), 0, stream,
         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), m, n, k, e);
   } else {
     return set_error(KVE_ERR_DTYPE, "kve_gemm: dtype %d", dtype);

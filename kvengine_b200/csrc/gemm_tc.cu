@@ -335,10 +335,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   const int split = blockIdx.z;
   const int kb0 = (int)((long long)split * a.k_blocks / a.splits);
   const int kb1 = (int)((long long)(split + 1) * a.k_blocks / a.splits);
-  // After a timeout anywhere in this launch, later CTAs skip their work instead
-  // of each waiting out the limit again.
-  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
-  const int n_iter = aborted ? 0 : kb1 - kb0;
   uint32_t tmem_cols = 32;
   while ((int)tmem_cols < a.mt) tmem_cols <<= 1;
 
@@ -363,6 +359,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   __syncthreads();
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touched only this CTA's shared memory and TMEM; global
+  // memory is read and written only after the previous kernel has completed.
+  grid_dep_wait();
+  grid_dep_launch();
+  // After a timeout anywhere in this launch, later CTAs skip their work instead
+  // of each waiting out the limit again.
+  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
+  const int n_iter = aborted ? 0 : kb1 - kb0;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -816,19 +820,14 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   if (rc) return rc;
   rc = make_map(&mx, x, m, k, p.n_g);
   if (rc) return rc;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.token_tiles, p.feat_tiles, p.splits);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = (size_t)p.stages * p.stage_bytes + 1024 + 512;
-  cfg.stream = stream;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
   attr.val.clusterDim.x = 1;
   attr.val.clusterDim.y = 1;
   attr.val.clusterDim.z = p.splits;
-  cfg.attrs = &attr;
-  cfg.numAttrs = p.splits > 1 ? 1 : 0;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel_for(e.mode, e.out_dtype, p.ng), mw, mx, a);
+  cudaError_t err = launch_kernel_ex(kernel_for(e.mode, e.out_dtype, p.ng), dim3(p.token_tiles, p.feat_tiles, p.splits),
+                                     dim3(kThreads), (size_t)p.stages * p.stage_bytes + 1024 + 512, stream, &attr,
+                                     p.splits > 1 ? 1 : 0, mw, mx, a);
   if (err != cudaSuccess) {
     cudaGetLastError();
     count_launch();

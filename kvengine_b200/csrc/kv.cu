@@ -14,6 +14,8 @@ __global__ void kv_append_kernel(const uint4* __restrict__ k_new, const uint4* _
                                  const int64_t* __restrict__ slots, int n_tokens, int chunks_per_row,
                                  uint4* __restrict__ pool_k, uint4* __restrict__ pool_v,
                                  int64_t num_slots, int* status) {
+  grid_dep_wait();
+  grid_dep_launch();
   int64_t total = (int64_t)n_tokens * chunks_per_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < 2 * total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -51,6 +53,8 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int nq, int nk
                                        const float* __restrict__ rope_sin, int rope_len,
                                        T* __restrict__ q_out, T* __restrict__ pool_k,
                                        T* __restrict__ pool_v, int64_t num_slots, int* status) {
+  grid_dep_wait();
+  grid_dep_launch();
   const int t = blockIdx.x;
   const int half = hd / 2;
   const int width = (nq + 2 * nkv) * hd;
@@ -94,6 +98,8 @@ template <typename T>
 __global__ void gather_kv_kernel(const T* __restrict__ pool, const int32_t* __restrict__ table, int length,
                                  int nkv, int hd, int bs, int64_t num_blocks, T* __restrict__ out,
                                  int* status) {
+  grid_dep_wait();
+  grid_dep_launch();
   int64_t total = (int64_t)nkv * length * hd;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -111,6 +117,8 @@ __global__ void gather_kv_kernel(const T* __restrict__ pool, const int32_t* __re
 template <typename T>
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restrict__ table, int hidden,
                              int vocab, T* __restrict__ out, int* status) {
+  grid_dep_wait();
+  grid_dep_launch();
   int t = blockIdx.x;
   int id = ids[t];
   bool ok = id >= 0 && id < vocab;
@@ -130,6 +138,8 @@ template <typename T>
 __global__ void __launch_bounds__(kNormThreads)
 rmsnorm_kernel(const T* __restrict__ x, const float* __restrict__ w, int hidden, float eps,
                const int32_t* __restrict__ row_index, T* __restrict__ out) {
+  grid_dep_wait();
+  grid_dep_launch();
   int r = blockIdx.x;
   int src_row = row_index ? row_index[r] : r;
   const T* xr = x + (size_t)src_row * hidden;
@@ -187,7 +197,7 @@ extern "C" int kve_kv_append(const void* k_new, const void* v_new, int dtype, co
     if ((uintptr_t)p % 16) return set_error(KVE_ERR_ARG, "kve_kv_append: pointers must be 16-byte aligned");
   int cpr = (int)(row_bytes / 16);
   int threads = 256;
-  kv_append_kernel<<<grid_for(2LL * n_tokens * cpr, threads), threads, 0, stream>>>(
+  launch_kernel(kv_append_kernel, dim3(grid_for(2LL * n_tokens * cpr, threads)), dim3(threads), 0, stream,
       static_cast<const uint4*>(k_new), static_cast<const uint4*>(v_new), slot_ids, n_tokens, cpr,
       static_cast<uint4*>(pool_k), static_cast<uint4*>(pool_v), num_slots, dev_status);
   return check_launch("kve_kv_append");
@@ -206,12 +216,12 @@ extern "C" int kve_qkv_rope_append(const void* qkv, int dtype, int n_tokens, int
     return set_error(KVE_ERR_ARG, "kve_qkv_rope_append: null pointer");
   int threads = 128;
   if (dtype == KVE_F32) {
-    qkv_rope_append_kernel<float><<<n_tokens, threads, 0, stream>>>(
+    launch_kernel(qkv_rope_append_kernel<float>, dim3(n_tokens), dim3(threads), 0, stream,
         static_cast<const float*>(qkv), num_heads, num_kv_heads, head_dim, positions, slots, rope_cos,
         rope_sin, rope_len, static_cast<float*>(q_out), static_cast<float*>(pool_k),
         static_cast<float*>(pool_v), num_slots, dev_status);
   } else if (dtype == KVE_BF16) {
-    qkv_rope_append_kernel<__nv_bfloat16><<<n_tokens, threads, 0, stream>>>(
+    launch_kernel(qkv_rope_append_kernel<__nv_bfloat16>, dim3(n_tokens), dim3(threads), 0, stream,
         static_cast<const __nv_bfloat16*>(qkv), num_heads, num_kv_heads, head_dim, positions, slots,
         rope_cos, rope_sin, rope_len, static_cast<__nv_bfloat16*>(q_out),
         static_cast<__nv_bfloat16*>(pool_k), static_cast<__nv_bfloat16*>(pool_v), num_slots, dev_status);
@@ -230,11 +240,11 @@ extern "C" int kve_gather_kv(const void* pool, int dtype, const int32_t* block_t
   if (!pool || !block_table || !out) return set_error(KVE_ERR_ARG, "kve_gather_kv: null pointer");
   int64_t work = (int64_t)num_kv_heads * length * head_dim;
   if (dtype == KVE_F32) {
-    gather_kv_kernel<float><<<grid_for(work, 256), 256, 0, stream>>>(
+    launch_kernel(gather_kv_kernel<float>, dim3(grid_for(work, 256)), dim3(256), 0, stream,
         static_cast<const float*>(pool), block_table, length, num_kv_heads, head_dim, block_size,
         num_blocks, static_cast<float*>(out), dev_status);
   } else if (dtype == KVE_BF16) {
-    gather_kv_kernel<__nv_bfloat16><<<grid_for(work, 256), 256, 0, stream>>>(
+    launch_kernel(gather_kv_kernel<__nv_bfloat16>, dim3(grid_for(work, 256)), dim3(256), 0, stream,
         static_cast<const __nv_bfloat16*>(pool), block_table, length, num_kv_heads, head_dim,
         block_size, num_blocks, static_cast<__nv_bfloat16*>(out), dev_status);
   } else {
@@ -249,10 +259,10 @@ extern "C" int kve_embed(const int32_t* ids, int n_tokens, const void* table, in
   if (n_tokens == 0) return KVE_OK;
   if (!ids || !table || !out) return set_error(KVE_ERR_ARG, "kve_embed: null pointer");
   if (dtype == KVE_F32) {
-    embed_kernel<float><<<n_tokens, 256, 0, stream>>>(ids, static_cast<const float*>(table), hidden,
+    launch_kernel(embed_kernel<float>, dim3(n_tokens), dim3(256), 0, stream, ids, static_cast<const float*>(table), hidden,
                                                       vocab, static_cast<float*>(out), dev_status);
   } else if (dtype == KVE_BF16) {
-    embed_kernel<__nv_bfloat16><<<n_tokens, 256, 0, stream>>>(
+    launch_kernel(embed_kernel<__nv_bfloat16>, dim3(n_tokens), dim3(256), 0, stream,
         ids, static_cast<const __nv_bfloat16*>(table), hidden, vocab, static_cast<__nv_bfloat16*>(out),
         dev_status);
   } else {
@@ -267,10 +277,10 @@ extern "C" int kve_rmsnorm(const void* x, int dtype, const float* weight, int ro
   if (rows == 0) return KVE_OK;
   if (!x || !weight || !out) return set_error(KVE_ERR_ARG, "kve_rmsnorm: null pointer");
   if (dtype == KVE_F32) {
-    rmsnorm_kernel<float><<<rows, kNormThreads, 0, stream>>>(
+    launch_kernel(rmsnorm_kernel<float>, dim3(rows), dim3(kNormThreads), 0, stream,
         static_cast<const float*>(x), weight, hidden, eps, row_index, static_cast<float*>(out));
   } else if (dtype == KVE_BF16) {
-    rmsnorm_kernel<__nv_bfloat16><<<rows, kNormThreads, 0, stream>>>(
+    launch_kernel(rmsnorm_kernel<__nv_bfloat16>, dim3(rows), dim3(kNormThreads), 0, stream,
         static_cast<const __nv_bfloat16*>(x), weight, hidden, eps, row_index,
         static_cast<__nv_bfloat16*>(out));
   } else {

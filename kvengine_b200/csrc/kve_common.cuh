@@ -7,6 +7,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/kvengine_b200.h"
 
 namespace kve {
@@ -62,5 +64,46 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // Every spin-wait in this library gives up after this long and reports
 // KVE_ERR_TIMEOUT instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Programmatic dependent launch. Kernels of this library are launched so that
+// the next kernel in the stream may be scheduled, and run its prologue, while
+// this one drains. The contract every kernel keeps: grid_dep_wait() comes before
+// its first global-memory access, read or write (it returns once the kernels
+// before it in the stream have completed and their writes are visible), and
+// grid_dep_launch() follows it. Both are no-ops for a plain launch.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Dependent launches are on unless KVE_PDL=0 is set in the environment.
+bool pdl_enabled();
+
+// Launch with the programmatic-stream-serialization attribute (plus any extra
+// attributes, e.g. a cluster shape).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             const cudaLaunchAttribute* extra, int n_extra, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[4];
+  int n = 0;
+  for (int i = 0; i < n_extra && n < 3; ++i) attrs[n++] = extra[i];
+  if (pdl_enabled()) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  return launch_kernel_ex(kernel, grid, block, smem, stream, nullptr, 0, std::forward<Args>(args)...);
+}
 
 }  // namespace kve
