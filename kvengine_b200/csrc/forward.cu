@@ -1,6 +1,7 @@
 // kve_forward: the launch sequence of one model pass over a ragged batch.
-// Host code only; every kernel it launches is one of the library's entry points.
-#include "kve_common.cuh"
+// Host code only; every kernel it launches is one of the library's entry points (the GEMMs
+// through gemm_run, which may request the constant weights before the previous kernel ends).
+#include "gemm_epilogue.cuh"
 
 namespace {
 
@@ -51,8 +52,8 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
   for (int l = 0; l < m->num_layers; ++l) {
     const kve_layer_t& L = m->layers[l];
     KVE_TRY(kve_rmsnorm(s->hidden, dt, L.ln1, M, H, m->rms_eps, nullptr, s->normed, stream));
-    KVE_TRY(kve_gemm(s->normed, L.w_qkv, dt, M, qkv, H, KVE_EPI_BIAS, L.b_qkv, nullptr, s->qkv, dt,
-                     s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
+    KVE_TRY(gemm_run(s->normed, L.w_qkv, dt, M, qkv, H, KVE_EPI_BIAS, L.b_qkv, nullptr, s->qkv, dt,
+                     s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
     KVE_TRY(kve_qkv_rope_append(s->qkv, dt, M, m->num_heads, m->num_kv_heads, m->head_dim, b->positions,
                                 b->slots, m->rope_cos, m->rope_sin, m->rope_len, s->q, L.pool_k, L.pool_v,
                                 num_slots, s->dev_status, stream));
@@ -60,17 +61,17 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
                                   b->q_lens, b->q_offsets, b->n_seqs, b->max_q_len, b->max_ctx, m->num_heads,
                                   m->num_kv_heads, m->head_dim, m->block_size, m->num_blocks, scale, s->attn,
                                   s->attn_ws, s->attn_ws_bytes, s->dev_status, stream));
-    KVE_TRY(kve_gemm(s->attn, L.w_o, dt, M, H, qsz, KVE_EPI_RESIDUAL, nullptr, s->hidden, s->hidden, dt,
-                     s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
+    KVE_TRY(gemm_run(s->attn, L.w_o, dt, M, H, qsz, KVE_EPI_RESIDUAL, nullptr, s->hidden, s->hidden, dt,
+                     s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
     KVE_TRY(kve_rmsnorm(s->hidden, dt, L.ln2, M, H, m->rms_eps, nullptr, s->normed, stream));
-    KVE_TRY(kve_gemm(s->normed, L.w_gu, dt, M, 2 * m->intermediate, H, KVE_EPI_SILU_MUL, nullptr, nullptr,
-                     s->act, dt, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
-    KVE_TRY(kve_gemm(s->act, L.w_down, dt, M, H, m->intermediate, KVE_EPI_RESIDUAL, nullptr, s->hidden,
-                     s->hidden, dt, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
+    KVE_TRY(gemm_run(s->normed, L.w_gu, dt, M, 2 * m->intermediate, H, KVE_EPI_SILU_MUL, nullptr, nullptr,
+                     s->act, dt, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
+    KVE_TRY(gemm_run(s->act, L.w_down, dt, M, H, m->intermediate, KVE_EPI_RESIDUAL, nullptr, s->hidden,
+                     s->hidden, dt, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
   }
   if (b->n_out == 0) return KVE_OK;
   KVE_TRY(kve_rmsnorm(s->hidden, dt, m->final_norm, b->n_out, H, m->rms_eps, b->out_rows, s->out_normed, stream));
-  KVE_TRY(kve_gemm(s->out_normed, m->lm_head, dt, b->n_out, m->vocab, H, KVE_EPI_STORE, nullptr, nullptr,
-                   b->logits, b->logits_dtype, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, stream));
+  KVE_TRY(gemm_run(s->out_normed, m->lm_head, dt, b->n_out, m->vocab, H, KVE_EPI_STORE, nullptr, nullptr,
+                   b->logits, b->logits_dtype, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
   return KVE_OK;
 }

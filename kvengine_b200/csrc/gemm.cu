@@ -9,10 +9,11 @@ extern "C" size_t kve_gemm_workspace_bytes(int m, int n, int k, int dtype) {
   return gemm_tc_workspace_bytes(m, n, k);
 }
 
-extern "C" int kve_gemm_ex(const void* x, const void* w, int dtype, int m, int n, int k, int epilogue,
-                           const float* bias, const void* residual, void* out, int out_dtype,
-                           void* workspace, size_t workspace_bytes, int* dev_status, int algo,
-                           cudaStream_t stream) {
+namespace kve {
+
+int gemm_run(const void* x, const void* w, int dtype, int m, int n, int k, int epilogue, const float* bias,
+             const void* residual, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+             int* dev_status, int algo, bool w_static, cudaStream_t stream) {
   if (m < 0 || n < 1 || k < 1) return set_error(KVE_ERR_ARG, "kve_gemm: bad sizes m=%d n=%d k=%d", m, n, k);
   if (m == 0) return KVE_OK;
   if (!x || !w || !out) return set_error(KVE_ERR_ARG, "kve_gemm: null pointer");
@@ -31,6 +32,7 @@ extern "C" int kve_gemm_ex(const void* x, const void* w, int dtype, int m, int n
   e.bias = bias;
   e.residual = residual;
   e.out = out;
+  e.w_static = w_static ? 1 : 0;
   if (algo == KVE_GEMM_AUTO) algo = dtype == KVE_BF16 ? KVE_GEMM_TCGEN05 : KVE_GEMM_SIMT;
   if (algo == KVE_GEMM_TCGEN05) {
     if (dtype != KVE_BF16) return set_error(KVE_ERR_DTYPE, "kve_gemm: tcgen05 path takes bf16 inputs");
@@ -38,6 +40,16 @@ extern "C" int kve_gemm_ex(const void* x, const void* w, int dtype, int m, int n
   }
   if (algo == KVE_GEMM_SIMT) return gemm_simt(x, w, dtype, m, n, k, e, stream);
   return set_error(KVE_ERR_ARG, "kve_gemm: algo %d", algo);
+}
+
+}  // namespace kve
+
+extern "C" int kve_gemm_ex(const void* x, const void* w, int dtype, int m, int n, int k, int epilogue,
+                           const float* bias, const void* residual, void* out, int out_dtype,
+                           void* workspace, size_t workspace_bytes, int* dev_status, int algo,
+                           cudaStream_t stream) {
+  return gemm_run(x, w, dtype, m, n, k, epilogue, bias, residual, out, out_dtype, workspace, workspace_bytes,
+                  dev_status, algo, false, stream);
 }
 
 extern "C" int kve_gemm(const void* x, const void* w, int dtype, int m, int n, int k, int epilogue,

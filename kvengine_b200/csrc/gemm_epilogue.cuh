@@ -17,6 +17,7 @@ struct EpiArgs {
   const float* bias;  // [n] (BIAS)
   const void* residual;  // [m, n] in out_dtype (RESIDUAL); may alias out
   void* out;
+  int w_static;       // w is written by no kernel that may still run: its loads may start early
 };
 
 __device__ __forceinline__ float round_to(int dtype, float v) {
@@ -61,5 +62,10 @@ int gemm_simt(const void* x, const void* w, int dtype, int m, int n, int k, cons
 int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e, void* workspace,
             size_t workspace_bytes, int* status, cudaStream_t stream);
 size_t gemm_tc_workspace_bytes(int m, int n, int k);
+
+// kve_gemm_ex with the weight-is-constant hint (model weights in kve_forward).
+int gemm_run(const void* x, const void* w, int dtype, int m, int n, int k, int epilogue, const float* bias,
+             const void* residual, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+             int* dev_status, int algo, bool w_static, cudaStream_t stream);
 
 }  // namespace kve

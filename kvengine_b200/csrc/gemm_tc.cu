@@ -37,7 +37,8 @@ namespace {
 constexpr int BM = 128;          // features per tile (MMA M)
 constexpr int BK = 64;           // K per stage: one 128-byte swizzle row of bf16
 constexpr int UMMA_K = 16;       // K per tcgen05.mma for 16-bit inputs
-constexpr int kThreads = 192;    // 6 warps
+constexpr int kEpiGroups = 2;    // epilogue warpgroups (each covers all 128 TMEM lanes)
+constexpr int kThreads = 64 + 128 * kEpiGroups;  // producer warp, MMA warp, epilogue warps
 constexpr int kMaxNG = 256;      // tokens per MMA (N of one tcgen05.mma)
 constexpr int kMaxStages = 8;
 constexpr int kMaxSplits = 8;    // portable cluster size
@@ -53,6 +54,7 @@ struct TcArgs {
   int rch;               // split-K: tokens reduced per round (the receive buffer holds rch tokens)
   int stg_off;           // byte offset of the output staging buffer in the drained stage area
   int out_vec_ok;        // output rows start on 16-byte boundaries
+  int w_static;          // weight tiles may be requested before the previous kernel completes
   EpiArgs e;
   int* status;
 };
@@ -67,6 +69,15 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Raise the expected transaction bytes of the current phase without arriving.
+__device__ __forceinline__ void mbar_add_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -151,7 +162,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of one epilogue warpgroup (ids 1 and up; 0 is __syncthreads).
+__device__ __forceinline__ void epi_bar(int group) { asm volatile("bar.sync %0, 128;" ::"r"(group + 1) : "memory"); }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -344,7 +356,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       mbar_init(smem_u32(&empty[s]), 1);
     }
     mbar_init(smem_u32(tmem_full), 1);
-    mbar_init(smem_u32(epi_done), 4);  // one arrival per epilogue warp
+    mbar_init(smem_u32(epi_done), 4 * kEpiGroups);  // one arrival per epilogue warp
     mbar_init(smem_u32(recv_bar), 1);  // this CTA's expect-tx arrival per split-K round
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -359,8 +371,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   __syncthreads();
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Everything above touched only this CTA's shared memory and TMEM; global
-  // memory is read and written only after the previous kernel has completed.
+  // Weights no kernel writes (w_static): the first stages' weight tiles are
+  // requested before waiting on the previous kernel, so their latency overlaps
+  // its tail. Their full barriers expect the bytes now and get the arrival (with
+  // the activation bytes) once the activations may be read.
+  const int pre = a.w_static ? min(kb1 - kb0, a.stages) : 0;
+  if (warp == 0 && lane == 0) {
+    prefetch_map(&map_w);
+    prefetch_map(&map_x);
+    uint8_t* sa = smem;
+    for (int it = 0; it < pre; ++it, sa += a.stage_bytes) {
+      const uint32_t fb = smem_u32(&full[it]);
+      mbar_add_tx(fb, BM * BK * 2);
+      tma_load_2d(smem_u32(sa), &map_w, (kb0 + it) * BK, feat0, fb);
+    }
+  }
+  // Everything else touches global memory only after the previous kernel has
+  // completed.
   grid_dep_wait();
   grid_dep_launch();
   // After a timeout anywhere in this launch, later CTAs skip their work instead
@@ -378,8 +405,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       for (int it = 0; it < n_iter; ++it) {
         if (it >= a.stages && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, a.status)) break;
         const uint32_t fb = smem_u32(&full[s]);
-        mbar_expect_tx(fb, a.stage_bytes);
-        tma_load_2d(smem_u32(sa), &map_w, kx, feat0, fb);
+        if (it < pre) {
+          mbar_expect_tx(fb, a.stage_bytes - BM * BK * 2);  // weight tile already requested
+        } else {
+          mbar_expect_tx(fb, a.stage_bytes);
+          tma_load_2d(smem_u32(sa), &map_w, kx, feat0, fb);
+        }
         uint8_t* sb = sa + BM * BK * 2;
         tma_load_2d(smem_u32(sb), &map_x, kx, tok0, fb);
         if (NG == 2) tma_load_2d(smem_u32(sb + a.n_g * BK * 2), &map_x, kx, tok0 + a.n_g, fb);
@@ -393,6 +424,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
           sa += a.stage_bytes;
         }
       }
+      // Early weight loads of stages the loop never reached (abort): arrive so
+      // their phase completes once those bytes land.
+      for (int it = issued; it < pre; ++it) mbar_arrive(smem_u32(&full[it]));
+      if (issued < pre) issued = pre;
       // Do not leave while a bulk copy may still be writing this CTA's shared memory.
       for (int it = issued - a.stages < 0 ? 0 : issued - a.stages; it < issued; ++it)
         mbar_wait(smem_u32(&full[it % a.stages]), (uint32_t)(it / a.stages) & 1u, a.status);
@@ -440,16 +475,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   }
 
   // ---------------------------------------------------------------- epilogue
-  // Warps 2-5 own TMEM lane quarters (warp w reads lanes 32*(w%4) ...), i.e.
-  // feature rows; tokens are TMEM columns. Output is staged 32 tokens at a time
-  // in a dense [32][W] buffer (double-buffered) and written as whole rows.
+  // Epilogue warps 2.. own TMEM lane quarters (warp w reads lanes 32*(w%4) ...),
+  // i.e. feature rows; tokens are TMEM columns. Each warpgroup takes every
+  // kEpiGroups-th chunk of 32 tokens, stages it in a dense [32][W] buffer of its
+  // own (double-buffered) and writes it as whole rows.
   const bool epi = warp >= 2;
+  const int egrp = epi ? (warp - 2) / 4 : 0;
   const int quad = warp & 3;
   const int f_local = quad * 32 + lane;
   const int feat = feat0 + f_local;
   const int col0 = MODE == KVE_EPI_SILU_MUL ? feat0 / 2 : feat0;
   const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);
-  const int etid = threadIdx.x - 64;
+  const int etid = (threadIdx.x - 64) & 127;  // thread index within its warpgroup
   const float bias_f = (MODE == KVE_EPI_BIAS && epi && feat < a.n) ? a.e.bias[feat] : 0.f;
   bool have = false;
   if (epi) {
@@ -462,15 +499,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   if (S == 1) {
     if (epi) {
       int it = 0;
-      for (int c0 = 0; c0 < a.mt; c0 += kRows, ++it) {
+      for (int c0 = egrp * kRows; c0 < a.mt; c0 += kEpiGroups * kRows, ++it) {
         const int n = min(kRows, a.mt - c0);
-        uint8_t* buf = stg + (it & 1) * kStgBuf;
+        uint8_t* buf = stg + (egrp * 2 + (it & 1)) * kStgBuf;
         uint4 res[E::NPASS];
         E::load_res(a, tok0 + c0, n, col0, etid, res);
         float v[32];
         tmem_load_cols(t_lane + c0, n, have, v);
         E::template stage<32>(buf, 0, n, f_local, v, bias_f);
-        epi_bar();
+        epi_bar(egrp);
         E::copy_out(a, buf, tok0 + c0, n, col0, etid, res);
       }
     }
@@ -490,7 +527,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       // the cluster has finished its main loop (and, in later rounds, its reads).
       cluster_sync();
       const int my_lo = (int)((long long)rank * ch / S), my_hi = (int)((long long)(rank + 1) * ch / S);
-      if (epi) {
+      if (epi && egrp == 0) {
         // Owner u's tokens [lo_u, hi_u) are contiguous rows of pout.
         float* prow = pout + f_local;
         for (int c = 0; c < ch; c += kRows) {
@@ -502,7 +539,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
             if (j < n) prow[(c + j) * BM] = v[j];
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        epi_bar();
+        epi_bar(0);
         if (etid == 0) {
           const uint32_t mine = (uint32_t)(my_hi - my_lo);
           mbar_expect_tx(smem_u32(recv_bar), (uint32_t)(S - 1) * mine * BM * 4);
@@ -541,11 +578,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
             }
             E::template stage<4>(buf, j0, n, f_local, acc, bias_f);
           }
-          epi_bar();
+          epi_bar(0);
           E::copy_out(a, buf, tok0 + r0 + my_lo + t0, n, col0, etid, res);
         }
         if (etid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-        epi_bar();
+        epi_bar(0);
       }
     }
   }
@@ -812,6 +849,7 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   a.m = m; a.n = n; a.k = k; a.mt = p.mt; a.ng = p.ng; a.n_g = p.n_g; a.k_blocks = p.k_blocks;
   a.splits = p.splits; a.stages = p.stages; a.stage_bytes = p.stage_bytes; a.e = e; a.status = status;
   a.rch = p.rch; a.stg_off = p.stg_off;
+  a.w_static = e.w_static;
   const int es = e.out_dtype == KVE_BF16 ? 2 : 4;
   a.out_vec_ok = ((uintptr_t)e.out % 16 == 0) && ((size_t)e.ld_out * es % 16 == 0) &&
                  (e.mode != KVE_EPI_RESIDUAL || (uintptr_t)e.residual % 16 == 0);

@@ -68,9 +68,11 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 // Programmatic dependent launch. Kernels of this library are launched so that
 // the next kernel in the stream may be scheduled, and run its prologue, while
 // this one drains. The contract every kernel keeps: grid_dep_wait() comes before
-// its first global-memory access, read or write (it returns once the kernels
-// before it in the stream have completed and their writes are visible), and
-// grid_dep_launch() follows it. Both are no-ops for a plain launch.
+// its first access, read or write, to global memory that an earlier kernel may
+// write (it returns once the kernels before it in the stream have completed and
+// their writes are visible); only inputs declared constant, such as model
+// weights in kve_forward, are read before it. grid_dep_launch() follows it.
+// Both are no-ops for a plain launch.
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
