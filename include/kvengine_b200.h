@@ -71,6 +71,23 @@ int kve_greedy_accept(const void* logits, int dtype, int64_t row_stride, const i
                       int32_t* out_preds, int32_t* out_n_accepted, int32_t* out_emitted,
                       void* workspace, size_t workspace_bytes, int* dev_status, cudaStream_t stream);
 
+/* Allocation-free variant of kve_greedy_accept: same arguments and results,
+ * minus the workspace. It has no counterpart in kvengine; it exists for callers
+ * that cannot allocate device memory at the call site (plain C/FFI hosts without
+ * a device allocator, code inside a CUDA-graph capture, fixed-budget serving
+ * loops). Its per-sequence counters live in a static device array of
+ * kve_greedy_accept_noalloc_max_batch() entries (4096); a larger batch returns
+ * KVE_ERR_ARG without launching. The array starts at zero and every completed
+ * call leaves it at zero. All calls on one device share it, so calls must not
+ * overlap in time (keep them on one stream). The array's device address is
+ * looked up on the first call on each device; make that first call outside a
+ * stream capture. */
+int kve_greedy_accept_noalloc_max_batch(void);
+int kve_greedy_accept_noalloc(const void* logits, int dtype, int64_t row_stride, const int32_t* drafts,
+                              int64_t draft_stride_b, int64_t draft_stride_j, int batch, int k, int vocab,
+                              int32_t* out_preds, int32_t* out_n_accepted, int32_t* out_emitted,
+                              cudaStream_t stream);
+
 /* Row argmax. Replaces the draft's `int(torch.argmax(logits[-1]))`
  * (kvengine/speculative.py:155) and greedy decoding's argmax (kvengine/decode.py:303).
  * x: [rows, cols] with `row_stride`; out: [rows] int32. Same tie/NaN rule as above. */

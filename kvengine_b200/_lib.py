@@ -64,6 +64,8 @@ _SIGNATURES = {
     "kve_launch_count": (C.c_ulonglong, []),
     "kve_greedy_accept_workspace_bytes": (sz, [i32]),
     "kve_greedy_accept": (i32, [vp, i32, i64, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp, sz, vp, vp]),
+    "kve_greedy_accept_noalloc_max_batch": (i32, []),
+    "kve_greedy_accept_noalloc": (i32, [vp, i32, i64, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp]),
     "kve_argmax_rows": (i32, [vp, i32, i32, i32, i64, vp, vp]),
     "kve_kv_append": (i32, [vp, vp, i32, vp, i32, i32, i32, vp, vp, i64, vp, vp]),
     "kve_qkv_rope_append": (i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp, vp, i64, vp, vp]),

@@ -7,6 +7,8 @@
 // warp ballot and resets the counter to zero, so the workspace stays clean.
 #include <math.h>
 
+#include <mutex>
+
 #include "kve_common.cuh"
 
 namespace kve {
@@ -203,4 +205,97 @@ extern "C" int kve_argmax_rows(const void* x, int dtype, int rows, int cols, int
     return set_error(KVE_ERR_DTYPE, "kve_argmax_rows: dtype %d", dtype);
   }
   return check_launch("kve_argmax_rows");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free greedy acceptance.
+//
+// kve_greedy_accept asks the caller for a small device workspace (one int32
+// arrival counter per sequence). Some callers cannot provide one on demand: a
+// host with no device allocator of its own (a plain C or FFI caller holding only
+// the logits and output pointers), or code running where an allocation is not
+// allowed (inside a CUDA-graph capture, or a serving loop with a fixed memory
+// budget). This entry point takes the counters from a file-scope device array
+// instead, so it allocates nothing.
+//
+// * The array holds kNoAllocMaxBatch counters (16 KiB); larger batches are
+//   rejected with KVE_ERR_ARG before anything is launched.
+// * The counters must be zero when a call starts. The array is zero when the
+//   module loads and every completed call leaves it zero again (the last CTA of
+//   each sequence resets that sequence's counter).
+// * Calls on one device share the array: two calls that overlap in time (on
+//   different streams without ordering between them) race on it. Order them on
+//   one stream, or use kve_greedy_accept with a workspace per stream.
+// * The device address of the array is looked up once per device, with that
+//   device current, on its first call. That lookup is not a stream operation,
+//   but it may load the module; make the first call on each device outside any
+//   stream capture.
+namespace kve {
+namespace {
+
+constexpr int kNoAllocMaxBatch = 4096;
+static __device__ __align__(256) int32_t g_accept_counters[kNoAllocMaxBatch];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_counter_mu;
+int32_t* g_counter_ptr[kMaxDevices] = {};
+
+// Device address of g_accept_counters on the current device, or null with the
+// error message set.
+int32_t* accept_counters_for_current_device() {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error(KVE_ERR_CUDA, "kve_greedy_accept_noalloc: no current device (%s)", cudaGetErrorString(e));
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> g(g_counter_mu);
+  if (!g_counter_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_accept_counters);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      set_error(KVE_ERR_CUDA, "kve_greedy_accept_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_counter_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  return g_counter_ptr[dev];
+}
+
+}  // namespace
+}  // namespace kve
+
+extern "C" int kve_greedy_accept_noalloc_max_batch(void) { return kve::kNoAllocMaxBatch; }
+
+extern "C" int kve_greedy_accept_noalloc(const void* logits, int dtype, int64_t row_stride, const int32_t* drafts,
+                                         int64_t draft_stride_b, int64_t draft_stride_j, int batch, int k,
+                                         int vocab, int32_t* out_preds, int32_t* out_n_accepted,
+                                         int32_t* out_emitted, cudaStream_t stream) {
+  if (batch < 0 || k < 1 || k > 31 || vocab < 1 || row_stride < vocab)
+    return set_error(KVE_ERR_ARG, "kve_greedy_accept_noalloc: bad sizes batch=%d k=%d vocab=%d stride=%lld",
+                     batch, k, vocab, (long long)row_stride);
+  if (batch > kNoAllocMaxBatch)
+    return set_error(KVE_ERR_ARG,
+                     "kve_greedy_accept_noalloc: batch %d exceeds the built-in maximum of %d sequences "
+                     "(use kve_greedy_accept with a workspace)",
+                     batch, kNoAllocMaxBatch);
+  if (batch == 0) return KVE_OK;
+  if (!logits || !drafts || !out_preds || !out_n_accepted || !out_emitted)
+    return set_error(KVE_ERR_ARG, "kve_greedy_accept_noalloc: null pointer");
+  if (dtype != KVE_F32 && dtype != KVE_BF16) return set_error(KVE_ERR_DTYPE, "kve_greedy_accept_noalloc: dtype %d", dtype);
+  int32_t* counters = accept_counters_for_current_device();
+  if (!counters) return KVE_ERR_CUDA;
+  dim3 grid(batch * (k + 1));
+  if (dtype == KVE_F32) {
+    launch_kernel(accept_kernel<float>, grid, dim3(kArgmaxThreads), 0, stream, static_cast<const float*>(logits),
+                  row_stride, drafts, draft_stride_b, draft_stride_j, k, vocab, vec_aligned(logits, row_stride, 4),
+                  out_preds, out_n_accepted, out_emitted, counters);
+  } else {
+    launch_kernel(accept_kernel<__nv_bfloat16>, grid, dim3(kArgmaxThreads), 0, stream,
+                  static_cast<const __nv_bfloat16*>(logits), row_stride, drafts, draft_stride_b, draft_stride_j, k,
+                  vocab, vec_aligned(logits, row_stride, 2), out_preds, out_n_accepted, out_emitted, counters);
+  }
+  return check_launch("kve_greedy_accept_noalloc");
 }
