@@ -224,8 +224,9 @@ def run_gpu(args):
         "kernel": "verify step: kve_forward of the 3B target over B*(k+1)=320 rows (36 layers + lm_head)",
         "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
         "frac": round(achieved / peak, 4), "peak_src": pk["src"] + (" sustained" if bound == "tensor" else ""),
-        "traffic": None,
-        "verify_ms": round(v_ms, 4), "verify_launches": len(steady),
+        "traffic": VERIFY_PASS_DRAM_BYTES, "traffic_src": "ncu dram__bytes_read.sum + dram__bytes_write.sum summed "
+        "over the kernels of one steady verify pass (bench.py --profile-iteration, --cache-control none)",
+        "verify_ms": round(v_ms, 4), "verify_passes_timed": len(steady),
         "alg_bytes_per_launch": round(alg_b), "alg_flops_per_launch": round(alg_f),
         "hbm_gbs_achieved": round(alg_b / (v_ms / 1e3) / 1e9, 1),
         "hbm_frac": round(alg_b / (v_ms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
@@ -420,6 +421,11 @@ def _time_launches(fns, iters: int) -> float:
 
 
 L2_BYTES = 126 * 2**20
+
+# DRAM bytes (read + write) of one steady verify pass of the config-4 workload, summed
+# over its kernels from an ncu launch list of `bench.py --profile-iteration` with
+# dram__bytes_read.sum and dram__bytes_write.sum (measured, not modelled).
+VERIFY_PASS_DRAM_BYTES = 7_191_400_000
 
 
 def run_micro(args):
