@@ -16,6 +16,7 @@
 #include <type_traits>
 
 #include "kve_common.cuh"
+#include "passes.cuh"
 
 namespace kve {
 namespace {
@@ -44,6 +45,11 @@ struct AttnParams {
   float* ws;  // split mode partials, null otherwise
   int n_chunks, n_qtiles;
   int* status;
+  // Keys before ctx - q_len of every sequence, the block tables and the
+  // length arrays are written by no kernel that may still be running (true in
+  // kve_forward: the pass's only K/V writer appends the new tokens): their loads
+  // may start before the dependency wait.
+  int hist_static;
 };
 
 __host__ __device__ inline size_t partial_floats(int hd) { return (size_t)kMaxRows * (hd + 2); }
@@ -222,7 +228,10 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
 template <int HD, int BS>
 __global__ void __launch_bounds__(kAttnThreads)
 paged_attn_mma_kernel(AttnParams p) {
-  grid_dep_wait();
+  // With hist_static the wait moves down to the first load of a key written in
+  // this pass (or of q); everything before it reads constant inputs only.
+  bool waited = !p.hist_static;
+  if (waited) grid_dep_wait();
   grid_dep_launch();
   constexpr int ROW = HD * 2 + 16;             // padded smem row (bytes)
   constexpr int TILE = kMmaKeyTile * ROW;      // one K or V tile
@@ -237,18 +246,23 @@ paged_attn_mma_kernel(AttnParams p) {
   const int c = blockIdx.x, bh = blockIdx.y, qtile = blockIdx.z;
   const int b = bh / p.nkv, h = bh % p.nkv;
   const int ctx = p.ctx_lens[b], ql = p.q_lens[b], qoff = p.q_offsets[b];
+  // Every CTA passes the dependency wait before it exits, so this grid never
+  // completes ahead of the kernels before it.
   if (ql < 0 || ctx < ql || ctx > p.table_stride * p.bs) {
+    if (!waited) grid_dep_wait();
     if (threadIdx.x == 0 && c == 0 && qtile == 0) report(p.status, KVE_ERR_BOUNDS);
     return;
   }
   const int t0 = qtile * p.qt;
-  if (t0 >= ql) return;
   const int nt = min(p.qt, ql - t0);
   const int rows = nt * p.group;
   const int first_pos = ctx - ql + t0;
   const int last_pos = first_pos + nt - 1;
   const int key_lo = c * kChunk;
-  if (key_lo > last_pos) return;
+  if (t0 >= ql || key_lo > last_pos) {
+    if (!waited) grid_dep_wait();
+    return;
+  }
   const int key_hi = min(min(ctx, key_lo + kChunk), last_pos + 1);
   const int n_tiles = (key_hi - key_lo + kMmaKeyTile - 1) / kMmaKeyTile;
 
@@ -310,11 +324,19 @@ paged_attn_mma_kernel(AttnParams p) {
   };
 
   // Prologue: keep kMmaStages - 1 tiles in flight (one commit group per tile, empty groups past the end).
+  const int hist_end = ctx - ql;  // keys below this were written before this pass
 #pragma unroll
   for (int t = 0; t < kMmaStages - 1; ++t) {
-    if (t < n_tiles) load_tile(t, t);
+    if (t < n_tiles) {
+      if (!waited && key_lo + (t + 1) * kMmaKeyTile > hist_end) {
+        grid_dep_wait();
+        waited = true;
+      }
+      load_tile(t, t);
+    }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
+  if (!waited) grid_dep_wait();  // before q and the remaining tiles
 
   // Q fragments for this warp's 16 rows (rows >= `rows` are zero).
   const int r_lo = warp * 16 + g, r_hi = r_lo + 8;
@@ -559,13 +581,12 @@ extern "C" size_t kve_paged_attn_workspace_bytes(int batch, int max_q_len, int m
   return (size_t)batch * num_kv_heads * n_qtiles * n_chunks * partial_floats(head_dim) * sizeof(float);
 }
 
-extern "C" int kve_paged_verify_attn(const void* q, int dtype, const void* pool_k, const void* pool_v,
-                                     const int32_t* block_tables, int table_stride, const int32_t* ctx_lens,
-                                     const int32_t* q_lens, const int32_t* q_offsets, int batch,
-                                     int max_q_len, int max_ctx, int num_heads, int num_kv_heads,
-                                     int head_dim, int block_size, int64_t num_blocks, float scale,
-                                     void* out, void* workspace, size_t workspace_bytes, int* dev_status,
-                                     cudaStream_t stream) {
+int kve::paged_attn_run(const void* q, int dtype, const void* pool_k, const void* pool_v,
+                        const int32_t* block_tables, int table_stride, const int32_t* ctx_lens,
+                        const int32_t* q_lens, const int32_t* q_offsets, int batch, int max_q_len, int max_ctx,
+                        int num_heads, int num_kv_heads, int head_dim, int block_size, int64_t num_blocks,
+                        float scale, void* out, void* workspace, size_t workspace_bytes, int* dev_status,
+                        bool hist_static, cudaStream_t stream) {
   if (batch < 0 || max_q_len < 0 || max_ctx < 0 || num_heads < 1 || num_kv_heads < 1 ||
       num_heads % num_kv_heads || block_size < 1 || table_stride < 1 || num_blocks < 1)
     return set_error(KVE_ERR_ARG, "kve_paged_verify_attn: bad sizes");
@@ -583,6 +604,7 @@ extern "C" int kve_paged_verify_attn(const void* q, int dtype, const void* pool_
   p.ctx_lens = ctx_lens; p.q_lens = q_lens; p.q_offsets = q_offsets;
   p.nq = num_heads; p.nkv = num_kv_heads; p.group = group; p.qt = qtile_tokens(group);
   p.bs = block_size; p.num_blocks = num_blocks; p.scale = scale; p.out = out; p.status = dev_status;
+  p.hist_static = hist_static ? 1 : 0;
   p.n_qtiles = (max_q_len + p.qt - 1) / p.qt;
   p.n_chunks = (max_ctx + kChunk - 1) / kChunk;
   if (p.n_chunks < 1) p.n_chunks = 1;
@@ -600,4 +622,16 @@ extern "C" int kve_paged_verify_attn(const void* q, int dtype, const void* pool_
                           : launch<__nv_bfloat16, 128>(p, batch, stream);
   }
   return set_error(KVE_ERR_DTYPE, "kve_paged_verify_attn: dtype %d", dtype);
+}
+
+extern "C" int kve_paged_verify_attn(const void* q, int dtype, const void* pool_k, const void* pool_v,
+                                     const int32_t* block_tables, int table_stride, const int32_t* ctx_lens,
+                                     const int32_t* q_lens, const int32_t* q_offsets, int batch,
+                                     int max_q_len, int max_ctx, int num_heads, int num_kv_heads,
+                                     int head_dim, int block_size, int64_t num_blocks, float scale,
+                                     void* out, void* workspace, size_t workspace_bytes, int* dev_status,
+                                     cudaStream_t stream) {
+  return paged_attn_run(q, dtype, pool_k, pool_v, block_tables, table_stride, ctx_lens, q_lens, q_offsets, batch,
+                        max_q_len, max_ctx, num_heads, num_kv_heads, head_dim, block_size, num_blocks, scale, out,
+                        workspace, workspace_bytes, dev_status, false, stream);
 }

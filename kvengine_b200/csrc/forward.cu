@@ -2,6 +2,7 @@
 // Host code only; every kernel it launches is one of the library's entry points (the GEMMs
 // through gemm_run, which may request the constant weights before the previous kernel ends).
 #include "gemm_epilogue.cuh"
+#include "passes.cuh"
 
 namespace {
 
@@ -57,10 +58,10 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
     KVE_TRY(kve_qkv_rope_append(s->qkv, dt, M, m->num_heads, m->num_kv_heads, m->head_dim, b->positions,
                                 b->slots, m->rope_cos, m->rope_sin, m->rope_len, s->q, L.pool_k, L.pool_v,
                                 num_slots, s->dev_status, stream));
-    KVE_TRY(kve_paged_verify_attn(s->q, dt, L.pool_k, L.pool_v, b->block_tables, b->table_stride, b->ctx_lens,
+    KVE_TRY(paged_attn_run(s->q, dt, L.pool_k, L.pool_v, b->block_tables, b->table_stride, b->ctx_lens,
                                   b->q_lens, b->q_offsets, b->n_seqs, b->max_q_len, b->max_ctx, m->num_heads,
                                   m->num_kv_heads, m->head_dim, m->block_size, m->num_blocks, scale, s->attn,
-                                  s->attn_ws, s->attn_ws_bytes, s->dev_status, stream));
+                                  s->attn_ws, s->attn_ws_bytes, s->dev_status, true, stream));
     KVE_TRY(gemm_run(s->attn, L.w_o, dt, M, H, qsz, KVE_EPI_RESIDUAL, nullptr, s->hidden, s->hidden, dt,
                      s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
     KVE_TRY(kve_rmsnorm(s->hidden, dt, L.ln2, M, H, m->rms_eps, nullptr, s->normed, stream));
