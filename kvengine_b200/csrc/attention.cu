@@ -3,8 +3,9 @@
 // CTA = (context chunk, sequence x kv-head, query tile). All query rows of one
 // kv-head group (q tokens x group heads, <= 64 rows) share every K/V tile the
 // CTA stages through shared memory, so each K/V byte is read from HBM once per
-// query tile. Keys are visited in absolute 32-key tiles; chunks of 512 keys
-// run in parallel and are merged in a fixed order by a second kernel. A
+// query tile. Keys are visited in absolute 32-key tiles; chunks of kChunk keys
+// run in parallel and are merged in chunk order (bf16: by the last chunk CTA
+// to finish, in the same launch; fp32: by a second kernel). A
 // query's result therefore depends only on its own position and keys: the
 // draft's 1-row pass and the target's k+1-row pass agree bit for bit.
 //
@@ -43,7 +44,9 @@ struct AttnParams {
   float scale;
   void* out;
   float* ws;  // split mode partials, null otherwise
+  int* counters;  // split mode (bf16): finished-chunk count per (sequence x kv-head, query tile), left at zero
   int n_chunks, n_qtiles;
+  int rb;  // bf16 kernel: row blocks (16 query rows each) per CTA
   int* status;
   // Keys before ctx - q_len of every sequence, the block tables and the
   // length arrays are written by no kernel that may still be running (true in
@@ -67,7 +70,7 @@ paged_attn_kernel(AttnParams p) {
   float* ks = qs + kMaxRows * HD;            // [kKeyTile][HD + 1]
   float* vs = ks + kKeyTile * (HD + 1);      // [kKeyTile][HD]
 
-  const int c = blockIdx.x, bh = blockIdx.y, qtile = blockIdx.z;
+  const int bh = blockIdx.x, c = blockIdx.y, qtile = blockIdx.z;
   const int b = bh / p.nkv, h = bh % p.nkv;
   const int ctx = p.ctx_lens[b], ql = p.q_lens[b], qoff = p.q_offsets[b];
   if (ql < 0 || ctx < ql || ctx > p.table_stride * p.bs) {
@@ -197,7 +200,12 @@ paged_attn_kernel(AttnParams p) {
 // softmax in registers. Every row's arithmetic depends only on that row and on
 // keys at fixed absolute positions, so results do not depend on the batch.
 constexpr int kMmaKeyTile = 32;
-constexpr int kMmaStages = 4;
+// Key tile t of a chunk (32 keys at key_lo + 32 t) belongs to key slice
+// t % kKeySlices. The slices of a row block (16 query rows) run in separate warps
+// at the same time and their softmax states merge in slice order at the end, so
+// a row's arithmetic is the same whatever the number of row blocks in its CTA.
+constexpr int kKeySlices = 4;
+constexpr int kRoundBufs = 2;  // rounds (kKeySlices tiles each) staged in shared memory
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -225,25 +233,63 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 
-template <int HD, int BS>
-__global__ void __launch_bounds__(kAttnThreads)
+// Merge chunk partials in chunk order for the rows of one (sequence x kv-head,
+// query tile). A row at position pos reads chunks 0 .. pos / kChunk; with a
+// single chunk this reproduces acc / l exactly. Partials are read through L2
+// (another CTA of the same launch may have written them).
+template <typename T, int HD, int WARPS>
+__device__ __forceinline__ void merge_partials(const AttnParams& p, int bh, int qtile, int h, int rows,
+                                               int first_pos, int qoff, int t0) {
+  constexpr int DPL = HD / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* base = p.ws + (((size_t)bh * p.n_qtiles + qtile) * p.n_chunks) * partial_floats(HD);
+  T* out = static_cast<T*>(p.out);
+  for (int r = warp; r < rows; r += WARPS) {
+    const int pos = first_pos + r / p.group;
+    const int live = pos / kChunk + 1;
+    float mx = -INFINITY;
+    for (int c = 0; c < live; ++c) mx = fmaxf(mx, __ldcg(base + c * partial_floats(HD) + (size_t)r * (HD + 2) + HD));
+    float lsum = 0.f, acc[DPL];
+#pragma unroll
+    for (int dd = 0; dd < DPL; ++dd) acc[dd] = 0.f;
+    for (int c = 0; c < live; ++c) {
+      const float* pr = base + c * partial_floats(HD) + (size_t)r * (HD + 2);
+      float w = expf(__ldcg(pr + HD) - mx);
+      lsum += __ldcg(pr + HD + 1) * w;
+#pragma unroll
+      for (int dd = 0; dd < DPL; ++dd) acc[dd] += __ldcg(pr + lane + dd * 32) * w;
+    }
+    int t = r / p.group, g = r % p.group;
+    T* o = out + ((size_t)(qoff + t0 + t) * p.nq + h * p.group + g) * HD;
+#pragma unroll
+    for (int dd = 0; dd < DPL; ++dd) o[lane + dd * 32] = Elem<T>::from_f(acc[dd] / lsum);
+  }
+}
+
+template <int HD, int BS, int RB>
+__global__ void __launch_bounds__(RB * kKeySlices * 32, 1)
 paged_attn_mma_kernel(AttnParams p) {
   // With hist_static the wait moves down to the first load of a key written in
   // this pass (or of q); everything before it reads constant inputs only.
   bool waited = !p.hist_static;
   if (waited) grid_dep_wait();
   grid_dep_launch();
-  constexpr int ROW = HD * 2 + 16;             // padded smem row (bytes)
-  constexpr int TILE = kMmaKeyTile * ROW;      // one K or V tile
-  constexpr int KSTEPS = HD / 16;              // k16 steps over the head dim
-  constexpr int NT = kMmaKeyTile / 8;          // n8 tiles of keys per tile
-  constexpr int DT = HD / 8;                   // n8 tiles of the output
-  constexpr int CPR = HD * 2 / 16;             // 16-byte chunks per key row
+  constexpr int NTHR = RB * kKeySlices * 32;
+  constexpr int ROW = HD * 2 + 16;                  // padded smem row (bytes)
+  constexpr int TILE = kMmaKeyTile * ROW;           // one K or V tile
+  constexpr int ROUND = kKeySlices * 2 * TILE;      // K and V of one round (kKeySlices tiles)
+  constexpr int KSTEPS = HD / 16;                   // k16 steps over the head dim
+  constexpr int NT = kMmaKeyTile / 8;               // n8 tiles of keys per tile
+  constexpr int DT = HD / 8;                        // n8 tiles of the output
+  constexpr int CPR = HD * 2 / 16;                  // 16-byte chunks per key row
+  constexpr int TCH = 2 * kMmaKeyTile * CPR;        // 16-byte chunks of one tile (K and V)
+  constexpr int SLOTS = kKeySlices * TCH / NTHR;    // chunks per thread per round
+  static_assert(kKeySlices * TCH % NTHR == 0, "round copy must divide evenly");
   extern __shared__ __align__(128) uint8_t smem_attn[];
   const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem_attn));
-  // buffers: [stage][K|V] tiles, then the chunk's block table
+  // buffers: [round buffer][slice][K|V] tiles, then the chunk's block table
 
-  const int c = blockIdx.x, bh = blockIdx.y, qtile = blockIdx.z;
+  const int bh = blockIdx.x, c = blockIdx.y, qtile = blockIdx.z;
   const int b = bh / p.nkv, h = bh % p.nkv;
   const int ctx = p.ctx_lens[b], ql = p.q_lens[b], qoff = p.q_offsets[b];
   // Every CTA passes the dependency wait before it exits, so this grid never
@@ -265,19 +311,21 @@ paged_attn_mma_kernel(AttnParams p) {
   }
   const int key_hi = min(min(ctx, key_lo + kChunk), last_pos + 1);
   const int n_tiles = (key_hi - key_lo + kMmaKeyTile - 1) / kMmaKeyTile;
+  const int n_rounds = (n_tiles + kKeySlices - 1) / kKeySlices;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rb = warp % RB, ks = warp / RB;  // row block, key slice
   const int g = lane >> 2, tq = lane & 3;
   const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.q);
   const __nv_bfloat16* pk = static_cast<const __nv_bfloat16*>(p.pool_k);
   const __nv_bfloat16* pv = static_cast<const __nv_bfloat16*>(p.pool_v);
   const int32_t* table = p.tables + (size_t)b * p.table_stride;
 
-  // The chunk's block-table entries, staged once (512 keys / block size).
-  int* tab = reinterpret_cast<int*>(smem_attn + kMmaStages * 2 * TILE);
+  // The chunk's block-table entries, staged once (kChunk keys / block size).
+  int* tab = reinterpret_cast<int*>(smem_attn + kRoundBufs * ROUND);
   const int blk_lo = BS > 0 ? key_lo / BS : key_lo / p.bs;
   const int n_blk = (BS > 0 ? (key_hi - 1) / BS : (key_hi - 1) / p.bs) - blk_lo + 1;
-  for (int i = threadIdx.x; i < n_blk; i += kAttnThreads) {
+  for (int i = threadIdx.x; i < n_blk; i += NTHR) {
     int64_t blk = table[blk_lo + i];
     if (blk < 0 || blk >= p.num_blocks) {
       report(p.status, KVE_ERR_BOUNDS);
@@ -287,23 +335,24 @@ paged_attn_mma_kernel(AttnParams p) {
   }
   __syncthreads();
 
-  // Each thread copies the same (key-in-tile, 16-byte chunk) slots of every tile.
-  constexpr int SLOTS = 2 * kMmaKeyTile * CPR / kAttnThreads;  // K and V chunks per thread per tile
-  static_assert(2 * kMmaKeyTile * CPR % kAttnThreads == 0, "tile copy must divide evenly");
+  // Round r holds tiles r*kKeySlices .. +kKeySlices-1 (tile s of the round at
+  // slot s); every thread copies the same slots of every round.
   const size_t head_off = (size_t)h * HD;
   const size_t row_stride = (size_t)p.nkv * HD;  // elements between consecutive tokens
-  auto load_tile = [&](int tile, int stage) {
-    const int kt = key_lo + tile * kMmaKeyTile;
+  auto load_round = [&](int r) {
+    const uint32_t rbase = sbase + (uint32_t)((r % kRoundBufs) * ROUND);
 #pragma unroll
     for (int u = 0; u < SLOTS; ++u) {
-      const int i = threadIdx.x + u * kAttnThreads;
-      const bool is_v = i >= kMmaKeyTile * CPR;
-      const int j = is_v ? i - kMmaKeyTile * CPR : i;
+      const int i = threadIdx.x + u * NTHR;
+      const int s = i / TCH, rem = i % TCH;
+      const bool is_v = rem >= kMmaKeyTile * CPR;
+      const int j = is_v ? rem - kMmaKeyTile * CPR : rem;
       const int kk = j / CPR, ch = j % CPR;
-      const int key = kt + kk;
+      const int tile = r * kKeySlices + s;
+      const int key = key_lo + tile * kMmaKeyTile + kk;
       const __nv_bfloat16* src = pk;
       uint32_t bytes = 0;
-      if (key < key_hi) {
+      if (tile < n_tiles && key < key_hi) {
         int blk, off;
         if constexpr (BS > 0) {
           blk = tab[key / BS - blk_lo];
@@ -318,28 +367,29 @@ paged_attn_mma_kernel(AttnParams p) {
           bytes = 16;
         }
       }
-      const uint32_t dst = sbase + (uint32_t)(stage * 2 * TILE + (is_v ? TILE : 0) + kk * ROW + ch * 16);
-      cp_async16(dst, src, bytes);
+      cp_async16(rbase + (uint32_t)(s * 2 * TILE + (is_v ? TILE : 0) + kk * ROW + ch * 16), src, bytes);
     }
   };
 
-  // Prologue: keep kMmaStages - 1 tiles in flight (one commit group per tile, empty groups past the end).
+  // Prologue: kRoundBufs rounds in flight (one commit group per round, empty
+  // groups past the end). Rounds of history keys may load before the wait.
   const int hist_end = ctx - ql;  // keys below this were written before this pass
 #pragma unroll
-  for (int t = 0; t < kMmaStages - 1; ++t) {
-    if (t < n_tiles) {
-      if (!waited && key_lo + (t + 1) * kMmaKeyTile > hist_end) {
+  for (int r = 0; r < kRoundBufs; ++r) {
+    if (r < n_rounds) {
+      if (!waited && key_lo + (r + 1) * kKeySlices * kMmaKeyTile > hist_end) {
         grid_dep_wait();
         waited = true;
       }
-      load_tile(t, t);
+      load_round(r);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
-  if (!waited) grid_dep_wait();  // before q and the remaining tiles
+  if (!waited) grid_dep_wait();  // before q and the remaining rounds
 
   // Q fragments for this warp's 16 rows (rows >= `rows` are zero).
-  const int r_lo = warp * 16 + g, r_hi = r_lo + 8;
+  const int r_lo = rb * 16 + g, r_hi = r_lo + 8;
+  const bool active = rb * 16 < rows;
   uint32_t qa[KSTEPS][4];
   {
     const __nv_bfloat16* q_lo = nullptr;
@@ -363,18 +413,15 @@ paged_attn_mma_kernel(AttnParams p) {
 #pragma unroll
   for (int j = 0; j < DT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 
-  for (int tile = 0; tile < n_tiles; ++tile) {
-    const int stage = tile % kMmaStages;
-    // Tile `tile` is the oldest outstanding group once kMmaStages - 2 newer ones may remain.
-    asm volatile("cp.async.wait_group %0;" ::"n"(kMmaStages - 2) : "memory");
+  for (int r = 0; r < n_rounds; ++r) {
+    // Round r is the oldest outstanding group once kRoundBufs - 1 newer ones may remain.
+    asm volatile("cp.async.wait_group %0;" ::"n"(kRoundBufs - 1) : "memory");
     __syncthreads();
-    // Refill the stage freed by the previous iteration (everyone passed the barrier above).
-    if (tile + kMmaStages - 1 < n_tiles) load_tile(tile + kMmaStages - 1, (tile + kMmaStages - 1) % kMmaStages);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    const uint32_t kbase = sbase + stage * 2 * TILE;
-    const uint32_t vbase = kbase + TILE;
-    const int kt = key_lo + tile * kMmaKeyTile;
-    if (warp * 16 < rows) {
+    const int tile = r * kKeySlices + ks;
+    if (active && tile < n_tiles) {
+      const uint32_t kbase = sbase + (uint32_t)((r % kRoundBufs) * ROUND + ks * 2 * TILE);
+      const uint32_t vbase = kbase + TILE;
+      const int kt = key_lo + tile * kMmaKeyTile;
       // S = Q K^T over this tile's 32 keys.
       float sc[NT][4];
 #pragma unroll
@@ -456,12 +503,80 @@ paged_attn_mma_kernel(AttnParams p) {
         }
       }
     }
+    __syncthreads();  // every slice is done with this round's buffer
+    if (r + kRoundBufs < n_rounds) load_round(r + kRoundBufs);
+    asm volatile("cp.async.commit_group;" ::: "memory");
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
 
-  // Write the normalised output, or this chunk's partial for the combine kernel.
-  if (warp * 16 >= rows) return;
+  // Merge the key slices of each row block in slice order through shared memory
+  // (the round buffers are free now): slices 1.. publish, slice 0 merges. A
+  // slice that saw no key of a row has m = -inf and weight 0.
+  constexpr int XS = HD + 8;  // padded row (floats): the 8 rows g of a warp hit different banks
+  float* xs = reinterpret_cast<float*>(smem_attn);                 // [slice-1][rb][16 rows][XS]
+  float* xml = xs + (size_t)(kKeySlices - 1) * RB * 16 * XS;       // [slice-1][rb][16 rows][m, l]
+  if (ks > 0 && active) {
+    float* a = xs + (size_t)((ks - 1) * RB + rb) * 16 * XS;
+#pragma unroll
+    for (int j = 0; j < DT; ++j) {
+      *reinterpret_cast<float2*>(a + g * XS + 8 * j + 2 * tq) = make_float2(acc[j][0], acc[j][1]);
+      *reinterpret_cast<float2*>(a + (g + 8) * XS + 8 * j + 2 * tq) = make_float2(acc[j][2], acc[j][3]);
+    }
+    if (tq == 0) {
+      float* ml = xml + (size_t)((ks - 1) * RB + rb) * 16 * 2;
+      ml[g * 2] = m_lo;
+      ml[g * 2 + 1] = l_lo;
+      ml[(g + 8) * 2] = m_hi;
+      ml[(g + 8) * 2 + 1] = l_hi;
+    }
+  }
+  __syncthreads();
+  const bool writer = ks == 0 && active;
+  if (writer) {
+    float mm_lo = m_lo, mm_hi = m_hi;
+#pragma unroll
+    for (int s = 1; s < kKeySlices; ++s) {
+      const float* ml = xml + (size_t)((s - 1) * RB + rb) * 16 * 2;
+      mm_lo = fmaxf(mm_lo, ml[g * 2]);
+      mm_hi = fmaxf(mm_hi, ml[(g + 8) * 2]);
+    }
+    const float w0_lo = m_lo == -INFINITY ? 0.f : expf(m_lo - mm_lo);
+    const float w0_hi = m_hi == -INFINITY ? 0.f : expf(m_hi - mm_hi);
+    l_lo *= w0_lo;
+    l_hi *= w0_hi;
+#pragma unroll
+    for (int j = 0; j < DT; ++j) {
+      acc[j][0] *= w0_lo; acc[j][1] *= w0_lo;
+      acc[j][2] *= w0_hi; acc[j][3] *= w0_hi;
+    }
+#pragma unroll
+    for (int s = 1; s < kKeySlices; ++s) {
+      const float* ml = xml + (size_t)((s - 1) * RB + rb) * 16 * 2;
+      const float* a = xs + (size_t)((s - 1) * RB + rb) * 16 * XS;
+      const float ms_lo = ml[g * 2], ms_hi = ml[(g + 8) * 2];
+      const float w_lo = ms_lo == -INFINITY ? 0.f : expf(ms_lo - mm_lo);
+      const float w_hi = ms_hi == -INFINITY ? 0.f : expf(ms_hi - mm_hi);
+      l_lo += ml[g * 2 + 1] * w_lo;
+      l_hi += ml[(g + 8) * 2 + 1] * w_hi;
+#pragma unroll
+      for (int j = 0; j < DT; ++j) {
+        const float2 x_lo = *reinterpret_cast<const float2*>(a + g * XS + 8 * j + 2 * tq);
+        const float2 x_hi = *reinterpret_cast<const float2*>(a + (g + 8) * XS + 8 * j + 2 * tq);
+        acc[j][0] += x_lo.x * w_lo;
+        acc[j][1] += x_lo.y * w_lo;
+        acc[j][2] += x_hi.x * w_hi;
+        acc[j][3] += x_hi.y * w_hi;
+      }
+    }
+    m_lo = mm_lo;
+    m_hi = mm_hi;
+  }
+
+  // Write the normalised output, or this chunk's partial; the last chunk CTA of
+  // this (sequence x kv-head, query tile) to finish then merges all of them.
   if (p.ws == nullptr) {
+    if (!writer) return;
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
@@ -480,7 +595,7 @@ paged_attn_mma_kernel(AttnParams p) {
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int r = half ? r_hi : r_lo;
-      if (r >= rows) continue;
+      if (!writer || r >= rows) continue;
       float* pr = part + (size_t)r * (HD + 2);
 #pragma unroll
       for (int j = 0; j < DT; ++j) {
@@ -492,17 +607,31 @@ paged_attn_mma_kernel(AttnParams p) {
         pr[HD + 1] = half ? l_hi : l_lo;
       }
     }
+    if (!p.counters) return;  // merged by attn_combine_kernel
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (threadIdx.x == 0) {
+      // CTAs c = 0 .. last_pos / kChunk do work for this tile; the others exited early.
+      int* cnt = p.counters + (size_t)bh * p.n_qtiles + qtile;
+      const int prev = atomicAdd(cnt, 1);
+      s_last = prev == last_pos / kChunk;
+      if (s_last) *cnt = 0;  // leave the workspace zeroed
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      merge_partials<__nv_bfloat16, HD, NTHR / 32>(p, bh, qtile, h, rows, first_pos, qoff, t0);
+    }
   }
 }
 
-// Merge chunk partials in chunk order. A row at position pos reads chunks
-// 0 .. pos / kChunk; with a single chunk this reproduces acc / l exactly.
+// Separate merge pass for the CUDA-core (fp32) kernel's chunk partials.
 template <typename T, int HD>
 __global__ void __launch_bounds__(kAttnThreads)
 attn_combine_kernel(AttnParams p) {
   grid_dep_wait();
   grid_dep_launch();
-  constexpr int DPL = HD / 32;
   const int bh = blockIdx.x, qtile = blockIdx.y;
   const int b = bh / p.nkv, h = bh % p.nkv;
   const int ctx = p.ctx_lens[b], ql = p.q_lens[b], qoff = p.q_offsets[b];
@@ -510,46 +639,39 @@ attn_combine_kernel(AttnParams p) {
   const int t0 = qtile * p.qt;
   if (t0 >= ql) return;
   const int nt = min(p.qt, ql - t0);
-  const int rows = nt * p.group;
-  const int first_pos = ctx - ql + t0;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float* base = p.ws + (((size_t)bh * p.n_qtiles + qtile) * p.n_chunks) * partial_floats(HD);
-  T* out = static_cast<T*>(p.out);
-  for (int r = warp; r < rows; r += kWarps) {
-    const int pos = first_pos + r / p.group;
-    const int live = pos / kChunk + 1;
-    float mx = -INFINITY;
-    for (int c = 0; c < live; ++c) mx = fmaxf(mx, base[c * partial_floats(HD) + (size_t)r * (HD + 2) + HD]);
-    float lsum = 0.f, acc[DPL];
-#pragma unroll
-    for (int dd = 0; dd < DPL; ++dd) acc[dd] = 0.f;
-    for (int c = 0; c < live; ++c) {
-      const float* pr = base + c * partial_floats(HD) + (size_t)r * (HD + 2);
-      float w = expf(pr[HD] - mx);
-      lsum += pr[HD + 1] * w;
-#pragma unroll
-      for (int dd = 0; dd < DPL; ++dd) acc[dd] += pr[lane + dd * 32] * w;
-    }
-    int t = r / p.group, g = r % p.group;
-    T* o = out + ((size_t)(qoff + t0 + t) * p.nq + h * p.group + g) * HD;
-#pragma unroll
-    for (int dd = 0; dd < DPL; ++dd) o[lane + dd * 32] = Elem<T>::from_f(acc[dd] / lsum);
-  }
+  merge_partials<T, HD, kWarps>(p, bh, qtile, h, nt * p.group, ctx - ql + t0, qoff, t0);
+}
+
+template <int HD, int BS, int RB>
+void launch_mma(const AttnParams& p, dim3 grid, cudaStream_t stream) {
+  // round buffers (K + V of kKeySlices tiles, twice), then the chunk's block table
+  // (<= kChunk entries); the slice merge reuses the round buffers.
+  constexpr size_t kRounds = (size_t)kRoundBufs * kKeySlices * 2 * kMmaKeyTile * (HD * 2 + 16);
+  constexpr size_t kMerge = (size_t)(kKeySlices - 1) * RB * 16 * (HD + 8 + 2) * sizeof(float);
+  static_assert(kMerge <= kRounds, "slice merge must fit in the round buffers");
+  constexpr size_t smem = kRounds + kChunk * sizeof(int);
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(paged_attn_mma_kernel<HD, BS, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  launch_kernel(paged_attn_mma_kernel<HD, BS, RB>, grid, dim3(RB * kKeySlices * 32), smem, stream, p);
+}
+
+template <int HD, int BS>
+void launch_mma_rb(const AttnParams& p, dim3 grid, cudaStream_t stream) {
+  if (p.rb == 1) launch_mma<HD, BS, 1>(p, grid, stream);
+  else if (p.rb == 2) launch_mma<HD, BS, 2>(p, grid, stream);
+  else launch_mma<HD, BS, 4>(p, grid, stream);
 }
 
 template <typename T, int HD>
 int launch(AttnParams& p, int batch, cudaStream_t stream) {
-  dim3 grid(p.n_chunks, batch * p.nkv, p.n_qtiles);
+  // (sequence x kv-head) fastest: every sequence's chunk-0 CTA is scheduled before any
+  // later chunk, and the empty late-chunk CTAs of short sequences come last.
+  dim3 grid(batch * p.nkv, p.n_chunks, p.n_qtiles);
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    // stages x (K + V) tiles, then the chunk's block table (<= 512 entries for block size >= 1)
-    const size_t smem = (size_t)kMmaStages * 2 * kMmaKeyTile * (HD * 2 + 16) + kChunk * sizeof(int);
-    static std::once_flag once;
-    std::call_once(once, [smem] {
-      cudaFuncSetAttribute(paged_attn_mma_kernel<HD, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      cudaFuncSetAttribute(paged_attn_mma_kernel<HD, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    });
-    if (p.bs == 16) launch_kernel(paged_attn_mma_kernel<HD, 16>, dim3(grid), dim3(kAttnThreads), smem, stream, p);
-    else launch_kernel(paged_attn_mma_kernel<HD, 0>, dim3(grid), dim3(kAttnThreads), smem, stream, p);
+    if (p.bs == 16) launch_mma_rb<HD, 16>(p, grid, stream);
+    else launch_mma_rb<HD, 0>(p, grid, stream);
   } else {
     const size_t smem = sizeof(float) * ((size_t)kMaxRows * HD + kKeyTile * (HD + 1) + kKeyTile * HD);
     static std::once_flag once;
@@ -559,12 +681,30 @@ int launch(AttnParams& p, int batch, cudaStream_t stream) {
     launch_kernel(paged_attn_kernel<T, HD>, dim3(grid), dim3(kAttnThreads), smem, stream, p);
   }
   int rc = check_launch("kve_paged_verify_attn");
-  if (rc || !p.ws) return rc;
+  if (rc || !p.ws || (std::is_same<T, __nv_bfloat16>::value && p.counters)) return rc;  // merged in-kernel
   launch_kernel(attn_combine_kernel<T, HD>, dim3(batch * p.nkv, p.n_qtiles), dim3(kAttnThreads), 0, stream, p);
   return check_launch("kve_paged_verify_attn(combine)");
 }
 
 int qtile_tokens(int group) { return group >= kMaxRows ? 1 : kMaxRows / group; }
+
+// bf16 kernel: row blocks of 16 query rows per CTA, from the largest query tile
+// (rows = tokens x group) of the call; a query tile holds 16 * rb / group tokens.
+int row_blocks(int max_q_len, int group) {
+  const long long rows = (long long)max_q_len * group;
+  return rows <= 16 ? 1 : rows <= 32 ? 2 : 4;
+}
+int mma_qtile_tokens(int max_q_len, int group) { return row_blocks(max_q_len, group) * 16 / group; }
+
+// Split-mode workspace: kCounterSlots int32 chunk counters at offset 0 (always the
+// same addresses, so no call's partials ever land on them), then the fp32
+// partials [B*nkv][n_qtiles][n_chunks][64 rows][hd + 2]. Tiles beyond
+// kCounterSlots merge in a second kernel instead.
+constexpr size_t kCounterSlots = 16384;
+constexpr size_t kCounterBytes = kCounterSlots * sizeof(int32_t);
+size_t partials_bytes(size_t batch, size_t nkv, size_t n_qtiles, size_t n_chunks, int hd) {
+  return batch * nkv * n_qtiles * n_chunks * partial_floats(hd) * sizeof(float);
+}
 
 }  // namespace
 }  // namespace kve
@@ -575,10 +715,12 @@ extern "C" size_t kve_paged_attn_workspace_bytes(int batch, int max_q_len, int m
                                                  int num_kv_heads, int head_dim) {
   if (batch <= 0 || num_kv_heads <= 0 || max_ctx <= kChunk || head_dim <= 0) return 0;
   int group = num_heads / num_kv_heads;
-  int qt = qtile_tokens(group);
+  if (group < 1 || group > kMaxRows) return 0;
+  // The bf16 kernel's query tiles are never larger than the fp32 kernel's: size for them.
+  int qt = mma_qtile_tokens(max_q_len, group);
   size_t n_qtiles = (max_q_len + qt - 1) / qt;
   size_t n_chunks = (max_ctx + kChunk - 1) / kChunk;
-  return (size_t)batch * num_kv_heads * n_qtiles * n_chunks * partial_floats(head_dim) * sizeof(float);
+  return kCounterBytes + partials_bytes(batch, num_kv_heads, n_qtiles, n_chunks, head_dim);
 }
 
 int kve::paged_attn_run(const void* q, int dtype, const void* pool_k, const void* pool_v,
@@ -602,7 +744,9 @@ int kve::paged_attn_run(const void* q, int dtype, const void* pool_k, const void
   AttnParams p{};
   p.q = q; p.pool_k = pool_k; p.pool_v = pool_v; p.tables = block_tables; p.table_stride = table_stride;
   p.ctx_lens = ctx_lens; p.q_lens = q_lens; p.q_offsets = q_offsets;
-  p.nq = num_heads; p.nkv = num_kv_heads; p.group = group; p.qt = qtile_tokens(group);
+  p.nq = num_heads; p.nkv = num_kv_heads; p.group = group;
+  p.rb = row_blocks(max_q_len, group);
+  p.qt = dtype == KVE_BF16 ? mma_qtile_tokens(max_q_len, group) : qtile_tokens(group);
   p.bs = block_size; p.num_blocks = num_blocks; p.scale = scale; p.out = out; p.status = dev_status;
   p.hist_static = hist_static ? 1 : 0;
   p.n_qtiles = (max_q_len + p.qt - 1) / p.qt;
@@ -613,7 +757,9 @@ int kve::paged_attn_run(const void* q, int dtype, const void* pool_k, const void
     size_t need = kve_paged_attn_workspace_bytes(batch, max_q_len, max_ctx, num_heads, num_kv_heads, head_dim);
     if (!workspace || workspace_bytes < need)
       return set_error(KVE_ERR_WORKSPACE, "kve_paged_verify_attn: workspace needs %zu bytes", need);
-    p.ws = static_cast<float*>(workspace);
+    p.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
+    p.counters = (size_t)batch * num_kv_heads * p.n_qtiles <= kCounterSlots ? static_cast<int*>(workspace)
+                                                                             : nullptr;
   }
   if (dtype == KVE_F32) {
     return head_dim == 64 ? launch<float, 64>(p, batch, stream) : launch<float, 128>(p, batch, stream);
