@@ -168,6 +168,21 @@ int kve_gemm_ex(const void* x, const void* w, int dtype, int m, int n, int k, in
                 const float* bias, const void* residual, void* out, int out_dtype, void* workspace,
                 size_t workspace_bytes, int* dev_status, int algo, cudaStream_t stream);
 
+/* Tuning and test hook (no kvengine counterpart): force the tcgen05 GEMM's launch
+ * shape for later calls in this process: token_tiles (tiles the tokens are cut
+ * into), weight_halves (1 or 2 blocks of 128 weight rows per CTA) and k_chunks
+ * (1, 2 or 4 64-wide k-chunks per pipeline stage); 0 restores the model's choice
+ * for that parameter. A forced value applies only where it is valid for a given
+ * GEMM. The split-K factor is never forced, so results are bit-identical under
+ * every shape; only speed changes. */
+int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_chunks);
+
+/* The tcgen05 GEMM's launch plan for an [m, k] x [n, k]^T product (no kvengine
+ * counterpart): out[0..8] = split-K factor, token tiles, token groups per tile,
+ * tokens per group, weight halves, k-chunks per stage, pipeline stages, 3-D
+ * tensor maps (0/1), feature tiles. */
+int kve_gemm_plan_info(int m, int n, int k, int* out);
+
 /* ------------------------------------------------------------------------
  * Whole forward pass (one call launches every kernel of one model pass).
  * Replaces kvengine/forward.py:147-215 (`forward_with_own_cache`) generalised

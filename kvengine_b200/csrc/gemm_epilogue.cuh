@@ -49,6 +49,16 @@ __device__ __forceinline__ void epi_store(const EpiArgs& e, int row, int col, fl
 
 __device__ __forceinline__ float silu_ref(float g) { return g / (1.0f + expf(-g)); }
 
+// SiLU with the fast exponential and division intrinsics: a few fp32 ulp, and
+// branch-free, so the SwiGLU pairs of one thread overlap instead of running one
+// division slow-path check after another. The exponent is capped at 80 so the
+// denominator stays below 2^126, the range __fdividef is exact to 2 ulp in; for
+// g < -80 the true result (|g| e^g < 1e-33) and this one are both 0 to within
+// bf16 rounding of any sum they enter. The result is rounded to the model dtype
+// right after, where the difference from g / (1 + expf(-g)) is far below one
+// bf16 ulp except next to a rounding boundary.
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(fminf(-g, 80.0f))); }
+
 // SwiGLU pair: gate and up accumulators of output column j.
 __device__ __forceinline__ void epi_silu_mul(const EpiArgs& e, int row, int j, float gate, float up) {
   float g = round_to(e.out_dtype, gate);

@@ -25,6 +25,7 @@
 #include <cuda.h>
 #include <math.h>
 
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 #include <type_traits>
@@ -40,7 +41,7 @@ constexpr int UMMA_K = 16;       // K per tcgen05.mma for 16-bit inputs
 constexpr int kEpiGroups = 2;    // epilogue warpgroups (each covers all 128 TMEM lanes)
 constexpr int kThreads = 64 + 128 * kEpiGroups;  // producer warp, MMA warp, epilogue warps
 constexpr int kMaxNG = 256;      // tokens per MMA (N of one tcgen05.mma)
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 12;
 constexpr int kMaxSplits = 8;    // portable cluster size
 constexpr int kRows = 32;                    // tokens per staged output chunk
 constexpr int kStageBytes = 2 * kRows * 128 * 4;  // double-buffered output staging (fp32 worst case)
@@ -55,6 +56,9 @@ struct TcArgs {
   int stg_off;           // byte offset of the output staging buffer in the drained stage area
   int out_vec_ok;        // output rows start on 16-byte boundaries
   int w_static;          // weight tiles may be requested before the previous kernel completes
+  int kc;                // 64-wide k-chunks per pipeline stage (one 3-D box each for W and X)
+  int tma3d;             // tensor maps are 3-D (64, rows, k/64): box {64, rows, kc}
+  uint32_t w_bytes;      // weight bytes per stage (MH x 128 rows x kc chunks)
   EpiArgs e;
   int* status;
 };
@@ -108,6 +112,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* st
       return false;
     }
   }
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
@@ -230,13 +241,20 @@ struct Epi {
     if constexpr (MODE == KVE_EPI_SILU_MUL) {
       const int odd = f_local & 1;
       T* col = b + (f_local >> 1);
+      // All exchanges first, then the arithmetic: the shuffles are warp-synchronous
+      // and would otherwise serialise the independent SwiGLU evaluations.
+      float gs[CNT / 2], us[CNT / 2];
 #pragma unroll
-      for (int j = 0; j < CNT; j += 2) {
-        const float recv = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[j + 1], 1);
-        const float g = rnd(odd ? recv : v[j]);
-        const float u = rnd(odd ? v[j + 1] : recv);
-        const int r = r0 + j + odd;
-        if (r < nr) col[r * W] = cvt(__fmul_rn(rnd(silu_ref(g)), u));
+      for (int i = 0; i < CNT / 2; ++i) {
+        const float recv = __shfl_xor_sync(0xffffffffu, odd ? v[2 * i] : v[2 * i + 1], 1);
+        gs[i] = rnd(odd ? recv : v[2 * i]);
+        us[i] = rnd(odd ? v[2 * i + 1] : recv);
+      }
+#pragma unroll
+      for (int i = 0; i < CNT / 2; ++i) {
+        const int r = r0 + 2 * i + odd;
+        const T y = cvt(__fmul_rn(rnd(silu_fast(gs[i])), us[i]));
+        if (r < nr) col[r * W] = y;
       }
     } else {
 #pragma unroll
@@ -324,7 +342,9 @@ __device__ __forceinline__ uint32_t map_to(uint32_t local, uint32_t rank) {
   return r;
 }
 
-template <int MODE, bool BF, int NG>
+// Rows of weights per CTA: MH halves of 128 (one MMA M-tile each) sharing the
+// activation tile, so each activation byte a CTA loads serves 128 * MH features.
+template <int MODE, bool BF, int NG, int MH>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, TcArgs a) {
   using E = Epi<MODE, BF>;
@@ -343,12 +363,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * a.mt;
-  const int feat0 = blockIdx.y * BM;
+  const int feat0 = blockIdx.y * BM * MH;
   const int split = blockIdx.z;
   const int kb0 = (int)((long long)split * a.k_blocks / a.splits);
   const int kb1 = (int)((long long)(split + 1) * a.k_blocks / a.splits);
+  const int n_stages_work = (kb1 - kb0 + a.kc - 1) / a.kc;  // pipeline stages of kc k-blocks
   uint32_t tmem_cols = 32;
-  while ((int)tmem_cols < a.mt) tmem_cols <<= 1;
+  while ((int)tmem_cols < MH * a.mt) tmem_cols <<= 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -375,15 +396,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   // requested before waiting on the previous kernel, so their latency overlaps
   // its tail. Their full barriers expect the bytes now and get the arrival (with
   // the activation bytes) once the activations may be read.
-  const int pre = a.w_static ? min(kb1 - kb0, a.stages) : 0;
+  // Stage layout: weights [kc][128 * MH rows][64] then, per token group,
+  // activations [kc][n_g rows][64]; every [rows][64] slab is one SW128 K-major tile.
+  auto load_w = [&](uint8_t* dst, int chunk, uint32_t fb) {
+    if (a.tma3d) tma_load_3d(smem_u32(dst), &map_w, 0, feat0, chunk, fb);
+    else tma_load_2d(smem_u32(dst), &map_w, chunk * BK, feat0, fb);
+  };
+  auto load_x = [&](uint8_t* dst, int chunk, uint32_t fb) {
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      uint8_t* d = dst + (size_t)g * a.kc * a.n_g * BK * 2;
+      if (a.tma3d) tma_load_3d(smem_u32(d), &map_x, 0, tok0 + g * a.n_g, chunk, fb);
+      else tma_load_2d(smem_u32(d), &map_x, chunk * BK, tok0 + g * a.n_g, fb);
+    }
+  };
+  const int pre = a.w_static ? min(n_stages_work, a.stages) : 0;
   if (warp == 0 && lane == 0) {
     prefetch_map(&map_w);
     prefetch_map(&map_x);
     uint8_t* sa = smem;
     for (int it = 0; it < pre; ++it, sa += a.stage_bytes) {
       const uint32_t fb = smem_u32(&full[it]);
-      mbar_add_tx(fb, BM * BK * 2);
-      tma_load_2d(smem_u32(sa), &map_w, (kb0 + it) * BK, feat0, fb);
+      mbar_add_tx(fb, a.w_bytes);
+      load_w(sa, kb0 + it * a.kc, fb);
     }
   }
   // Everything else touches global memory only after the previous kernel has
@@ -393,7 +428,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   // After a timeout anywhere in this launch, later CTAs skip their work instead
   // of each waiting out the limit again.
   const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
-  const int n_iter = aborted ? 0 : kb1 - kb0;
+  const int n_iter = aborted ? 0 : n_stages_work;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -401,21 +436,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       int issued = 0, s = 0;
       uint32_t ph = 0;
       uint8_t* sa = smem;
-      int kx = kb0 * BK;
+      int chunk = kb0;
       for (int it = 0; it < n_iter; ++it) {
         if (it >= a.stages && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, a.status)) break;
         const uint32_t fb = smem_u32(&full[s]);
         if (it < pre) {
-          mbar_expect_tx(fb, a.stage_bytes - BM * BK * 2);  // weight tile already requested
+          mbar_expect_tx(fb, a.stage_bytes - a.w_bytes);  // weight tile already requested
         } else {
           mbar_expect_tx(fb, a.stage_bytes);
-          tma_load_2d(smem_u32(sa), &map_w, kx, feat0, fb);
+          load_w(sa, chunk, fb);
         }
-        uint8_t* sb = sa + BM * BK * 2;
-        tma_load_2d(smem_u32(sb), &map_x, kx, tok0, fb);
-        if (NG == 2) tma_load_2d(smem_u32(sb + a.n_g * BK * 2), &map_x, kx, tok0 + a.n_g, fb);
+        load_x(sa + a.w_bytes, chunk, fb);
         ++issued;
-        kx += BK;
+        chunk += a.kc;
         if (++s == a.stages) {
           s = 0;
           ph ^= 1u;
@@ -441,25 +474,35 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     if (lane == 0) {
       const uint32_t idesc = umma_idesc(a.n_g);
       const uint64_t a0 = umma_desc(smem_u32(smem));
-      const uint64_t b0 = umma_desc(smem_u32(smem) + BM * BK * 2);
+      const uint64_t b0 = umma_desc(smem_u32(smem) + a.w_bytes);
       const uint64_t stage_step = (uint64_t)(a.stage_bytes >> 4);
-      const uint64_t grp_step = (uint64_t)((a.n_g * BK * 2) >> 4);
+      constexpr uint64_t half_step = (uint64_t)((BM * BK * 2) >> 4);             // next 128 weight rows
+      const uint64_t a_chunk = (uint64_t)((MH * BM * BK * 2) >> 4);              // next k-chunk of weights
+      const uint64_t b_chunk = (uint64_t)((a.n_g * BK * 2) >> 4);                // next k-chunk of a group
+      const uint64_t grp_step = (uint64_t)((a.kc * a.n_g * BK * 2) >> 4);        // next token group
       constexpr uint64_t kstep = (UMMA_K * 2) >> 4;  // 32 bytes along K
-      const uint32_t t1 = tmem_base + a.n_g;
       int s = 0;
       uint32_t ph = 0;
       uint64_t soff = 0;
+      int chunk = kb0;
       for (int it = 0; it < n_iter; ++it) {
         if (!mbar_wait(smem_u32(&full[s]), ph, a.status)) break;
         fence_after();
-        const uint64_t ad = a0 + soff, bd = b0 + soff;
-        umma_bf16(tmem_base, ad, bd, idesc, it > 0 ? 1u : 0u);
-        if (NG == 2) umma_bf16(t1, ad, bd + grp_step, idesc, it > 0 ? 1u : 0u);
+        const int nch = min(a.kc, kb1 - chunk);  // a partial last stage multiplies only real chunks
+        for (int j = 0; j < nch; ++j) {
+          const uint64_t ad = a0 + soff + j * a_chunk, bd = b0 + soff + j * b_chunk;
 #pragma unroll
-        for (int kk = 1; kk < BK / UMMA_K; ++kk) {
-          umma_bf16(tmem_base, ad + kk * kstep, bd + kk * kstep, idesc, 1u);
-          if (NG == 2) umma_bf16(t1, ad + kk * kstep, bd + grp_step + kk * kstep, idesc, 1u);
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint32_t acc = (it > 0 || j > 0 || kk > 0) ? 1u : 0u;
+#pragma unroll
+            for (int h = 0; h < MH; ++h)
+#pragma unroll
+              for (int g = 0; g < NG; ++g)
+                umma_bf16(tmem_base + h * a.mt + g * a.n_g, ad + h * half_step + kk * kstep,
+                          bd + g * grp_step + kk * kstep, idesc, acc);
+          }
         }
+        chunk += a.kc;
         umma_commit(smem_u32(&empty[s]));
         if (++s == a.stages) {
           s = 0;
@@ -476,16 +519,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
 
   // ---------------------------------------------------------------- epilogue
   // Epilogue warps 2.. own TMEM lane quarters (warp w reads lanes 32*(w%4) ...),
-  // i.e. feature rows; tokens are TMEM columns. Each warpgroup takes every
-  // kEpiGroups-th chunk of 32 tokens, stages it in a dense [32][W] buffer of its
-  // own (double-buffered) and writes it as whole rows.
+  // i.e. feature rows; tokens are TMEM columns. With one weight half (MH == 1)
+  // each warpgroup takes every kEpiGroups-th chunk of 32 tokens; with two, each
+  // warpgroup drains one half. A chunk is staged in a dense [32][W] buffer of the
+  // warpgroup's own (double-buffered) and written as whole rows.
+  static_assert(MH == 1 || MH == kEpiGroups, "one epilogue warpgroup per weight half");
   const bool epi = warp >= 2;
   const int egrp = epi ? (warp - 2) / 4 : 0;
+  const int half = MH == 1 ? 0 : egrp;
   const int quad = warp & 3;
   const int f_local = quad * 32 + lane;
-  const int feat = feat0 + f_local;
-  const int col0 = MODE == KVE_EPI_SILU_MUL ? feat0 / 2 : feat0;
-  const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);
+  const int fbase = feat0 + half * BM;  // first feature of this warpgroup's rows
+  const int feat = fbase + f_local;
+  const int col0 = MODE == KVE_EPI_SILU_MUL ? fbase / 2 : fbase;
+  const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * a.mt);
   const int etid = (threadIdx.x - 64) & 127;  // thread index within its warpgroup
   const float bias_f = (MODE == KVE_EPI_BIAS && epi && feat < a.n) ? a.e.bias[feat] : 0.f;
   bool have = false;
@@ -499,7 +546,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   if (S == 1) {
     if (epi) {
       int it = 0;
-      for (int c0 = egrp * kRows; c0 < a.mt; c0 += kEpiGroups * kRows, ++it) {
+      constexpr int kChunkStride = (MH == 1 ? kEpiGroups : 1) * kRows;
+      for (int c0 = MH == 1 ? egrp * kRows : 0; c0 < a.mt; c0 += kChunkStride, ++it) {
         const int n = min(kRows, a.mt - c0);
         uint8_t* buf = stg + (egrp * 2 + (it & 1)) * kStgBuf;
         uint4 res[E::NPASS];
@@ -634,30 +682,50 @@ int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int box_rows) {
   return KVE_OK;
 }
 
-inline int round16(int x) { return (x + 15) / 16 * 16; }
+// The same [rows, k] matrix as a 3-D tensor (64, rows, k / 64) whose third
+// dimension steps 128 bytes along k: one box {64, box_rows, kc} brings kc
+// consecutive 64-wide k-chunks, each landing as its own SW128 [box_rows][64]
+// tile. Needs k % 64 == 0 (a partial chunk would read the next row).
+int make_map3(CUtensorMap* map, const void* ptr, int rows, int k, int box_rows, int kc) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(KVE_ERR_CUDA, "kve_gemm: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)BK, (cuuint64_t)rows, (cuuint64_t)(k / BK)};
+  cuuint64_t strides[2] = {(cuuint64_t)k * 2, (cuuint64_t)BK * 2};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)kc};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(KVE_ERR_CUDA, "kve_gemm: cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return KVE_OK;
+}
 
 struct Plan {
   int mt, ng, n_g, token_tiles, feat_tiles, k_blocks, splits, stages, rch, stg_off;
-  uint32_t stage_bytes;
+  int mh, kc, tma3d;  // weight halves per CTA, k-chunks per stage, 3-D tensor maps
+  uint32_t stage_bytes, w_bytes;
 };
 
 typedef void (*GemmKernel)(CUtensorMap, CUtensorMap, TcArgs);
 
-template <int NG>
-GemmKernel kernel_for_ng(int mode, bool bf) {
+template <int NG, int MH>
+GemmKernel kernel_for_shape(int mode, bool bf) {
   switch (mode) {
-    case KVE_EPI_BIAS: return bf ? gemm_tc_kernel<KVE_EPI_BIAS, true, NG> : gemm_tc_kernel<KVE_EPI_BIAS, false, NG>;
+    case KVE_EPI_BIAS:
+      return bf ? gemm_tc_kernel<KVE_EPI_BIAS, true, NG, MH> : gemm_tc_kernel<KVE_EPI_BIAS, false, NG, MH>;
     case KVE_EPI_RESIDUAL:
-      return bf ? gemm_tc_kernel<KVE_EPI_RESIDUAL, true, NG> : gemm_tc_kernel<KVE_EPI_RESIDUAL, false, NG>;
+      return bf ? gemm_tc_kernel<KVE_EPI_RESIDUAL, true, NG, MH> : gemm_tc_kernel<KVE_EPI_RESIDUAL, false, NG, MH>;
     case KVE_EPI_SILU_MUL:
-      return bf ? gemm_tc_kernel<KVE_EPI_SILU_MUL, true, NG> : gemm_tc_kernel<KVE_EPI_SILU_MUL, false, NG>;
-    default: return bf ? gemm_tc_kernel<KVE_EPI_STORE, true, NG> : gemm_tc_kernel<KVE_EPI_STORE, false, NG>;
+      return bf ? gemm_tc_kernel<KVE_EPI_SILU_MUL, true, NG, MH> : gemm_tc_kernel<KVE_EPI_SILU_MUL, false, NG, MH>;
+    default: return bf ? gemm_tc_kernel<KVE_EPI_STORE, true, NG, MH> : gemm_tc_kernel<KVE_EPI_STORE, false, NG, MH>;
   }
 }
 
-GemmKernel kernel_for(int mode, int out_dtype, int ng) {
+// Token groups x weight halves: (1, 1), (2, 1) for tiles above 256 tokens, (1, 2).
+GemmKernel kernel_for(int mode, int out_dtype, int ng, int mh) {
   const bool bf = out_dtype == KVE_BF16;
-  return ng == 2 ? kernel_for_ng<2>(mode, bf) : kernel_for_ng<1>(mode, bf);
+  if (mh == 2) return kernel_for_shape<1, 2>(mode, bf);
+  return ng == 2 ? kernel_for_shape<2, 1>(mode, bf) : kernel_for_shape<1, 1>(mode, bf);
 }
 
 void configure_kernel() {
@@ -665,9 +733,9 @@ void configure_kernel() {
   std::call_once(once, [] {
     for (int mode = KVE_EPI_STORE; mode <= KVE_EPI_SILU_MUL; ++mode)
       for (int dt : {KVE_F32, KVE_BF16})
-        for (int ng : {1, 2})
-          cudaFuncSetAttribute(kernel_for(mode, dt, ng), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)(kSmemLimit - 512));
+        for (int shape = 0; shape < 3; ++shape)
+          cudaFuncSetAttribute(kernel_for(mode, dt, shape == 1 ? 2 : 1, shape == 2 ? 2 : 1),
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
   });
 }
 
@@ -694,7 +762,7 @@ const int* cluster_capacity() {
       cfg.attrs = &attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(KVE_EPI_STORE, KVE_BF16, 1), &cfg) == cudaSuccess && n > 0)
+      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(KVE_EPI_STORE, KVE_BF16, 1, 1), &cfg) == cudaSuccess && n > 0)
         cap[s] = n * s;
     }
     cudaGetLastError();
@@ -702,31 +770,49 @@ const int* cluster_capacity() {
   return cap;
 }
 
-// Launch-time model (microseconds) used to pick split-K and token tiling, fitted
-// to B200 measurements of this kernel. One CTA per SM streams k-blocks at a rate
-// set by its stage size (latency x bytes in flight); a cluster exchange costs a
-// fixed part plus a part per token of the CTA's tile.
-double kblock_us(int m_cta) { return 0.1 + (double)(BM + m_cta) * BK * 2 / 130000.0; }
-double exchange_us(int m_cta, int s) { return s > 1 ? 2.5 + 0.25 * s + 0.04 * m_cta : 0.0; }
-double epilogue_us(int m_cta) { return 1.0 + 0.01 * m_cta; }
-
-double model_us(int feat_tiles, int k_blocks, int s, int token_tiles, int m_cta) {
-  const int* cap = cluster_capacity();
-  const long long ctas = (long long)feat_tiles * token_tiles * s;
-  const long long waves = (ctas + cap[s] - 1) / cap[s];
-  return waves * (((k_blocks + s - 1) / s) * kblock_us(m_cta) + exchange_us(m_cta, s) + epilogue_us(m_cta));
+// Launch-time model (microseconds) used to pick split-K, token tiling, weight
+// halves per CTA and k-chunks per stage, fitted to B200 measurements of this
+// kernel and of TMA streaming alone:
+// * a pipeline stage costs the largest of its TMA issue time (about 0.12 us plus
+//   0.1 us per box and k-chunk), the load latency spread over the stages in
+//   flight, and its MMAs;
+// * a cluster exchange costs a fixed part plus a part per token of the tile;
+// * the epilogue costs a fixed part plus a part per token each warpgroup drains.
+constexpr double kLoadLatencyUs = 2.0;
+double stage_us(int mh, int ng, int mt, int kc) {
+  const size_t bytes = (size_t)(mh * BM + mt) * BK * 2 * kc;
+  int stages = (int)((kSmemLimit - 2048) / bytes);
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < 2) return 1e9;
+  const double issue = 0.12 + 0.10 * (1 + ng) * kc;
+  const double lat = kLoadLatencyUs / stages;
+  const double mma = (double)mh * BM * mt * BK * kc * 2 / (7.7e3 * 1.9e3);  // 7.7k flop/clk/SM at 1.9 GHz
+  return fmax(issue, fmax(lat, mma));
 }
+double exchange_us(int m_cta, int s) { return s > 1 ? 2.5 + 0.25 * s + 0.04 * m_cta : 0.0; }
+double epilogue_us(int tokens_per_group) { return 0.5 + 0.03 * tokens_per_group; }
 
-// Token tiling: tokens are cut into token_tiles tiles of n_g (ng == 1) or
-// 2 x n_g (ng == 2, up to 384 tokens) so that small feature counts still fill the
-// SMs. Splitting tokens never changes a row's reduction order.
-struct TokenTiling {
-  int token_tiles, ng, n_g;
+inline int round16(int x) { return (x + 15) / 16 * 16; }
+
+// One launch shape: token_tiles tiles of ng x n_g tokens, mh weight halves of
+// 128 rows per CTA, kc k-chunks of 64 per pipeline stage.
+struct TileConfig {
+  int token_tiles, ng, n_g, mh, kc;
   double us;
 };
 
-TokenTiling tiling_for(int m, int t) {
-  TokenTiling tt{};
+double config_us(int feat_tiles, int k_blocks, int s, const TileConfig& c) {
+  const int* cap = cluster_capacity();
+  const long long ctas = (long long)((feat_tiles + c.mh - 1) / c.mh) * c.token_tiles * s;
+  const long long waves = (ctas + cap[s] - 1) / cap[s];
+  const int mt = c.ng * c.n_g;
+  const int iters = ((k_blocks + s - 1) / s + c.kc - 1) / c.kc;
+  const int per_group = c.mh == 1 ? (mt + kEpiGroups - 1) / kEpiGroups : mt;
+  return waves * (iters * stage_us(c.mh, c.ng, mt, c.kc) + exchange_us(mt, s) + epilogue_us(per_group));
+}
+
+TileConfig token_tiling(int m, int t) {
+  TileConfig tt{};
   const int per = (m + t - 1) / t;
   tt.token_tiles = t;
   if (per <= kMaxNG) {
@@ -736,36 +822,52 @@ TokenTiling tiling_for(int m, int t) {
     tt.ng = 2;
     tt.n_g = round16((per + 1) / 2);
   }
+  tt.mh = 1;
+  tt.kc = 1;
   return tt;
 }
 
-// Fewest token tiles that keep every tile within 384 tokens, then more while the
-// model gains clearly.
-TokenTiling best_tiling(int m, int feat_tiles, int k_blocks, int s) {
+// The cheapest token tiling by the model, preferring fewer tiles unless more
+// are clearly faster. Each tiling takes the most k-chunks per stage that still
+// leave two pipeline stages (fewer, larger TMA boxes measured faster than more
+// stages in flight); several k-chunks are single-split shapes on the 3-D maps
+// (k % 64 == 0). Two weight halves per CTA measured no faster on B200 and are
+// left to kve_gemm_force_shape. None of these choices changes a row's reduction
+// order.
+int chunks_for(int mt, int s, bool tma3d) {
+  if (s > 1 || !tma3d) return 1;
+  for (int kc = 4; kc > 1; kc /= 2)
+    if ((size_t)(BM + mt) * BK * 2 * kc * 2 <= kSmemLimit - 2048) return kc;
+  return 1;
+}
+
+TileConfig best_config(int m, int feat_tiles, int k_blocks, int s, bool tma3d) {
   int t_min = (m + 383) / 384;
   if (t_min < 1) t_min = 1;
-  TokenTiling best = tiling_for(m, t_min);
+  TileConfig best = token_tiling(m, t_min);
   best.us = 1e30;
   for (int t = t_min; t <= (m + 15) / 16; ++t) {
-    TokenTiling tt = tiling_for(m, t);
-    const int m_cta = tt.ng * tt.n_g;
-    if ((long long)(t - 1) * m_cta >= m) continue;  // an empty trailing tile
-    tt.us = model_us(feat_tiles, k_blocks, s, t, m_cta);
-    if (tt.us < best.us * 0.97) best = tt;
+    TileConfig c = token_tiling(m, t);
+    const int mt = c.ng * c.n_g;
+    if ((long long)(t - 1) * mt >= m) continue;  // an empty trailing tile
+    c.mh = 1;
+    c.kc = chunks_for(mt, s, tma3d);
+    c.us = config_us(feat_tiles, k_blocks, s, c);
+    if (c.us < best.us * 0.97) best = c;
   }
   return best;
 }
 
 // Split-K factor: a function of (n, k) only, so a row's reduction order never
 // depends on how many tokens are in the batch. It minimises the modelled time
-// summed over small, medium and large batches, each with its best token tiling.
-int choose_splits(int feat_tiles, int k_blocks) {
+// summed over small, medium and large batches, each with its best shape.
+int choose_splits(int feat_tiles, int k_blocks, bool tma3d) {
   int best = 1;
   double best_t = 1e30;
   for (int s = 1; s <= kMaxSplits; ++s) {
     if (s > 1 && k_blocks / s < 2) break;
     double t = 0;
-    for (int m_ref : {16, 64, 256}) t += best_tiling(m_ref, feat_tiles, k_blocks, s).us;
+    for (int m_ref : {16, 64, 256}) t += best_config(m_ref, feat_tiles, k_blocks, s, tma3d).us;
     if (t < best_t - 1e-9) {
       best_t = t;
       best = s;
@@ -774,17 +876,43 @@ int choose_splits(int feat_tiles, int k_blocks) {
   return best;
 }
 
+// Shape forced through kve_gemm_force_shape (0 = the model's choice).
+std::atomic<int> g_force_t{0}, g_force_mh{0}, g_force_kc{0};
+
 Plan make_plan_uncached(int m, int n, int k) {
   Plan p{};
   p.feat_tiles = (n + BM - 1) / BM;
   p.k_blocks = (k + BK - 1) / BK;
-  p.splits = choose_splits(p.feat_tiles, p.k_blocks);
-  const TokenTiling tt = best_tiling(m, p.feat_tiles, p.k_blocks, p.splits);
-  p.token_tiles = tt.token_tiles;
-  p.ng = tt.ng;
-  p.n_g = tt.n_g;
+  p.tma3d = k % BK == 0;
+  p.splits = choose_splits(p.feat_tiles, p.k_blocks, p.tma3d);
+  TileConfig c = best_config(m, p.feat_tiles, p.k_blocks, p.splits, p.tma3d);
+  // A forced shape applies where it is valid for this GEMM; it never touches the
+  // split factor, so results are the same bits either way.
+  const int ft = g_force_t.load(), fmh = g_force_mh.load(), fkc = g_force_kc.load();
+  if (ft > 0) {
+    TileConfig f = token_tiling(m, ft < (m + 15) / 16 ? ft : (m + 15) / 16);
+    f.mh = c.mh;
+    f.kc = c.kc;
+    if (f.ng == 2 || (long long)f.ng * f.n_g > 256) f.mh = 1;
+    c = f;
+  }
+  if (fmh == 1) c.mh = 1;
+  if (fmh == 2 && p.splits == 1 && c.ng == 1 && c.n_g <= 256 && p.feat_tiles >= 2) c.mh = 2;
+  if (fkc > 0 && (fkc == 1 || (p.splits == 1 && p.tma3d))) c.kc = fkc;
+  // ... and is shrunk until two pipeline stages fit in shared memory.
+  auto fits = [&](const TileConfig& t) {
+    return (size_t)(t.mh * BM + t.ng * t.n_g) * BK * 2 * t.kc * 2 <= kSmemLimit - 2048;
+  };
+  while (!fits(c) && c.kc > 1) c.kc /= 2;
+  if (!fits(c)) c.mh = 1;
+  p.token_tiles = c.token_tiles;
+  p.ng = c.ng;
+  p.n_g = c.n_g;
+  p.mh = c.mh;
+  p.kc = c.kc;
   p.mt = p.ng * p.n_g;
-  p.stage_bytes = (uint32_t)(BM * BK * 2 + p.mt * BK * 2);
+  p.w_bytes = (uint32_t)(p.mh * BM * BK * 2 * p.kc);
+  p.stage_bytes = (uint32_t)(p.w_bytes + p.mt * BK * 2 * p.kc);
   size_t avail = kSmemLimit - 2048 /*align slack + barriers + margin*/;
   p.stages = (int)(avail / p.stage_bytes);
   if (p.stages > kMaxStages) p.stages = kMaxStages;
@@ -811,9 +939,12 @@ Plan make_plan_uncached(int m, int n, int k) {
 
 // Plans are cached per (m, n, k): a forward pass asks for the same few shapes on
 // every layer.
+std::mutex g_plan_mu;
+std::unordered_map<uint64_t, Plan> g_plan_cache;
+
 Plan make_plan(int m, int n, int k) {
-  static std::mutex mu;
-  static std::unordered_map<uint64_t, Plan> cache;
+  std::mutex& mu = g_plan_mu;
+  std::unordered_map<uint64_t, Plan>& cache = g_plan_cache;
   const bool key_ok = m < (1 << 20) && n < (1 << 24) && k < (1 << 20);
   const uint64_t key = ((uint64_t)m << 44) | ((uint64_t)n << 20) | (uint64_t)k;
   if (key_ok) {
@@ -850,20 +981,22 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   a.splits = p.splits; a.stages = p.stages; a.stage_bytes = p.stage_bytes; a.e = e; a.status = status;
   a.rch = p.rch; a.stg_off = p.stg_off;
   a.w_static = e.w_static;
+  a.kc = p.kc; a.tma3d = p.tma3d; a.w_bytes = p.w_bytes;
   const int es = e.out_dtype == KVE_BF16 ? 2 : 4;
   a.out_vec_ok = ((uintptr_t)e.out % 16 == 0) && ((size_t)e.ld_out * es % 16 == 0) &&
                  (e.mode != KVE_EPI_RESIDUAL || (uintptr_t)e.residual % 16 == 0);
   CUtensorMap mw, mx;
-  int rc = make_map(&mw, w, n, k, BM);
+  int rc = p.tma3d ? make_map3(&mw, w, n, k, BM * p.mh, p.kc) : make_map(&mw, w, n, k, BM * p.mh);
   if (rc) return rc;
-  rc = make_map(&mx, x, m, k, p.n_g);
+  rc = p.tma3d ? make_map3(&mx, x, m, k, p.n_g, p.kc) : make_map(&mx, x, m, k, p.n_g);
   if (rc) return rc;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
   attr.val.clusterDim.x = 1;
   attr.val.clusterDim.y = 1;
   attr.val.clusterDim.z = p.splits;
-  cudaError_t err = launch_kernel_ex(kernel_for(e.mode, e.out_dtype, p.ng), dim3(p.token_tiles, p.feat_tiles, p.splits),
+  cudaError_t err = launch_kernel_ex(kernel_for(e.mode, e.out_dtype, p.ng, p.mh),
+                                     dim3(p.token_tiles, (p.feat_tiles + p.mh - 1) / p.mh, p.splits),
                                      dim3(kThreads), (size_t)p.stages * p.stage_bytes + 1024 + 512, stream, &attr,
                                      p.splits > 1 ? 1 : 0, mw, mx, a);
   if (err != cudaSuccess) {
@@ -875,3 +1008,26 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
 }
 
 }  // namespace kve
+
+extern "C" int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_chunks) {
+  using namespace kve;
+  if (token_tiles < 0 || weight_halves < 0 || weight_halves > 2 ||
+      !(k_chunks == 0 || k_chunks == 1 || k_chunks == 2 || k_chunks == 4))
+    return set_error(KVE_ERR_ARG, "kve_gemm_force_shape: token_tiles >= 0, weight_halves in 0..2, k_chunks in 0,1,2,4");
+  std::lock_guard<std::mutex> g(g_plan_mu);
+  g_force_t.store(token_tiles);
+  g_force_mh.store(weight_halves);
+  g_force_kc.store(k_chunks);
+  g_plan_cache.clear();
+  return KVE_OK;
+}
+
+extern "C" int kve_gemm_plan_info(int m, int n, int k, int* out) {
+  using namespace kve;
+  if (m < 1 || n < 1 || k < 1 || !out) return set_error(KVE_ERR_ARG, "kve_gemm_plan_info: bad arguments");
+  const Plan p = make_plan(m, n, k);
+  const int v[9] = {p.splits, p.token_tiles, p.ng, p.n_g, p.mh, p.kc, p.stages, p.tma3d,
+                    (p.feat_tiles + p.mh - 1) / p.mh};
+  for (int i = 0; i < 9; ++i) out[i] = v[i];
+  return KVE_OK;
+}

@@ -394,6 +394,38 @@ def test_gemm_rows_are_batch_invariant(cuda_device, algo, dt):
         assert torch.equal(shifted, full[3:8])
 
 
+@pytest.mark.gpu
+def test_gemm_launch_shapes_give_identical_bits(cuda_device):
+    """Token tiles, weight halves per CTA and k-chunks per pipeline stage change
+    speed only: every forced shape reproduces the model-chosen result exactly."""
+    lib = L.load()
+    g = torch.Generator(device=cuda_device).manual_seed(11)
+    cases = [(320, 2560, 2048, L.EPI_BIAS), (64, 9728, 896, L.EPI_SILU_MUL), (320, 4096, 2048, L.EPI_SILU_MUL),
+             (300, 1000, 136, L.EPI_STORE), (64, 896, 4864, L.EPI_RESIDUAL), (17, 512, 256, L.EPI_STORE),
+             (160, 1024, 512, L.EPI_RESIDUAL)]
+    shapes = [(1, 1, 1), (1, 2, 1), (2, 2, 2), (4, 1, 4), (3, 2, 4), (7, 1, 2), (2, 1, 2)]
+    try:
+        for m, n, k, epi in cases:
+            x = torch.randn(m, k, device=cuda_device, generator=g).to(torch.bfloat16)
+            w = (torch.randn(n, k, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+            n_out = n // 2 if epi == L.EPI_SILU_MUL else n
+            bias = torch.randn(n, device=cuda_device, generator=g) if epi == L.EPI_BIAS else None
+            res0 = torch.randn(m, n_out, device=cuda_device, generator=g).to(torch.bfloat16)
+
+            def run():
+                out = res0.clone() if epi == L.EPI_RESIDUAL else None
+                return ops.gemm(x, w, epilogue=epi, bias=bias, residual=out, out=out)
+
+            L.check(lib.kve_gemm_force_shape(0, 0, 0))
+            ref = run()
+            for t, mh, kc in shapes:
+                L.check(lib.kve_gemm_force_shape(t, mh, kc))
+                got = run()
+                assert torch.equal(got, ref), (m, n, k, epi, t, mh, kc)
+    finally:
+        L.check(lib.kve_gemm_force_shape(0, 0, 0))
+
+
 def test_gemm_repeatable_and_no_workspace(cuda_device):
     """Split-K partials are reduced in cluster shared memory: no workspace, identical repeats."""
     x = torch.randn(320, 2048, device=cuda_device).to(torch.bfloat16)
