@@ -49,15 +49,35 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
   const int64_t num_slots = m->num_blocks * m->block_size;
   const float scale = 1.0f / sqrtf((float)m->head_dim);
 
+  // The fused qkv epilogue needs bf16, 16-byte aligned outputs and heads that
+  // tile 128-feature blocks; otherwise the projection and the RoPE append run apart.
+  const int hd = m->head_dim;
+  const bool fused_qkv = dt == KVE_BF16 && hd % 8 == 0 && 128 % hd == 0 && m->rope_len > 0 &&
+                         (uintptr_t)s->q % 16 == 0 && (uintptr_t)m->rope_cos % 16 == 0 &&
+                         (uintptr_t)m->rope_sin % 16 == 0;
+
   KVE_TRY(kve_embed(b->ids, M, m->embed, dt, H, m->vocab, s->hidden, s->dev_status, stream));
   for (int l = 0; l < m->num_layers; ++l) {
     const kve_layer_t& L = m->layers[l];
     KVE_TRY(kve_rmsnorm(s->hidden, dt, L.ln1, M, H, m->rms_eps, nullptr, s->normed, stream));
-    KVE_TRY(gemm_run(s->normed, L.w_qkv, dt, M, qkv, H, KVE_EPI_BIAS, L.b_qkv, nullptr, s->qkv, dt,
-                     s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
-    KVE_TRY(kve_qkv_rope_append(s->qkv, dt, M, m->num_heads, m->num_kv_heads, m->head_dim, b->positions,
-                                b->slots, m->rope_cos, m->rope_sin, m->rope_len, s->q, L.pool_k, L.pool_v,
-                                num_slots, s->dev_status, stream));
+    if (fused_qkv) {
+      // bf16: projection, bias, RoPE and the K/V append in one kernel.
+      EpiArgs e{};
+      e.bias = L.b_qkv;
+      e.w_static = 1;
+      e.nq = m->num_heads; e.nkv = m->num_kv_heads; e.hd = m->head_dim;
+      e.positions = b->positions; e.slots = b->slots;
+      e.rope_cos = m->rope_cos; e.rope_sin = m->rope_sin; e.rope_len = m->rope_len;
+      e.q_out = s->q; e.pool_k = L.pool_k; e.pool_v = L.pool_v; e.num_slots = num_slots;
+      e.status = s->dev_status;
+      KVE_TRY(gemm_qkv_rope(s->normed, L.w_qkv, M, qkv, H, e, stream));
+    } else {
+      KVE_TRY(gemm_run(s->normed, L.w_qkv, dt, M, qkv, H, KVE_EPI_BIAS, L.b_qkv, nullptr, s->qkv, dt,
+                       s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
+      KVE_TRY(kve_qkv_rope_append(s->qkv, dt, M, m->num_heads, m->num_kv_heads, m->head_dim, b->positions,
+                                  b->slots, m->rope_cos, m->rope_sin, m->rope_len, s->q, L.pool_k, L.pool_v,
+                                  num_slots, s->dev_status, stream));
+    }
     KVE_TRY(paged_attn_run(s->q, dt, L.pool_k, L.pool_v, b->block_tables, b->table_stride, b->ctx_lens,
                                   b->q_lens, b->q_offsets, b->n_seqs, b->max_q_len, b->max_ctx, m->num_heads,
                                   m->num_kv_heads, m->head_dim, m->block_size, m->num_blocks, scale, s->attn,

@@ -18,7 +18,24 @@ struct EpiArgs {
   const void* residual;  // [m, n] in out_dtype (RESIDUAL); may alias out
   void* out;
   int w_static;       // w is written by no kernel that may still run: its loads may start early
+  // kEpiQkvRope only: the qkv projection's output goes straight to its consumers.
+  int nq, nkv, hd;
+  const int32_t* positions;  // [m]
+  const int32_t* slots;      // [m] pool slot of each token's K/V
+  const float* rope_cos;     // [rope_len, hd / 2]
+  const float* rope_sin;
+  int rope_len;
+  void* q_out;               // [m, nq * hd]
+  void* pool_k;              // [num_slots, nkv * hd]
+  void* pool_v;
+  int64_t num_slots;
+  int* status;
 };
+
+// Internal epilogue of the tcgen05 GEMM (not in the C ABI): bias, bf16 rounding,
+// RoPE of the q and k heads, q to q_out, k and v to their pool slots - the
+// qkv projection and kve_qkv_rope_append in one pass.
+constexpr int kEpiQkvRope = KVE_EPI_SILU_MUL + 1;
 
 __device__ __forceinline__ float round_to(int dtype, float v) {
   return dtype == KVE_BF16 ? Elem<__nv_bfloat16>::round(v) : v;
@@ -77,5 +94,9 @@ size_t gemm_tc_workspace_bytes(int m, int n, int k);
 int gemm_run(const void* x, const void* w, int dtype, int m, int n, int k, int epilogue, const float* bias,
              const void* residual, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
              int* dev_status, int algo, bool w_static, cudaStream_t stream);
+
+// The fused qkv projection of one layer (bf16): x [m, k] times w_qkv [n, k]^T
+// plus bias, then the work of kve_qkv_rope_append. `e` carries the rope fields.
+int gemm_qkv_rope(const void* x, const void* w, int m, int n, int k, const EpiArgs& e, cudaStream_t stream);
 
 }  // namespace kve

@@ -261,7 +261,7 @@ struct Epi {
       for (int j = 0; j < CNT; ++j) {
         const int r = r0 + j;
         if (r < nr) {
-          if constexpr (MODE == KVE_EPI_BIAS) b[r * W + f_local] = cvt(__fadd_rn(v[j], bias_f));
+          if constexpr (MODE == KVE_EPI_BIAS || MODE == kEpiQkvRope) b[r * W + f_local] = cvt(__fadd_rn(v[j], bias_f));
           else b[r * W + f_local] = cvt(v[j]);  // RESIDUAL adds the residual while copying out
         }
       }
@@ -294,6 +294,64 @@ struct Epi {
   // etid always handles the same column vector; RPP rows per pass.
   static __device__ __forceinline__ void copy_out(const TcArgs& a, const uint8_t* buf, int tok_base, int nr,
                                                   int col0, int etid, const uint4 (&res)[NPASS]) {
+    if constexpr (MODE == kEpiQkvRope) {
+      // The staged row holds round(acc + bias) for features col0 .. col0 + 127.
+      // A 16-byte vector (8 features) never straddles a head (hd % 8 == 0) and a
+      // head never straddles a tile (128 % hd == 0), so the RoPE partner vector
+      // (d +- hd/2) is in the same staged row.
+      const int c = (etid % VPR) * VE;
+      const int r_first = etid / VPR;
+      const int f = col0 + c;
+      if (f >= a.n) return;
+      const int hd = a.e.hd, half = hd >> 1;
+      const int q_end = a.e.nq * hd, rot_end = (a.e.nq + a.e.nkv) * hd, kv_w = a.e.nkv * hd;
+      const int d = f % hd;
+      const bool rot = f < rot_end, lo = d < half;
+      const int dd = lo ? d : d - half;
+      const int cp = lo ? c + half : c - half;
+#pragma unroll
+      for (int i = 0; i < NPASS; ++i) {
+        const int r = r_first + i * RPP;
+        const int t = tok_base + r;
+        if (r >= nr || t >= a.m) break;
+        const T* srow = reinterpret_cast<const T*>(buf) + r * W;
+        uint4 val = *reinterpret_cast<const uint4*>(srow + c);
+        if (rot) {
+          int pos = a.e.positions[t];
+          if (pos < 0 || pos >= a.e.rope_len) {
+            report(a.e.status, KVE_ERR_BOUNDS);
+            pos = 0;
+          }
+          const float4* cs = reinterpret_cast<const float4*>(a.e.rope_cos + (size_t)pos * half + dd);
+          const float4* sn = reinterpret_cast<const float4*>(a.e.rope_sin + (size_t)pos * half + dd);
+          const float4 c0 = cs[0], c1 = cs[1], s0 = sn[0], s1 = sn[1];
+          const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+          const uint4 pv = *reinterpret_cast<const uint4*>(srow + cp);
+          T* y = reinterpret_cast<T*>(&val);
+          const T* o = reinterpret_cast<const T*>(&pv);
+#pragma unroll
+          for (int e = 0; e < VE; ++e) {
+            const float self = (float)y[e], other = (float)o[e];
+            y[e] = cvt(lo ? rope_first<T>(self, other, cv[e], sv[e]) : rope_second<T>(other, self, cv[e], sv[e]));
+          }
+        }
+        T* dst;
+        if (f < q_end) {
+          dst = static_cast<T*>(a.e.q_out) + (size_t)t * q_end + f;
+        } else {
+          const int64_t slot = a.e.slots[t];
+          if (slot < 0 || slot >= a.e.num_slots) {
+            report(a.e.status, KVE_ERR_BOUNDS);
+            continue;
+          }
+          dst = rot ? static_cast<T*>(a.e.pool_k) + slot * kv_w + (f - q_end)
+                    : static_cast<T*>(a.e.pool_v) + slot * kv_w + (f - rot_end);
+        }
+        *reinterpret_cast<uint4*>(dst) = val;
+      }
+      return;
+    } else {
     const int nvalid = min(W, a.e.ld_out - col0);
     const int c = (etid % VPR) * VE;
     const int r_first = etid / VPR;
@@ -325,6 +383,7 @@ struct Epi {
           dst[j] = cvt(y);
         }
       }
+    }
     }
   }
 };
@@ -534,7 +593,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   const int col0 = MODE == KVE_EPI_SILU_MUL ? fbase / 2 : fbase;
   const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * a.mt);
   const int etid = (threadIdx.x - 64) & 127;  // thread index within its warpgroup
-  const float bias_f = (MODE == KVE_EPI_BIAS && epi && feat < a.n) ? a.e.bias[feat] : 0.f;
+  const float bias_f = ((MODE == KVE_EPI_BIAS || MODE == kEpiQkvRope) && epi && feat < a.n) ? a.e.bias[feat] : 0.f;
   bool have = false;
   if (epi) {
     have = !aborted && mbar_wait(smem_u32(tmem_full), 0, a.status);
@@ -717,6 +776,7 @@ GemmKernel kernel_for_shape(int mode, bool bf) {
       return bf ? gemm_tc_kernel<KVE_EPI_RESIDUAL, true, NG, MH> : gemm_tc_kernel<KVE_EPI_RESIDUAL, false, NG, MH>;
     case KVE_EPI_SILU_MUL:
       return bf ? gemm_tc_kernel<KVE_EPI_SILU_MUL, true, NG, MH> : gemm_tc_kernel<KVE_EPI_SILU_MUL, false, NG, MH>;
+    case kEpiQkvRope: return bf ? gemm_tc_kernel<kEpiQkvRope, true, NG, MH> : nullptr;  // bf16 only
     default: return bf ? gemm_tc_kernel<KVE_EPI_STORE, true, NG, MH> : gemm_tc_kernel<KVE_EPI_STORE, false, NG, MH>;
   }
 }
@@ -731,11 +791,12 @@ GemmKernel kernel_for(int mode, int out_dtype, int ng, int mh) {
 void configure_kernel() {
   static std::once_flag once;
   std::call_once(once, [] {
-    for (int mode = KVE_EPI_STORE; mode <= KVE_EPI_SILU_MUL; ++mode)
+    for (int mode = KVE_EPI_STORE; mode <= kEpiQkvRope; ++mode)
       for (int dt : {KVE_F32, KVE_BF16})
-        for (int shape = 0; shape < 3; ++shape)
-          cudaFuncSetAttribute(kernel_for(mode, dt, shape == 1 ? 2 : 1, shape == 2 ? 2 : 1),
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
+        for (int shape = 0; shape < 3; ++shape) {
+          GemmKernel kern = kernel_for(mode, dt, shape == 1 ? 2 : 1, shape == 2 ? 2 : 1);
+          if (kern) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
+        }
   });
 }
 
@@ -985,6 +1046,8 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   const int es = e.out_dtype == KVE_BF16 ? 2 : 4;
   a.out_vec_ok = ((uintptr_t)e.out % 16 == 0) && ((size_t)e.ld_out * es % 16 == 0) &&
                  (e.mode != KVE_EPI_RESIDUAL || (uintptr_t)e.residual % 16 == 0);
+  GemmKernel kern = kernel_for(e.mode, e.out_dtype, p.ng, p.mh);
+  if (!kern) return set_error(KVE_ERR_DTYPE, "kve_gemm(tcgen05): epilogue %d needs bf16 output", e.mode);
   CUtensorMap mw, mx;
   int rc = p.tma3d ? make_map3(&mw, w, n, k, BM * p.mh, p.kc) : make_map(&mw, w, n, k, BM * p.mh);
   if (rc) return rc;
@@ -995,7 +1058,7 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   attr.val.clusterDim.x = 1;
   attr.val.clusterDim.y = 1;
   attr.val.clusterDim.z = p.splits;
-  cudaError_t err = launch_kernel_ex(kernel_for(e.mode, e.out_dtype, p.ng, p.mh),
+  cudaError_t err = launch_kernel_ex(kern,
                                      dim3(p.token_tiles, (p.feat_tiles + p.mh - 1) / p.mh, p.splits),
                                      dim3(kThreads), (size_t)p.stages * p.stage_bytes + 1024 + 512, stream, &attr,
                                      p.splits > 1 ? 1 : 0, mw, mx, a);
@@ -1005,6 +1068,21 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
     return set_error(KVE_ERR_CUDA, "kve_gemm(tcgen05): launch failed: %s", cudaGetErrorString(err));
   }
   return check_launch("kve_gemm(tcgen05)");
+}
+
+int gemm_qkv_rope(const void* x, const void* w, int m, int n, int k, const EpiArgs& e_in, cudaStream_t stream) {
+  EpiArgs e = e_in;
+  e.mode = kEpiQkvRope;
+  e.out_dtype = KVE_BF16;
+  e.out = e.q_out;
+  e.ld_out = n;
+  if (e.hd < 8 || e.hd % 8 || 128 % e.hd || n != (e.nq + 2 * e.nkv) * e.hd || !e.bias || !e.positions ||
+      !e.slots || !e.rope_cos || !e.rope_sin || !e.q_out || !e.pool_k || !e.pool_v)
+    return set_error(KVE_ERR_ARG, "gemm_qkv_rope: bad head layout or null pointer");
+  const void* ptrs[5] = {e.q_out, e.pool_k, e.pool_v, e.rope_cos, e.rope_sin};
+  for (const void* q : ptrs)
+    if ((uintptr_t)q % 16) return set_error(KVE_ERR_ARG, "gemm_qkv_rope: pointers must be 16-byte aligned");
+  return gemm_tc(x, w, m, n, k, e, nullptr, 0, e.status, stream);
 }
 
 }  // namespace kve

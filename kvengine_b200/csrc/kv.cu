@@ -34,16 +34,8 @@ __global__ void kv_append_kernel(const uint4* __restrict__ k_new, const uint4* _
 // CTA per token. Rotate-half pairing (d, d + hd/2) exactly as
 // kvengine/forward.py:49-69; cos/sin are rounded to the model dtype first and
 // every product/sum is rounded like the reference's elementwise torch ops.
-template <typename T>
-__device__ __forceinline__ void rope_pair(float x1, float x2, float c, float s, T* o1, T* o2) {
-  float cb = Elem<T>::round(c), sb = Elem<T>::round(s);
-  float a = Elem<T>::round(__fmul_rn(x1, cb));
-  float b = Elem<T>::round(__fmul_rn(-x2, sb));
-  float e = Elem<T>::round(__fmul_rn(x2, cb));
-  float f = Elem<T>::round(__fmul_rn(x1, sb));
-  *o1 = Elem<T>::from_f(__fadd_rn(a, b));
-  *o2 = Elem<T>::from_f(__fadd_rn(e, f));
-}
+// rope_pair (kve_common.cuh) is the rotation itself, shared with the fused
+// qkv GEMM epilogue.
 
 template <typename T>
 __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int nq, int nkv, int hd,

@@ -44,6 +44,25 @@ template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 };
 
+// Rotate-half RoPE of one pair (x1 = element d, x2 = element d + hd/2), as
+// kvengine/forward.py:49-69 computes it in the model dtype: cos/sin rounded to
+// the dtype first, every product and the sum rounded like elementwise torch ops.
+template <typename T>
+__device__ __forceinline__ float rope_first(float x1, float x2, float c, float s) {
+  const float cb = Elem<T>::round(c), sb = Elem<T>::round(s);
+  return __fadd_rn(Elem<T>::round(__fmul_rn(x1, cb)), Elem<T>::round(__fmul_rn(-x2, sb)));
+}
+template <typename T>
+__device__ __forceinline__ float rope_second(float x1, float x2, float c, float s) {
+  const float cb = Elem<T>::round(c), sb = Elem<T>::round(s);
+  return __fadd_rn(Elem<T>::round(__fmul_rn(x2, cb)), Elem<T>::round(__fmul_rn(x1, sb)));
+}
+template <typename T>
+__device__ __forceinline__ void rope_pair(float x1, float x2, float c, float s, T* o1, T* o2) {
+  *o1 = Elem<T>::from_f(rope_first<T>(x1, x2, c, s));
+  *o2 = Elem<T>::from_f(rope_second<T>(x1, x2, c, s));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
