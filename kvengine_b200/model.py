@@ -98,29 +98,37 @@ class ForwardPlan:
     offsets: dict = field(init=False)
 
     def __post_init__(self):
-        S = len(self.seqs)
+        seqs = self.seqs
+        S = len(seqs)
         bs = self.block_size
-        q = np.array([s.q_len for s in self.seqs], dtype=np.int64)
-        start = np.array([s.start for s in self.seqs], dtype=np.int64)
+        q = np.fromiter((s.q_len for s in seqs), dtype=np.int64, count=S)
+        start = np.fromiter((s.start for s in seqs), dtype=np.int64, count=S)
+        n_out = np.fromiter((s.n_out for s in seqs), dtype=np.int64, count=S)
+        nblk = np.fromiter((len(s.blocks) for s in seqs), dtype=np.int64, count=S)
         M = int(q.sum())
         self.n_tokens = M
         self.max_q_len = int(q.max()) if S else 0
         ctx = start + q
         self.max_ctx = int(ctx.max()) if S else 0
-        self.width = max(1, max((len(s.blocks) for s in self.seqs), default=1))
+        if S and bool((nblk * bs < ctx).any()):
+            raise ValueError("block table does not cover the sequence (reserve first)")
+        width = self.width = max(1, int(nblk.max()) if S else 1)
         q_off = np.zeros(S + 1, dtype=np.int64)
         np.cumsum(q, out=q_off[1:])
         seq_of_tok = np.repeat(np.arange(S), q)
         pos = (np.arange(M) - q_off[:-1][seq_of_tok]) + start[seq_of_tok]
-        tables = np.zeros((S, self.width), dtype=np.int64)
-        for i, s in enumerate(self.seqs):
-            if len(s.blocks) * bs < s.start + s.q_len:
-                raise ValueError("block table does not cover the sequence (reserve first)")
-            tables[i, : len(s.blocks)] = s.blocks
+        # [S, width] block table, zero-padded
+        tables = np.zeros((S, width), dtype=np.int64)
+        if S:
+            flat = np.fromiter((b for s in seqs for b in s.blocks), dtype=np.int64, count=int(nblk.sum()))
+            row = np.repeat(np.arange(S), nblk)
+            col = np.arange(flat.shape[0]) - np.repeat(np.cumsum(nblk) - nblk, nblk)
+            tables[row, col] = flat
         slots = tables[seq_of_tok, pos // bs] * bs + pos % bs
-        out_rows = np.concatenate([np.arange(q_off[i + 1] - s.n_out, q_off[i + 1])
-                                   for i, s in enumerate(self.seqs)]) if S else np.zeros(0, np.int64)
-        self.n_out = int(out_rows.shape[0])
+        # logits rows: the last n_out rows of every sequence
+        n_tot = int(n_out.sum())
+        out_rows = np.repeat(q_off[1:] - n_out, n_out) + (np.arange(n_tot) - np.repeat(np.cumsum(n_out) - n_out, n_out))
+        self.n_out = n_tot
         parts = {"positions": pos, "slots": slots, "q_lens": q, "q_offsets": q_off, "ctx_lens": ctx,
                  "out_rows": out_rows, "tables": tables.reshape(-1)}
         self.offsets = {}

@@ -103,6 +103,7 @@ class SpecEngine:
         self.V = self.target.cfg.vocab_size
         self._cap = 0
         self.stats = {"iterations": 0, "verify_rows": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+        self._pinned: list[torch.Tensor | None] = []
         # When a list, every verify pass appends (start_event, end_event, plan) so a
         # caller can time the verify step on the stream it runs on.
         self.verify_events: list | None = None
@@ -117,6 +118,25 @@ class SpecEngine:
         self.drafts = torch.empty(k, S, dtype=torch.int32, device=dev)
         self.accept_ws = ops.Workspace(dev)
 
+    def _upload(self, slot: int, arrays: list[np.ndarray]) -> list[torch.Tensor]:
+        """Copy int32 host arrays to the device in one transfer through pinned
+        staging buffer `slot` (the next iteration reuses it only after this one's
+        readback, by which time the copy has run); returns device views."""
+        offs = np.cumsum([0] + [a.shape[0] for a in arrays])
+        n = int(offs[-1])
+        buf = self._pinned[slot] if slot < len(self._pinned) else None
+        if buf is None or buf.numel() < n:
+            buf = torch.empty(max(n, 4096) * 2, dtype=torch.int32, pin_memory=True)
+            while len(self._pinned) <= slot:
+                self._pinned.append(None)
+            self._pinned[slot] = buf
+        host = buf.numpy()
+        for a, lo in zip(arrays, offs[:-1]):
+            host[lo:lo + a.shape[0]] = a
+        dev = buf[:n].to(self.device, non_blocking=True)
+        self.stats["h2d_bytes"] += n * 4
+        return [dev[offs[i]:offs[i + 1]] for i in range(len(arrays))]
+
     def step(self, reqs: list[_Request], eos: set[int]) -> None:
         """One draft/verify/accept iteration for every request in `reqs`."""
         k, S = self.k, len(reqs)
@@ -129,32 +149,30 @@ class SpecEngine:
         for r in reqs:
             r.t_seq.reserve(r.u_t + k)
         bs_d, bs_t = self.d_pool.block_size, self.t_pool.block_size
-        plans = [ForwardPlan([SeqSpec(r.d_seq.length, r.u_d, r.d_seq.blocks, 1) for r in reqs], bs_d)]
+        # --- upload 1: the first draft pass's plan and ids, so the GPU starts while
+        # the host builds the other plans (upload 2 queues behind that pass).
+        plan0 = ForwardPlan([SeqSpec(r.d_seq.length, r.u_d, r.d_seq.blocks, 1) for r in reqs], bs_d)
+        d_ids = [t for r in reqs for t in r.tokens[len(r.tokens) - r.u_d:]]
+        (plan0_dev, d_ids_dev) = self._upload(0, [plan0.host, np.asarray(d_ids, np.int32)])
+        # --- draft: k passes, argmax feeding the next pass on the device
+        self.dr.forward(plan0, d_ids_dev, self.dlog[:S], plan_dev=plan0_dev)
+        ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S])
+        plans = [plan0]
         for j in range(1, k):
             plans.append(ForwardPlan([SeqSpec(r.d_seq.length + r.u_d + j - 1, 1, r.d_seq.blocks, 1)
                                       for r in reqs], bs_d))
         vplan = ForwardPlan([SeqSpec(r.t_seq.length, r.u_t + k, r.t_seq.blocks, k + 1) for r in reqs], bs_t)
-        d_ids = [t for r in reqs for t in r.tokens[len(r.tokens) - r.u_d:]]
         v_ids, dst = [], np.empty((k, S), dtype=np.int64)
         for i, r in enumerate(reqs):
             base = len(v_ids) + r.u_t
             v_ids.extend(r.tokens[len(r.tokens) - r.u_t:])
             v_ids.extend([0] * k)
             dst[:, i] = base + np.arange(k)
-        # --- one host->device copy for every plan and input of this iteration
-        host = [p.host for p in plans] + [vplan.host, np.asarray(d_ids, np.int32), np.asarray(v_ids, np.int32),
-                                          dst.reshape(-1).astype(np.int32)]
-        offs = np.cumsum([0] + [h.shape[0] for h in host])
-        packed = np.concatenate(host)
-        dev_all = torch.from_numpy(packed).to(self.device)
-        self.stats["h2d_bytes"] += packed.nbytes
-        views = [dev_all[offs[i]:offs[i + 1]] for i in range(len(host))]
-        d_ids_dev, v_ids_dev, dst_dev = views[-3], views[-2], views[-1].long()
-        # --- draft: k passes, argmax feeding the next pass on the device
-        self.dr.forward(plans[0], d_ids_dev, self.dlog[:S], plan_dev=views[0])
-        ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S])
+        views = self._upload(1, [p.host for p in plans[1:]] + [vplan.host, np.asarray(v_ids, np.int32),
+                                                                dst.reshape(-1).astype(np.int32)])
+        v_ids_dev, dst_dev = views[-2], views[-1].long()
         for j in range(1, k):
-            self.dr.forward(plans[j], self.drafts[j - 1, :S], self.dlog[:S], plan_dev=views[j])
+            self.dr.forward(plans[j], self.drafts[j - 1, :S], self.dlog[:S], plan_dev=views[j - 1])
             ops.argmax_rows(self.dlog[:S], out=self.drafts[j, :S])
         # --- verify: one target pass over every request's u+k rows
         drafts = self.drafts[:, :S]
@@ -163,7 +181,7 @@ class SpecEngine:
         if self.verify_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
-        self.tr.forward(vplan, v_ids_dev, tlog, plan_dev=views[k])
+        self.tr.forward(vplan, v_ids_dev, tlog, plan_dev=views[k - 1])
         if self.verify_events is not None:
             ev1.record()
             self.verify_events.append((ev0, ev1, vplan))
