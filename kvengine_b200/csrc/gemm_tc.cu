@@ -892,13 +892,14 @@ TileConfig token_tiling(int m, int t) {
 // are clearly faster. Each tiling takes the most k-chunks per stage that still
 // leave two pipeline stages (fewer, larger TMA boxes measured faster than more
 // stages in flight); several k-chunks are single-split shapes on the 3-D maps
-// (k % 64 == 0). Two weight halves per CTA measured no faster on B200 and are
-// left to kve_gemm_force_shape. None of these choices changes a row's reduction
-// order.
-int chunks_for(int mt, int s, bool tma3d) {
+// (k % 64 == 0). Two weight halves per CTA (256 weight rows sharing each
+// activation tile) measured faster only for prompt-sized batches (m >= kLargeM).
+// None of these choices changes a row's reduction order.
+constexpr int kLargeM = 2048;
+int chunks_for(int mh, int mt, int s, bool tma3d) {
   if (s > 1 || !tma3d) return 1;
   for (int kc = 4; kc > 1; kc /= 2)
-    if ((size_t)(BM + mt) * BK * 2 * kc * 2 <= kSmemLimit - 2048) return kc;
+    if ((size_t)(mh * BM + mt) * BK * 2 * kc * 2 <= kSmemLimit - 2048) return kc;
   return 1;
 }
 
@@ -911,18 +912,25 @@ TileConfig best_config(int m, int feat_tiles, int k_blocks, int s, bool tma3d) {
     TileConfig c = token_tiling(m, t);
     const int mt = c.ng * c.n_g;
     if ((long long)(t - 1) * mt >= m) continue;  // an empty trailing tile
-    c.mh = 1;
-    c.kc = chunks_for(mt, s, tma3d);
-    c.us = config_us(feat_tiles, k_blocks, s, c);
-    if (c.us < best.us * 0.97) best = c;
+    for (int mh = 1; mh <= (m >= kLargeM ? 2 : 1); ++mh) {
+      if (mh == 2 && (s > 1 || c.ng == 2 || mt > 256 || feat_tiles < 2)) continue;
+      c.mh = mh;
+      c.kc = chunks_for(mh, mt, s, tma3d);
+      c.us = config_us(feat_tiles, k_blocks, s, c);
+      if (c.us < best.us * 0.97) best = c;
+    }
   }
   return best;
 }
 
-// Split-K factor: a function of (n, k) only, so a row's reduction order never
-// depends on how many tokens are in the batch. It minimises the modelled time
-// summed over small, medium and large batches, each with its best shape.
-int choose_splits(int feat_tiles, int k_blocks, bool tma3d) {
+// Split-K factor: for batches below kLargeM a function of (n, k) only, so a
+// row's reduction order never depends on how many tokens are decoded together
+// (draft and verify passes agree bit for bit); it minimises the modelled time
+// summed over small, medium and large decode batches, each with its best shape.
+// Prompt-sized batches (m >= kLargeM) have tiles enough for every SM and never
+// split K.
+int choose_splits(int feat_tiles, int k_blocks, bool tma3d, bool large) {
+  if (large) return 1;
   int best = 1;
   double best_t = 1e30;
   for (int s = 1; s <= kMaxSplits; ++s) {
@@ -945,7 +953,7 @@ Plan make_plan_uncached(int m, int n, int k) {
   p.feat_tiles = (n + BM - 1) / BM;
   p.k_blocks = (k + BK - 1) / BK;
   p.tma3d = k % BK == 0;
-  p.splits = choose_splits(p.feat_tiles, p.k_blocks, p.tma3d);
+  p.splits = choose_splits(p.feat_tiles, p.k_blocks, p.tma3d, m >= kLargeM);
   TileConfig c = best_config(m, p.feat_tiles, p.k_blocks, p.splits, p.tma3d);
   // A forced shape applies where it is valid for this GEMM; it never touches the
   // split factor, so results are the same bits either way.
