@@ -13,11 +13,13 @@
 // accumulator all fp32), masked keys contribute exact zeros.
 #include <math.h>
 
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
 #include "kve_common.cuh"
 #include "passes.cuh"
+#include "tma.cuh"
 
 namespace kve {
 namespace {
@@ -266,17 +268,22 @@ __device__ __forceinline__ void merge_partials(const AttnParams& p, int bh, int 
   }
 }
 
-template <int HD, int BS, int RB>
+// TMA: block size 16 only. One thread brings each round's K and V with 2 KB
+// boxes (16 keys x 64 dims, SWIZZLE_128B) straight from the pool; keys past the
+// chunk load from outside the tensor (zero fill) and the tail of the last
+// partial block is zeroed in shared memory. Otherwise 16-byte cp.async per thread.
+template <int HD, int BS, int RB, bool TMA>
 __global__ void __launch_bounds__(RB * kKeySlices * 32, 1)
-paged_attn_mma_kernel(AttnParams p) {
+paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                      AttnParams p) {
   // With hist_static the wait moves down to the first load of a key written in
   // this pass (or of q); everything before it reads constant inputs only.
   bool waited = !p.hist_static;
   if (waited) grid_dep_wait();
   grid_dep_launch();
   constexpr int NTHR = RB * kKeySlices * 32;
-  constexpr int ROW = HD * 2 + 16;                  // padded smem row (bytes)
-  constexpr int TILE = kMmaKeyTile * ROW;           // one K or V tile
+  constexpr int ROW = HD * 2 + 16;                  // padded smem row (bytes, cp.async layout)
+  constexpr int TILE = TMA ? kMmaKeyTile * HD * 2 : kMmaKeyTile * ROW;  // one K or V tile
   constexpr int ROUND = kKeySlices * 2 * TILE;      // K and V of one round (kKeySlices tiles)
   constexpr int KSTEPS = HD / 16;                   // k16 steps over the head dim
   constexpr int NT = kMmaKeyTile / 8;               // n8 tiles of keys per tile
@@ -285,9 +292,19 @@ paged_attn_mma_kernel(AttnParams p) {
   constexpr int TCH = 2 * kMmaKeyTile * CPR;        // 16-byte chunks of one tile (K and V)
   constexpr int SLOTS = kKeySlices * TCH / NTHR;    // chunks per thread per round
   static_assert(kKeySlices * TCH % NTHR == 0, "round copy must divide evenly");
-  extern __shared__ __align__(128) uint8_t smem_attn[];
+  extern __shared__ __align__(128) uint8_t smem_dyn[];
+  // The 128-byte swizzle repeats every 1024 bytes: TMA tiles start 1024-aligned.
+  uint8_t* smem_attn = TMA ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023))
+                           : smem_dyn;
   const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem_attn));
-  // buffers: [round buffer][slice][K|V] tiles, then the chunk's block table
+  // buffers: [round buffer][slice][K|V] tiles, then the chunk's block table, then (TMA) the round barriers
+  uint64_t* round_full = reinterpret_cast<uint64_t*>(smem_attn + kRoundBufs * ROUND + kChunk * sizeof(int));
+  if constexpr (TMA) {
+    if (threadIdx.x == 0) {
+      for (int b = 0; b < kRoundBufs; ++b) mbar_init(smem_u32(&round_full[b]), 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+  }
 
   const int bh = blockIdx.x, c = blockIdx.y, qtile = blockIdx.z;
   const int b = bh / p.nkv, h = bh % p.nkv;
@@ -371,6 +388,38 @@ paged_attn_mma_kernel(AttnParams p) {
     }
   };
 
+  // TMA round: thread 0 asks for every 16-key block of the round's tiles.
+  const int oob_row = (int)(p.num_blocks * 16);  // first row past the pool: loads there fill zeros
+  auto tma_round = [&](int r) {
+    if constexpr (TMA) {
+      if (threadIdx.x != 0) return;
+      const uint32_t fb = smem_u32(&round_full[r % kRoundBufs]);
+      const uint32_t rbase = sbase + (uint32_t)((r % kRoundBufs) * ROUND);
+      int tiles = 0;
+      for (int s = 0; s < kKeySlices; ++s) tiles += r * kKeySlices + s < n_tiles;
+      mbar_expect_tx(fb, (uint32_t)(tiles * 2 * TILE));  // K and V of every tile of the round
+      for (int s = 0; s < kKeySlices; ++s) {
+        const int tile = r * kKeySlices + s;
+        if (tile >= n_tiles) break;
+#pragma unroll
+        for (int jb = 0; jb < 2; ++jb) {
+          const int key0 = key_lo + tile * kMmaKeyTile + jb * 16;
+          int y = oob_row;
+          if (key0 < key_hi) {
+            const int blk = tab[key0 / 16 - blk_lo];
+            if (blk >= 0) y = blk * 16;
+          }
+#pragma unroll
+          for (int half = 0; half < HD / 64; ++half) {
+            const uint32_t off = (uint32_t)(s * 2 * TILE + half * 4096 + jb * 2048);
+            tma_load_2d(rbase + off, &map_k, h * HD + half * 64, y, fb);
+            tma_load_2d(rbase + off + TILE, &map_v, h * HD + half * 64, y, fb);
+          }
+        }
+      }
+    }
+  };
+
   // Prologue: kRoundBufs rounds in flight (one commit group per round, empty
   // groups past the end). Rounds of history keys may load before the wait.
   const int hist_end = ctx - ql;  // keys below this were written before this pass
@@ -381,9 +430,10 @@ paged_attn_mma_kernel(AttnParams p) {
         grid_dep_wait();
         waited = true;
       }
-      load_round(r);
+      if constexpr (TMA) tma_round(r);
+      else load_round(r);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    if constexpr (!TMA) asm volatile("cp.async.commit_group;" ::: "memory");
   }
   if (!waited) grid_dep_wait();  // before q and the remaining rounds
 
@@ -413,10 +463,44 @@ paged_attn_mma_kernel(AttnParams p) {
 #pragma unroll
   for (int j = 0; j < DT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 
+  // Shared-memory address of (key row, dim) in a K or V tile; dim is a multiple of 8.
+  auto tile_addr = [&](uint32_t base, int key_row, int dim) -> uint32_t {
+    if constexpr (TMA)
+      return base + (uint32_t)((dim >> 6) * 4096 + key_row * 128 + ((((dim & 63) >> 3) ^ (key_row & 7)) << 4));
+    else
+      return base + (uint32_t)(key_row * ROW + dim * 2);
+  };
+  bool failed = false;
   for (int r = 0; r < n_rounds; ++r) {
-    // Round r is the oldest outstanding group once kRoundBufs - 1 newer ones may remain.
-    asm volatile("cp.async.wait_group %0;" ::"n"(kRoundBufs - 1) : "memory");
-    __syncthreads();
+    if constexpr (TMA) {
+      const bool ok = mbar_wait(smem_u32(&round_full[r % kRoundBufs]), (uint32_t)(r / kRoundBufs) & 1u, p.status);
+      if (__syncthreads_or(!ok)) {
+        // Let the other buffer's loads (if any were issued) land before leaving.
+        for (int rr = r + 1; rr < n_rounds && rr < r + kRoundBufs; ++rr)
+          mbar_wait(smem_u32(&round_full[rr % kRoundBufs]), (uint32_t)(rr / kRoundBufs) & 1u, p.status);
+        failed = true;
+        break;
+      }
+      // Zero the V rows of the last partial block past the chunk's keys (pool contents there are
+      // not this sequence's keys; P is 0 for them but 0 * NaN would not be).
+      const int t_last = (key_hi - 1 - key_lo) / kMmaKeyTile;
+      if (t_last / kKeySlices == r) {
+        const int first = key_hi - (key_lo + t_last * kMmaKeyTile);
+        if (first < kMmaKeyTile) {
+          uint8_t* vt = smem_attn + (r % kRoundBufs) * ROUND + (t_last % kKeySlices) * 2 * TILE + TILE;
+          const int per_half = (kMmaKeyTile - first) * 8;  // 16-byte pieces of one 64-dim half
+          for (int i = threadIdx.x; i < per_half * (HD / 64); i += NTHR) {
+            const int half = i / per_half, rem = i % per_half;
+            reinterpret_cast<uint4*>(vt + half * 4096 + (first + rem / 8) * 128)[rem % 8] = make_uint4(0, 0, 0, 0);
+          }
+        }
+        __syncthreads();
+      }
+    } else {
+      // Round r is the oldest outstanding group once kRoundBufs - 1 newer ones may remain.
+      asm volatile("cp.async.wait_group %0;" ::"n"(kRoundBufs - 1) : "memory");
+      __syncthreads();
+    }
     const int tile = r * kKeySlices + ks;
     if (active && tile < n_tiles) {
       const uint32_t kbase = sbase + (uint32_t)((r % kRoundBufs) * ROUND + ks * 2 * TILE);
@@ -435,7 +519,7 @@ paged_attn_mma_kernel(AttnParams p) {
           const int key_row = 8 * j2 + ((mat >> 1) << 3) + rr;
           const int dim = kk * 16 + ((mat & 1) << 3);
           uint32_t b0, b1, b2, b3;
-          ldsm_x4(kbase + key_row * ROW + dim * 2, b0, b1, b2, b3);
+          ldsm_x4(tile_addr(kbase, key_row, dim), b0, b1, b2, b3);
           mma_bf16_16816(sc[j2], qa[kk], b0, b1);
           mma_bf16_16816(sc[j2 + 1], qa[kk], b2, b3);
         }
@@ -497,17 +581,25 @@ paged_attn_mma_kernel(AttnParams p) {
           const int key_row = s16 * 16 + ((mat & 1) << 3) + rr;
           const int dim = 8 * j2 + ((mat >> 1) << 3);
           uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(vbase + key_row * ROW + dim * 2, b0, b1, b2, b3);
+          ldsm_x4_t(tile_addr(vbase, key_row, dim), b0, b1, b2, b3);
           mma_bf16_16816(acc[j2], a, b0, b1);
           mma_bf16_16816(acc[j2 + 1], a, b2, b3);
         }
       }
     }
     __syncthreads();  // every slice is done with this round's buffer
-    if (r + kRoundBufs < n_rounds) load_round(r + kRoundBufs);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    if constexpr (TMA) {
+      if (threadIdx.x == 0 && r + kRoundBufs < n_rounds) {
+        fence_proxy_async_smem();
+        tma_round(r + kRoundBufs);
+      }
+    } else {
+      if (r + kRoundBufs < n_rounds) load_round(r + kRoundBufs);
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (failed) return;
+  if constexpr (!TMA) asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
 
   // Merge the key slices of each row block in slice order through shared memory
@@ -642,26 +734,41 @@ attn_combine_kernel(AttnParams p) {
   merge_partials<T, HD, kWarps>(p, bh, qtile, h, nt * p.group, ctx - ql + t0, qoff, t0);
 }
 
-template <int HD, int BS, int RB>
-void launch_mma(const AttnParams& p, dim3 grid, cudaStream_t stream) {
+template <int HD, int BS, int RB, bool TMA>
+void launch_mma(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid, cudaStream_t stream) {
   // round buffers (K + V of kKeySlices tiles, twice), then the chunk's block table
-  // (<= kChunk entries); the slice merge reuses the round buffers.
-  constexpr size_t kRounds = (size_t)kRoundBufs * kKeySlices * 2 * kMmaKeyTile * (HD * 2 + 16);
+  // (<= kChunk entries) and the round barriers; the slice merge reuses the round buffers.
+  constexpr size_t kRounds = (size_t)kRoundBufs * kKeySlices * 2 * kMmaKeyTile * (TMA ? HD * 2 : HD * 2 + 16);
   constexpr size_t kMerge = (size_t)(kKeySlices - 1) * RB * 16 * (HD + 8 + 2) * sizeof(float);
   static_assert(kMerge <= kRounds, "slice merge must fit in the round buffers");
-  constexpr size_t smem = kRounds + kChunk * sizeof(int);
+  constexpr size_t smem = kRounds + kChunk * sizeof(int) + kRoundBufs * sizeof(uint64_t) + (TMA ? 1024 : 0);
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(paged_attn_mma_kernel<HD, BS, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(paged_attn_mma_kernel<HD, BS, RB, TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
   });
-  launch_kernel(paged_attn_mma_kernel<HD, BS, RB>, grid, dim3(RB * kKeySlices * 32), smem, stream, p);
+  launch_kernel(paged_attn_mma_kernel<HD, BS, RB, TMA>, grid, dim3(RB * kKeySlices * 32), smem, stream, mk, mv, p);
 }
 
-template <int HD, int BS>
-void launch_mma_rb(const AttnParams& p, dim3 grid, cudaStream_t stream) {
-  if (p.rb == 1) launch_mma<HD, BS, 1>(p, grid, stream);
-  else if (p.rb == 2) launch_mma<HD, BS, 2>(p, grid, stream);
-  else launch_mma<HD, BS, 4>(p, grid, stream);
+template <int HD, int BS, bool TMA>
+void launch_mma_rb(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
+                   cudaStream_t stream) {
+  if (p.rb == 1) launch_mma<HD, BS, 1, TMA>(p, mk, mv, grid, stream);
+  else if (p.rb == 2) launch_mma<HD, BS, 2, TMA>(p, mk, mv, grid, stream);
+  else launch_mma<HD, BS, 4, TMA>(p, mk, mv, grid, stream);
+}
+
+// 2-D map of one layer's pool as [num_blocks * 16 rows, nkv * hd] bf16, box {64, 16}, SWIZZLE_128B.
+bool pool_map(CUtensorMap* map, const void* pool, int64_t rows, int width) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)width * 2};
+  cuuint32_t box[2] = {64, 16};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(pool), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <typename T, int HD>
@@ -670,8 +777,17 @@ int launch(AttnParams& p, int batch, cudaStream_t stream) {
   // later chunk, and the empty late-chunk CTAs of short sequences come last.
   dim3 grid(batch * p.nkv, p.n_chunks, p.n_qtiles);
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    if (p.bs == 16) launch_mma_rb<HD, 16>(p, grid, stream);
-    else launch_mma_rb<HD, 0>(p, grid, stream);
+    CUtensorMap mk, mv;
+    memset(&mk, 0, sizeof(mk));
+    memset(&mv, 0, sizeof(mv));
+    const int64_t rows = p.num_blocks * 16;
+    if (p.bs == 16 && rows < (1ll << 31) && pool_map(&mk, p.pool_k, rows, p.nkv * HD) &&
+        pool_map(&mv, p.pool_v, rows, p.nkv * HD))
+      launch_mma_rb<HD, 16, true>(p, mk, mv, grid, stream);
+    else if (p.bs == 16)
+      launch_mma_rb<HD, 16, false>(p, mk, mv, grid, stream);
+    else
+      launch_mma_rb<HD, 0, false>(p, mk, mv, grid, stream);
   } else {
     const size_t smem = sizeof(float) * ((size_t)kMaxRows * HD + kKeyTile * (HD + 1) + kKeyTile * HD);
     static std::once_flag once;
