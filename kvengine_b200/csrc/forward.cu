@@ -59,7 +59,7 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
   KVE_TRY(kve_embed(b->ids, M, m->embed, dt, H, m->vocab, s->hidden, s->dev_status, stream));
   for (int l = 0; l < m->num_layers; ++l) {
     const kve_layer_t& L = m->layers[l];
-    KVE_TRY(kve_rmsnorm(s->hidden, dt, L.ln1, M, H, m->rms_eps, nullptr, s->normed, stream));
+    KVE_TRY(rmsnorm_run(s->hidden, dt, L.ln1, M, H, m->rms_eps, nullptr, s->normed, true, stream));
     if (fused_qkv) {
       // bf16: projection, bias, RoPE and the K/V append in one kernel.
       EpiArgs e{};
@@ -84,14 +84,14 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
                                   s->attn_ws, s->attn_ws_bytes, s->dev_status, true, stream));
     KVE_TRY(gemm_run(s->attn, L.w_o, dt, M, H, qsz, KVE_EPI_RESIDUAL, nullptr, s->hidden, s->hidden, dt,
                      s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
-    KVE_TRY(kve_rmsnorm(s->hidden, dt, L.ln2, M, H, m->rms_eps, nullptr, s->normed, stream));
+    KVE_TRY(rmsnorm_run(s->hidden, dt, L.ln2, M, H, m->rms_eps, nullptr, s->normed, true, stream));
     KVE_TRY(gemm_run(s->normed, L.w_gu, dt, M, 2 * m->intermediate, H, KVE_EPI_SILU_MUL, nullptr, nullptr,
                      s->act, dt, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
     KVE_TRY(gemm_run(s->act, L.w_down, dt, M, H, m->intermediate, KVE_EPI_RESIDUAL, nullptr, s->hidden,
                      s->hidden, dt, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
   }
   if (b->n_out == 0) return KVE_OK;
-  KVE_TRY(kve_rmsnorm(s->hidden, dt, m->final_norm, b->n_out, H, m->rms_eps, b->out_rows, s->out_normed, stream));
+  KVE_TRY(rmsnorm_run(s->hidden, dt, m->final_norm, b->n_out, H, m->rms_eps, b->out_rows, s->out_normed, true, stream));
   KVE_TRY(gemm_run(s->out_normed, m->lm_head, dt, b->n_out, m->vocab, H, KVE_EPI_STORE, nullptr, nullptr,
                    b->logits, b->logits_dtype, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
   return KVE_OK;

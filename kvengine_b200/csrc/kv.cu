@@ -4,6 +4,7 @@
 #include <math.h>
 
 #include "kve_common.cuh"
+#include "passes.cuh"
 
 namespace kve {
 namespace {
@@ -129,14 +130,42 @@ constexpr int kNormThreads = 256;
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads)
 rmsnorm_kernel(const T* __restrict__ x, const float* __restrict__ w, int hidden, float eps,
-               const int32_t* __restrict__ row_index, T* __restrict__ out) {
+               const int32_t* __restrict__ row_index, T* __restrict__ out, int w_static) {
+  // Thread t owns elements t, t + 256, ...: the first kNormRegs of them stay in
+  // registers between the sum of squares and the scaling (one read of x), and the
+  // weights for them are read before the dependency wait when they are constant.
+  constexpr int kNormRegs = 8;  // hidden <= 2048 fully in registers
+  float wv[kNormRegs];
+  if (w_static) {
+#pragma unroll
+    for (int j = 0; j < kNormRegs; ++j) {
+      const int i = threadIdx.x + j * kNormThreads;
+      wv[j] = i < hidden ? w[i] : 0.f;
+    }
+  }
   grid_dep_wait();
   grid_dep_launch();
+  if (!w_static) {
+#pragma unroll
+    for (int j = 0; j < kNormRegs; ++j) {
+      const int i = threadIdx.x + j * kNormThreads;
+      wv[j] = i < hidden ? w[i] : 0.f;
+    }
+  }
   int r = blockIdx.x;
   int src_row = row_index ? row_index[r] : r;
   const T* xr = x + (size_t)src_row * hidden;
+  float xv[kNormRegs];
+#pragma unroll
+  for (int j = 0; j < kNormRegs; ++j) {
+    const int i = threadIdx.x + j * kNormThreads;
+    xv[j] = i < hidden ? Elem<T>::to_f(xr[i]) : 0.f;
+  }
   float ss = 0.f;
-  for (int i = threadIdx.x; i < hidden; i += kNormThreads) {
+#pragma unroll
+  for (int j = 0; j < kNormRegs; ++j)
+    if (threadIdx.x + j * kNormThreads < hidden) ss = fmaf(xv[j], xv[j], ss);
+  for (int i = threadIdx.x + kNormRegs * kNormThreads; i < hidden; i += kNormThreads) {
     float v = Elem<T>::to_f(xr[i]);
     ss = fmaf(v, v, ss);
   }
@@ -152,7 +181,12 @@ rmsnorm_kernel(const T* __restrict__ x, const float* __restrict__ w, int hidden,
   __syncthreads();
   float inv = 1.0f / sqrtf(red[0] / (float)hidden + eps);
   T* orow = out + (size_t)r * hidden;
-  for (int i = threadIdx.x; i < hidden; i += kNormThreads) {
+#pragma unroll
+  for (int j = 0; j < kNormRegs; ++j) {
+    const int i = threadIdx.x + j * kNormThreads;
+    if (i < hidden) orow[i] = Elem<T>::from_f(__fmul_rn(wv[j], Elem<T>::round(__fmul_rn(xv[j], inv))));
+  }
+  for (int i = threadIdx.x + kNormRegs * kNormThreads; i < hidden; i += kNormThreads) {
     float v = Elem<T>::round(__fmul_rn(Elem<T>::to_f(xr[i]), inv));
     orow[i] = Elem<T>::from_f(__fmul_rn(w[i], v));
   }
@@ -263,20 +297,25 @@ extern "C" int kve_embed(const int32_t* ids, int n_tokens, const void* table, in
   return check_launch("kve_embed");
 }
 
-extern "C" int kve_rmsnorm(const void* x, int dtype, const float* weight, int rows, int hidden, float eps,
-                           const int32_t* row_index, void* out, cudaStream_t stream) {
+int kve::rmsnorm_run(const void* x, int dtype, const float* weight, int rows, int hidden, float eps,
+                     const int32_t* row_index, void* out, bool w_static, cudaStream_t stream) {
   if (rows < 0 || hidden < 1) return set_error(KVE_ERR_ARG, "kve_rmsnorm: bad sizes");
   if (rows == 0) return KVE_OK;
   if (!x || !weight || !out) return set_error(KVE_ERR_ARG, "kve_rmsnorm: null pointer");
   if (dtype == KVE_F32) {
     launch_kernel(rmsnorm_kernel<float>, dim3(rows), dim3(kNormThreads), 0, stream,
-        static_cast<const float*>(x), weight, hidden, eps, row_index, static_cast<float*>(out));
+        static_cast<const float*>(x), weight, hidden, eps, row_index, static_cast<float*>(out), w_static ? 1 : 0);
   } else if (dtype == KVE_BF16) {
     launch_kernel(rmsnorm_kernel<__nv_bfloat16>, dim3(rows), dim3(kNormThreads), 0, stream,
         static_cast<const __nv_bfloat16*>(x), weight, hidden, eps, row_index,
-        static_cast<__nv_bfloat16*>(out));
+        static_cast<__nv_bfloat16*>(out), w_static ? 1 : 0);
   } else {
     return set_error(KVE_ERR_DTYPE, "kve_rmsnorm: dtype %d", dtype);
   }
   return check_launch("kve_rmsnorm");
+}
+
+extern "C" int kve_rmsnorm(const void* x, int dtype, const float* weight, int rows, int hidden, float eps,
+                           const int32_t* row_index, void* out, cudaStream_t stream) {
+  return rmsnorm_run(x, dtype, weight, rows, hidden, eps, row_index, out, false, stream);
 }

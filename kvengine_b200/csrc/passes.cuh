@@ -16,4 +16,9 @@ int paged_attn_run(const void* q, int dtype, const void* pool_k, const void* poo
                    int block_size, int64_t num_blocks, float scale, void* out, void* workspace,
                    size_t workspace_bytes, int* dev_status, bool hist_static, cudaStream_t stream);
 
+// kve_rmsnorm; w_static: the weight vector is written by no kernel that may
+// still be running, so it is read before the dependency wait.
+int rmsnorm_run(const void* x, int dtype, const float* weight, int rows, int hidden, float eps,
+                const int32_t* row_index, void* out, bool w_static, cudaStream_t stream);
+
 }  // namespace kve
