@@ -204,13 +204,39 @@ struct Epi {
     }
   }
 
-  // Residual vectors of rows [0, nr) for copy_out, loaded ahead of the stores so
-  // that all of them are in flight at once (out may alias the residual: each
-  // element is read and then written by the same thread).
+  // Per-row inputs of copy_out for rows [0, nr), loaded ahead so that they are
+  // in flight together (and, for a tile's first chunk, during the main loop):
+  // RESIDUAL - the residual vectors (out may alias the residual: each element is
+  // read and then written by the same thread); qkv+RoPE - the token's position
+  // and pool slot, with the cos/sin lines prefetched into L1.
   static constexpr int RPP = 128 / VPR;       // rows per copy_out pass
   static constexpr int NPASS = kRows / RPP;   // passes per staged chunk
   static __device__ __forceinline__ void load_res(const TcArgs& a, int tok_base, int nr, int col0, int etid,
                                                   uint4 (&res)[NPASS]) {
+    if constexpr (MODE == kEpiQkvRope) {
+      const int c = (etid % VPR) * VE;
+      const int r_first = etid / VPR;
+      const int f = col0 + c;
+      if (f >= a.n) return;
+      const int hd = a.e.hd, half = hd >> 1;
+      const int d = f % hd;
+      const int dd = d < half ? d : d - half;
+      const bool rot = f < (a.e.nq + a.e.nkv) * hd;
+#pragma unroll
+      for (int i = 0; i < NPASS; ++i) {
+        const int r = r_first + i * RPP;
+        const int t = tok_base + r;
+        if (r < nr && t < a.m) {
+          const int pos = a.e.positions[t];
+          const int64_t slot = a.e.slots[t];
+          res[i] = make_uint4((uint32_t)pos, (uint32_t)slot, (uint32_t)((uint64_t)slot >> 32), 0u);
+          if (rot && pos >= 0 && pos < a.e.rope_len) {
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(a.e.rope_cos + (size_t)pos * half + dd));
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(a.e.rope_sin + (size_t)pos * half + dd));
+          }
+        }
+      }
+    }
     if constexpr (MODE == KVE_EPI_RESIDUAL) {
       const int nvalid = min(W, a.e.ld_out - col0);
       const int c = (etid % VPR) * VE;
@@ -253,7 +279,7 @@ struct Epi {
         const T* srow = reinterpret_cast<const T*>(buf) + r * W;
         uint4 val = *reinterpret_cast<const uint4*>(srow + c);
         if (rot) {
-          int pos = a.e.positions[t];
+          int pos = (int)res[i].x;
           if (pos < 0 || pos >= a.e.rope_len) {
             report(a.e.status, KVE_ERR_BOUNDS);
             pos = 0;
@@ -276,7 +302,7 @@ struct Epi {
         if (f < q_end) {
           dst = static_cast<T*>(a.e.q_out) + (size_t)t * q_end + f;
         } else {
-          const int64_t slot = a.e.slots[t];
+          const int64_t slot = (int64_t)(((uint64_t)res[i].z << 32) | res[i].y);
           if (slot < 0 || slot >= a.e.num_slots) {
             report(a.e.status, KVE_ERR_BOUNDS);
             continue;
@@ -530,6 +556,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * a.mt);
   const int etid = (threadIdx.x - 64) & 127;  // thread index within its warpgroup
   const float bias_f = ((MODE == KVE_EPI_BIAS || MODE == kEpiQkvRope) && epi && feat < a.n) ? a.e.bias[feat] : 0.f;
+  // The first chunk's per-row inputs load while the main loop runs.
+  const int first_c0 = MH == 1 ? egrp * kRows : 0;
+  uint4 res_first[E::NPASS];
+  if (epi && a.splits == 1 && first_c0 < a.mt)
+    E::load_res(a, tok0 + first_c0, min(kRows, a.mt - first_c0), col0, etid, res_first);
   bool have = false;
   if (epi) {
     have = !aborted && mbar_wait(smem_u32(tmem_full), 0, a.status);
@@ -542,11 +573,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     if (epi) {
       int it = 0;
       constexpr int kChunkStride = (MH == 1 ? kEpiGroups : 1) * kRows;
-      for (int c0 = MH == 1 ? egrp * kRows : 0; c0 < a.mt; c0 += kChunkStride, ++it) {
+      for (int c0 = first_c0; c0 < a.mt; c0 += kChunkStride, ++it) {
         const int n = min(kRows, a.mt - c0);
         uint8_t* buf = stg + (egrp * 2 + (it & 1)) * kStgBuf;
         uint4 res[E::NPASS];
-        E::load_res(a, tok0 + c0, n, col0, etid, res);
+        if (it == 0) {
+#pragma unroll
+          for (int i = 0; i < E::NPASS; ++i) res[i] = res_first[i];
+        } else {
+          E::load_res(a, tok0 + c0, n, col0, etid, res);
+        }
         float v[32];
         tmem_load_cols(t_lane + c0, n, have, v);
         E::template stage<32>(buf, 0, n, f_local, v, bias_f);
