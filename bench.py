@@ -538,6 +538,74 @@ def run_profile_iteration(args):
     print(json.dumps({"profiled": "one steady-state spec iteration", "requests": N_REQ, "k": K_SPEC}))
 
 
+def run_serve(args):
+    """Config 5: continuous-batching spec decode over a lognormal request mix
+    (prompt mean 128, output mean 64, sigma 0.7, uniform tokens), requests sharded
+    over the ranks (rank r takes requests r, r + world, ...), `--serve N` requests
+    in total. 0.5B-arch draft -> 3B-arch target, or with --self-draft the 3B target
+    as its own draft (full acceptance). One timed pass over the whole mix."""
+    import torch.distributed as dist
+
+    from kvengine_b200 import Model, PagedKVCache, SpecServer
+    from kvengine_b200.config import QWEN2_0_5B, QWEN2_3B
+    from kvengine_b200.workloads import lognormal_requests
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=600))
+    target = Model.random_init(QWEN2_3B, seed=2, dtype=torch.bfloat16, device=dev, init_device=dev)
+    draft = target if args.self_draft else Model.random_init(QWEN2_0_5B, seed=1, dtype=torch.bfloat16, device=dev,
+                                                             init_device=dev)
+    mix = lognormal_requests(args.serve, seed=5)[rank::world]
+    blocks = args.serve_blocks
+    t_pool = PagedKVCache.for_model(target, num_blocks=blocks, block_size=BLOCK)
+    d_pool = PagedKVCache.for_model(draft, num_blocks=blocks, block_size=BLOCK)
+
+    def serve(reqs):
+        srv = SpecServer(target, draft, t_pool, d_pool, k=K_SPEC, max_batch=args.serve_batch, eos_token_id=None)
+        for p, n in reqs:
+            srv.add_request(p, n)
+        srv.run()
+        return srv
+
+    serve(mix[: min(len(mix), 2 * args.serve_batch)])  # warm-up: kernels, plans, allocator caches
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    srv = serve(mix)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+    tok = torch.tensor([float(srv.stats.new_tokens)], device=dev)
+    drafted = sum(r.tokens_drafted for r in srv.results.values())
+    accepted = sum(r.tokens_accepted for r in srv.results.values())
+    acc = torch.tensor([float(drafted), float(accepted)], device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tok, op=dist.ReduceOp.SUM)
+        dist.all_reduce(acc, op=dist.ReduceOp.SUM)
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "accepted tokens/s (config 5, continuous batching, k=4)",
+            "value": round(float(tok.item()) / (float(ms.item()) / 1e3), 2), "unit": "accepted tokens/s",
+            "n_gpus": world, "higher_is_better": True, "scaling": "strong",
+            "ms_total": round(float(ms.item()), 1), "new_tokens": int(tok.item()),
+            "acceptance_rate": round(float(acc[1].item() / acc[0].item()), 4) if acc[0].item() else None,
+            "config": {"workload": "config 5: lognormal prompts (mean 128) and outputs (mean 64), sigma 0.7",
+                       "requests": args.serve, "draft": "3B target (self)" if args.self_draft else "0.5B-arch seed 1",
+                       "target": "3B-arch seed 2", "max_batch_per_gpu": args.serve_batch,
+                       "kv_blocks_per_pool": blocks, "block_size": BLOCK},
+            "server": {"steps": srv.stats.steps, "admitted": srv.stats.admitted, "preempted": srv.stats.preempted,
+                       "peak_running": srv.stats.peak_running},
+            "dtype": "bf16", "data": "synthetic (seeded random ids, random-init weights)"}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -548,6 +616,10 @@ def main():
     ap.add_argument("--micro", default=None, help="comma list of accept,attention,gemm microbenchmarks")
     ap.add_argument("--gemm-case", default=None, help="restrict --micro gemm to these shapes (comma list)")
     ap.add_argument("--profile-iteration", action="store_true")
+    ap.add_argument("--serve", type=int, default=0, help="config 5: continuous batching over this many requests")
+    ap.add_argument("--serve-batch", type=int, default=128, help="running requests per GPU (--serve)")
+    ap.add_argument("--serve-blocks", type=int, default=8192, help="KV blocks per pool (--serve)")
+    ap.add_argument("--self-draft", action="store_true", help="--serve with the target as its own draft")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -555,6 +627,8 @@ def main():
         run_micro(args)
     elif args.profile_iteration:
         run_profile_iteration(args)
+    elif args.serve:
+        run_serve(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -17,11 +17,12 @@ from .decode import AUTO_EOS, GenerationResult, greedy_batch, greedy_paged
 from .forward import forward_with_own_cache
 from .model import Model, as_model
 from .paged import DEFAULT_BLOCK_SIZE, PagedKVCache, PagedSequenceCache
+from .serving import SpecServer
 from .speculative import SpecDecodeResult, SpecEngine, speculative_greedy, speculative_greedy_batch
 
 __all__ = [
     "AUTO_EOS", "DEFAULT_BLOCK_SIZE", "BlockManager", "DoubleFree", "GenerationResult", "Model",
     "ModelConfig", "OutOfBlocks", "PRESETS", "PagedKVCache", "PagedSequenceCache", "QWEN2_0_5B", "QWEN2_3B",
     "SpecDecodeResult", "SpecEngine", "TINY", "as_model", "forward_with_own_cache", "greedy_batch",
-    "greedy_paged", "speculative_greedy", "speculative_greedy_batch",
+    "greedy_paged", "speculative_greedy", "speculative_greedy_batch", "SpecServer",
 ]

@@ -878,14 +878,13 @@ TileConfig best_config(int m, int feat_tiles, int k_blocks, int s, bool tma3d) {
   return best;
 }
 
-// Split-K factor: for batches below kLargeM a function of (n, k) only, so a
-// row's reduction order never depends on how many tokens are decoded together
-// (draft and verify passes agree bit for bit); it minimises the modelled time
-// summed over small, medium and large decode batches, each with its best shape.
-// Prompt-sized batches (m >= kLargeM) have tiles enough for every SM and never
-// split K.
-int choose_splits(int feat_tiles, int k_blocks, bool tma3d, bool large) {
-  if (large) return 1;
+// Split-K factor: a function of (n, k) only, so a row's reduction order never
+// depends on how many tokens are processed together (draft and verify passes
+// agree bit for bit whatever the batch, prompts included - a draft identical to
+// the target is accepted in full under continuous batching). It minimises the
+// modelled time summed over small, medium and large decode batches, each with
+// its best shape.
+int choose_splits(int feat_tiles, int k_blocks, bool tma3d) {
   int best = 1;
   double best_t = 1e30;
   for (int s = 1; s <= kMaxSplits; ++s) {
@@ -908,7 +907,7 @@ Plan make_plan_uncached(int m, int n, int k) {
   p.feat_tiles = (n + BM - 1) / BM;
   p.k_blocks = (k + BK - 1) / BK;
   p.tma3d = k % BK == 0;
-  p.splits = choose_splits(p.feat_tiles, p.k_blocks, p.tma3d, m >= kLargeM);
+  p.splits = choose_splits(p.feat_tiles, p.k_blocks, p.tma3d);
   TileConfig c = best_config(m, p.feat_tiles, p.k_blocks, p.splits, p.tma3d);
   // A forced shape applies where it is valid for this GEMM; it never touches the
   // split factor, so results are the same bits either way.
