@@ -281,11 +281,11 @@ def run_gpu(args):
 
     if rank == 0:
         line = {
-            "metric": "accepted tokens/s (0.5B->3B, k=4)",
+            "metric": f"accepted tokens/s (0.5B->3B, k={K_SPEC})",
             "value": round(value, 2), "unit": "accepted tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random ids, random-init weights)",
-            "config": {"workload": "config 4 at k=4: 0.5B-arch draft (seed 1) -> 3B-arch target (seed 2), bf16",
+            "config": {"workload": f"config 4 at k={K_SPEC}: 0.5B-arch draft (seed 1) -> 3B-arch target (seed 2), bf16",
                        "requests_per_gpu": N_REQ, "prompt_len": PROMPT, "new_tokens": NEW, "k": K_SPEC,
                        "block_size": BLOCK, "global_requests": N_REQ * world, "parallelism": f"dp{world} (requests sharded)",
                        "l2": "inputs larger than L2 (6.2 GB target + 1.0 GB draft weights streamed per pass)"},
@@ -377,11 +377,11 @@ def run_reference(args):
         if i >= args.warmup:
             vals.append(info["value"])
     v = statistics.mean(vals)
-    line = {"impl": "reference", "metric": "accepted tokens/s (0.5B->3B, k=4)", "value": round(v, 3),
+    line = {"impl": "reference", "metric": f"accepted tokens/s (0.5B->3B, k={K_SPEC})", "value": round(v, 3),
             "unit": "accepted tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random ids, random-init weights)",
-            "config": {"workload": "config 4 at k=4: 0.5B-arch draft (seed 1) -> 3B-arch target (seed 2), bf16",
+            "config": {"workload": f"config 4 at k={K_SPEC}: 0.5B-arch draft (seed 1) -> 3B-arch target (seed 2), bf16",
                        "sample_per_step": info["sample"]},
             "cpu_baseline": {"value": round(v, 3), "unit": "accepted tokens/s", "cores": info["cores"],
                              "kind": "port", "sample": info["sample"]},
@@ -592,7 +592,7 @@ def run_serve(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps({
-            "metric": "accepted tokens/s (config 5, continuous batching, k=4)",
+            "metric": f"accepted tokens/s (config 5, continuous batching, k={K_SPEC})",
             "value": round(float(tok.item()) / (float(ms.item()) / 1e3), 2), "unit": "accepted tokens/s",
             "n_gpus": world, "higher_is_better": True, "scaling": "strong",
             "ms_total": round(float(ms.item()), 1), "new_tokens": int(tok.item()),
@@ -620,7 +620,10 @@ def main():
     ap.add_argument("--serve-batch", type=int, default=128, help="running requests per GPU (--serve)")
     ap.add_argument("--serve-blocks", type=int, default=8192, help="KV blocks per pool (--serve)")
     ap.add_argument("--self-draft", action="store_true", help="--serve with the target as its own draft")
+    ap.add_argument("--k", type=int, default=4, help="draft tokens per iteration (config 4 sweeps 1, 2, 4, 8)")
     args = ap.parse_args()
+    global K_SPEC
+    K_SPEC = args.k
     if args.warmup < 3:
         args.warmup = 3
     if args.micro:
