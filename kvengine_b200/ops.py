@@ -42,9 +42,11 @@ class Workspace:
 
 
 def greedy_accept(logits: torch.Tensor, drafts: torch.Tensor, workspace: Workspace | None = None,
-                  status: torch.Tensor | None = None):
+                  status: torch.Tensor | None = None, out=None):
     """logits [B, k+1, V] (fp32/bf16), drafts [B, k] (any int strides) ->
-    (preds [B, k+1], n_accepted [B], emitted [B, k+1]) int32."""
+    (preds [B, k+1], n_accepted [B], emitted [B, k+1]) int32. `out` may give
+    the three contiguous int32 result tensors (they may be views of one buffer,
+    so that a single copy reads n_accepted and emitted back)."""
     lib = L.load()
     L.require_cuda(logits, drafts)
     B, kp1, V = logits.shape
@@ -54,9 +56,15 @@ def greedy_accept(logits: torch.Tensor, drafts: torch.Tensor, workspace: Workspa
     if logits.stride(2) != 1 or logits.stride(0) != kp1 * logits.stride(1):
         raise ValueError("logits rows must be evenly strided with unit column stride")
     dev = logits.device
-    preds = torch.empty(B, kp1, dtype=torch.int32, device=dev)
-    n_acc = torch.empty(B, dtype=torch.int32, device=dev)
-    emitted = torch.empty(B, kp1, dtype=torch.int32, device=dev)
+    if out is None:
+        preds = torch.empty(B, kp1, dtype=torch.int32, device=dev)
+        n_acc = torch.empty(B, dtype=torch.int32, device=dev)
+        emitted = torch.empty(B, kp1, dtype=torch.int32, device=dev)
+    else:
+        preds, n_acc, emitted = out
+        for t, shape in ((preds, (B, kp1)), (n_acc, (B,)), (emitted, (B, kp1))):
+            if t.dtype != torch.int32 or tuple(t.shape) != shape or not t.is_contiguous() or t.device != dev:
+                raise ValueError("greedy_accept out tensors must be contiguous int32 on the logits' device")
     ws = (workspace or Workspace(dev)).get(lib.kve_greedy_accept_workspace_bytes(B))
     L.check(lib.kve_greedy_accept(
         logits.data_ptr(), L.dtype_code(logits.dtype), logits.stride(1), drafts.data_ptr(),

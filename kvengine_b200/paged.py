@@ -90,7 +90,7 @@ class PagedSequenceCache:
         self.blocks: list[int] = []
         self._length = 0
         self._pending_n = 0
-        self._pending_slots: list[int] | None = None
+        self._pending_start: int | None = None  # first position of the reserved, uncommitted tokens
         self._digest_chain: list[bytes] = []
         self._registered = 0
         self.tokens_reused = 0
@@ -124,7 +124,7 @@ class PagedSequenceCache:
         extra = need - len(self.blocks)
         if extra > 0:
             self.blocks.extend(self.pool.manager.allocate(extra, owner=self.request_id))
-        self._pending_slots = self.slot_list(self._length, n_tokens)
+        self._pending_start = self._length  # slots are listed only if write() needs them
         self._pending_n = n_tokens
 
     def slot_list(self, start: int, n_tokens: int) -> list[int]:
@@ -151,9 +151,9 @@ class PagedSequenceCache:
         assert k.shape[0] == 1, "one request per sequence cache"
         n = k.shape[2]
         assert start == self._length, f"write at {start} but sequence length is {self._length}"
-        assert self._pending_slots is not None and self._pending_n == n, (
+        assert self._pending_start == start and self._pending_n == n, (
             "reserve() must be called with this pass's token count before write()")
-        slots = torch.tensor(self._pending_slots, dtype=torch.long, device=self.pool.device)
+        slots = torch.tensor(self.slot_list(start, n), dtype=torch.long, device=self.pool.device)
         k_src = k[0].transpose(0, 1).contiguous()
         v_src = v[0].transpose(0, 1).contiguous()
         ops.kv_append(k_src, v_src, slots, self.pool.k[layer_idx], self.pool.v[layer_idx])
@@ -172,8 +172,21 @@ class PagedSequenceCache:
             raise OutOfBlocks(self.pool.manager.blocks_needed(self._length + n_tokens) - len(self.blocks),
                               self.pool.manager.num_free)
         self._length += n_tokens
-        self._pending_slots = None
+        self._pending_start = None
         self._pending_n = 0
+
+    def commit_and_keep(self, n_tokens: int, keep: int) -> None:
+        """commit(n_tokens) followed by truncate(min(length, keep)) - the per-iteration
+        bookkeeping of the spec loop in one call."""
+        new_len = self._length + n_tokens
+        if new_len > self.capacity:
+            raise OutOfBlocks(self.pool.manager.blocks_needed(new_len) - len(self.blocks),
+                              self.pool.manager.num_free)
+        self._length = new_len
+        self._pending_start = None
+        self._pending_n = 0
+        if keep < new_len:
+            self.truncate(keep)
 
     def truncate(self, n_tokens: int) -> None:
         """Roll back to n_tokens, freeing whole trailing blocks; no data moves (paged.py:344-380)."""
@@ -194,7 +207,7 @@ class PagedSequenceCache:
         self._registered = min(self._registered, first_invalid)
         del self._digest_chain[first_invalid:]
         self._length = n_tokens
-        self._pending_slots = None
+        self._pending_start = None
         self._pending_n = 0
 
     # ------------------------------------------------- prefix sharing
@@ -245,7 +258,7 @@ class PagedSequenceCache:
             self.pool.manager.free(self.blocks)
             self.blocks = []
         self._length = 0
-        self._pending_slots = None
+        self._pending_start = None
         self._pending_n = 0
         self._digest_chain = []
         self._registered = 0

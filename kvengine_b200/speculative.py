@@ -117,6 +117,9 @@ class SpecEngine:
         self.tlog = torch.empty(S * (k + 1), self.V, dtype=self.target.dtype, device=dev)
         self.drafts = torch.empty(k, S, dtype=torch.int32, device=dev)
         self.accept_ws = ops.Workspace(dev)
+        self.preds = torch.empty(S * (k + 1), dtype=torch.int32, device=dev)
+        # emitted [S, k+1] then n_accepted [S]: read back by one copy
+        self.accepted = torch.empty(S * (k + 2), dtype=torch.int32, device=dev)
 
     def _upload(self, slot: int, arrays: list[np.ndarray]) -> list[torch.Tensor]:
         """Copy int32 host arrays to the device in one transfer through pinned
@@ -186,15 +189,17 @@ class SpecEngine:
             ev1.record()
             self.verify_events.append((ev0, ev1, vplan))
         # --- accept (fused argmax + prefix match + bonus)
-        _, n_acc, emitted = ops.greedy_accept(tlog.view(S, k + 1, self.V), drafts.t(), self.accept_ws)
-        n_host = n_acc.cpu().tolist()
-        em_host = emitted.cpu().tolist()
-        self.stats["d2h_bytes"] += (n_acc.numel() + emitted.numel()) * 4
+        ne = S * (k + 1)
+        out = (self.preds[:ne].view(S, k + 1), self.accepted[ne:ne + S], self.accepted[:ne].view(S, k + 1))
+        ops.greedy_accept(tlog.view(S, k + 1, self.V), drafts.t(), self.accept_ws, out=out)
+        back = self.accepted[:ne + S].cpu().numpy()
+        n_host = back[ne:].tolist()
+        em_host = back[:ne].reshape(S, k + 1).tolist()
+        self.stats["d2h_bytes"] += back.nbytes
         self.stats["iterations"] += 1
         self.stats["verify_rows"] += vplan.n_tokens
-        for i, r in enumerate(reqs):
-            n = n_host[i]
-            em = em_host[i][: n + 1]
+        for r, n, row in zip(reqs, n_host, em_host):
+            em = row[: n + 1]
             res = r.res
             res.iterations += 1
             res.tokens_drafted += k
@@ -202,13 +207,11 @@ class SpecEngine:
             res.accepted_per_iter.append(n)
             res.draft_forwards += k
             res.target_forwards += 1
-            r.d_seq.commit(r.u_d + k - 1)
-            r.t_seq.commit(r.u_t + k)
             r.tokens.extend(em)
             res.new_token_ids.extend(em)
             keep = len(r.tokens) - 1
-            r.t_seq.truncate(min(r.t_seq.length, keep))
-            r.d_seq.truncate(min(r.d_seq.length, keep))
+            r.d_seq.commit_and_keep(r.u_d + k - 1, keep)
+            r.t_seq.commit_and_keep(r.u_t + k, keep)
             if eos and any(t in eos for t in em):
                 first = next(j for j, t in enumerate(em) if t in eos)
                 trim = len(em) - (first + 1)

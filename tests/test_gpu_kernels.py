@@ -93,6 +93,13 @@ def test_accept_workspace_stays_zero_and_repeats(cuda_device):
     b = ops.greedy_accept(lg, dr, ws)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+    # results written into views of one caller buffer (emitted, then n_accepted)
+    B, kp1 = dr.shape[0], dr.shape[1] + 1
+    buf = torch.full((B * (kp1 + 1),), -7, dtype=torch.int32, device=cuda_device)
+    preds = torch.empty(B, kp1, dtype=torch.int32, device=cuda_device)
+    c = ops.greedy_accept(lg, dr, ws, out=(preds, buf[B * kp1:], buf[:B * kp1].view(B, kp1)))
+    for x, y in zip(a, c):
+        assert torch.equal(x, y)
 
 
 def test_argmax_rows(cuda_device):
