@@ -177,10 +177,11 @@ int kve_gemm_ex(const void* x, const void* w, int dtype, int m, int n, int k, in
  * every shape; only speed changes. */
 int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_chunks);
 
-/* The tcgen05 GEMM's launch plan for an [m, k] x [n, k]^T product (no kvengine
- * counterpart): out[0..8] = split-K factor, token tiles, token groups per tile,
- * tokens per group, weight halves, k-chunks per stage, pipeline stages, 3-D
- * tensor maps (0/1), feature tiles. */
+/* The tcgen05 GEMM's launch plan for an [m, k] x [n, k]^T product with a bf16
+ * output (no kvengine counterpart): out[0..10] = split-K factor, token tiles,
+ * token groups per tile, tokens per group, weight halves, k-chunks per stage,
+ * pipeline stages, 3-D tensor maps (0/1), feature tiles, CTAs launched (fewer
+ * than the tiles when CTAs walk several tiles), TMEM accumulators per CTA. */
 int kve_gemm_plan_info(int m, int n, int k, int* out);
 
 /* ------------------------------------------------------------------------

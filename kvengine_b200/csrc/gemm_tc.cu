@@ -19,7 +19,10 @@
 // shared memory and the cluster sums them in rank order through distributed
 // shared memory, each CTA finishing a slice of the tokens (no global
 // workspace). The split count depends only on (n, k), so a row's result never
-// depends on m (draft and verify passes agree bit for bit). The epilogue stages
+// depends on m (draft and verify passes agree bit for bit). Launches without
+// split-K that have more tiles than SMs may instead run persistent CTAs that walk
+// several tiles with two TMEM accumulators (gemm_tc_persistent_kernel), where the
+// cost model prices that cheaper (the vocabulary projection of small batches). The epilogue stages
 // each 64-token chunk in shared memory and writes whole rows with 16-byte
 // stores. Every mbarrier wait is bounded; a timeout is reported via `status`.
 #include <cuda.h>
@@ -60,6 +63,10 @@ struct TcArgs {
   int kc;                // 64-wide k-chunks per pipeline stage (one 3-D box each for W and X)
   int tma3d;             // tensor maps are 3-D (64, rows, k/64): box {64, rows, kc}
   uint32_t w_bytes;      // weight bytes per stage (MH x 128 rows x kc chunks)
+  int token_tiles;       // tiles along tokens (tile t: token tile t % token_tiles)
+  int feat_ctas;         // tiles along features (128 x MH weight rows each)
+  int acc_bufs;          // TMEM accumulators per CTA (2: the epilogue overlaps the next tile)
+  int stg_bytes;         // output staging after the stage ring (CTAs that walk several tiles), else 0
   EpiArgs e;
   int* status;
 };
@@ -681,6 +688,267 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   }
 }
 
+// Persistent variant of gemm_tc_kernel for launches without split-K that have
+// more tiles than resident CTAs. Tile t covers tokens [(t % token_tiles) * mt,
+// +mt) and weight rows [(t / token_tiles) * 128 * MH, +128 * MH); CTA b walks
+// tiles b, b + gridDim.x, ..., so the CTAs running at the same time share weight
+// tiles through L2. The stage ring runs on across tiles (the producer loads the
+// next tile while the MMAs of this one drain), and with two TMEM accumulators the
+// epilogue of one tile overlaps the main loop of the next. The output staging sits
+// after the ring, since the ring is never drained between tiles. Each tile's
+// arithmetic is exactly gemm_tc_kernel's, so results are the same bits.
+template <int MODE, bool BF, int NG, int MH>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                          TcArgs a) {
+  using E = Epi<MODE, BF>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // [stages][stage_bytes] | output staging [stg_bytes] | barriers
+  uint8_t* stg = smem + (size_t)a.stages * a.stage_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stg + a.stg_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kMaxStages;
+  uint64_t* acc_full = bars + 2 * kMaxStages;       // [2] accumulator ready (MMA -> epilogue)
+  uint64_t* acc_empty = bars + 2 * kMaxStages + 2;  // [2] accumulator drained (epilogue -> MMA)
+  uint64_t* epi_done = bars + 2 * kMaxStages + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 5);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = a.token_tiles * a.feat_ctas;
+  const int n_stages_work = (a.k_blocks + a.kc - 1) / a.kc;  // pipeline stages of kc k-blocks per tile
+  const int acc_cols = MH * a.mt;                            // TMEM columns of one accumulator
+  uint32_t tmem_cols = 32;
+  while ((int)tmem_cols < a.acc_bufs * acc_cols) tmem_cols <<= 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 4 * kEpiGroups);  // one arrival per epilogue warp
+    }
+    mbar_init(smem_u32(epi_done), 4 * kEpiGroups);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  auto tile_tok0 = [&](int t) { return (t % a.token_tiles) * a.mt; };
+  auto tile_feat0 = [&](int t) { return (t / a.token_tiles) * BM * MH; };
+  // Stage layout as in gemm_tc_kernel.
+  auto load_w = [&](uint8_t* dst, int chunk, int feat0, uint32_t fb) {
+    if (a.tma3d) tma_load_3d(smem_u32(dst), &map_w, 0, feat0, chunk, fb);
+    else tma_load_2d(smem_u32(dst), &map_w, chunk * BK, feat0, fb);
+  };
+  auto load_x = [&](uint8_t* dst, int chunk, int tok0, uint32_t fb) {
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      uint8_t* d = dst + (size_t)g * a.kc * a.n_g * BK * 2;
+      if (a.tma3d) tma_load_3d(smem_u32(d), &map_x, 0, tok0 + g * a.n_g, chunk, fb);
+      else tma_load_2d(smem_u32(d), &map_x, chunk * BK, tok0 + g * a.n_g, fb);
+    }
+  };
+  // Constant weights (w_static): the first tile's first stages of weights are
+  // requested before waiting on the previous kernel.
+  const int pre = a.w_static ? min(n_stages_work, a.stages) : 0;
+  if (warp == 0 && lane == 0) {
+    prefetch_map(&map_w);
+    prefetch_map(&map_x);
+    uint8_t* sa = smem;
+    for (int it = 0; it < pre; ++it, sa += a.stage_bytes) {
+      const uint32_t fb = smem_u32(&full[it]);
+      mbar_add_tx(fb, a.w_bytes);
+      load_w(sa, it * a.kc, tile_feat0(blockIdx.x), fb);
+    }
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  // After a timeout anywhere in this launch every CTA that starts later skips
+  // all of its tiles.
+  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
+  const int tile_first = aborted ? n_tiles : (int)blockIdx.x;
+  const int tile_step = (int)gridDim.x;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- producer
+      int issued = 0, s = 0;
+      uint32_t ph = 0;
+      uint8_t* sa = smem;
+      bool ok = true;
+      for (int tile = tile_first, ti = 0; ok && tile < n_tiles; tile += tile_step, ++ti) {
+        const int tok0 = tile_tok0(tile), feat0 = tile_feat0(tile);
+        int chunk = 0;
+        for (int it = 0; it < n_stages_work; ++it) {
+          if (issued >= a.stages && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, a.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[s]);
+          if (ti == 0 && it < pre) {
+            mbar_expect_tx(fb, a.stage_bytes - a.w_bytes);  // weight tile already requested
+          } else {
+            mbar_expect_tx(fb, a.stage_bytes);
+            load_w(sa, chunk, feat0, fb);
+          }
+          load_x(sa + a.w_bytes, chunk, tok0, fb);
+          ++issued;
+          chunk += a.kc;
+          if (++s == a.stages) {
+            s = 0;
+            ph ^= 1u;
+            sa = smem;
+          } else {
+            sa += a.stage_bytes;
+          }
+        }
+      }
+      // Early weight loads of stages the loop never reached (abort): arrive so
+      // their phase completes once those bytes land.
+      for (int it = issued; it < pre; ++it) mbar_arrive(smem_u32(&full[it]));
+      if (issued < pre) issued = pre;
+      // Do not leave while a bulk copy may still be writing this CTA's shared memory.
+      for (int it = issued - a.stages < 0 ? 0 : issued - a.stages; it < issued; ++it)
+        mbar_wait(smem_u32(&full[it % a.stages]), (uint32_t)(it / a.stages) & 1u, a.status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc(a.n_g);
+      const uint64_t a0 = umma_desc(smem_u32(smem));
+      const uint64_t b0 = umma_desc(smem_u32(smem) + a.w_bytes);
+      const uint64_t stage_step = (uint64_t)(a.stage_bytes >> 4);
+      constexpr uint64_t half_step = (uint64_t)((BM * BK * 2) >> 4);
+      const uint64_t a_chunk = (uint64_t)((MH * BM * BK * 2) >> 4);
+      const uint64_t b_chunk = (uint64_t)((a.n_g * BK * 2) >> 4);
+      const uint64_t grp_step = (uint64_t)((a.kc * a.n_g * BK * 2) >> 4);
+      constexpr uint64_t kstep = (UMMA_K * 2) >> 4;
+      int s = 0;
+      uint32_t ph = 0;
+      uint64_t soff = 0;
+      bool ok = true;
+      for (int tile = tile_first, ti = 0; ok && tile < n_tiles; tile += tile_step, ++ti) {
+        const int ab = a.acc_bufs == 2 ? (ti & 1) : 0;
+        const int use = a.acc_bufs == 2 ? (ti >> 1) : ti;  // earlier tiles in this accumulator
+        if (use > 0) {
+          // The epilogue has drained this accumulator's previous tile.
+          if (!mbar_wait(smem_u32(&acc_empty[ab]), (uint32_t)(use - 1) & 1u, a.status)) break;
+          fence_after();
+        }
+        const uint32_t tacc = tmem_base + (uint32_t)(ab * acc_cols);
+        int chunk = 0;
+        for (int it = 0; it < n_stages_work; ++it) {
+          if (!mbar_wait(smem_u32(&full[s]), ph, a.status)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const int nch = min(a.kc, a.k_blocks - chunk);  // a partial last stage multiplies only real chunks
+          for (int j = 0; j < nch; ++j) {
+            const uint64_t ad = a0 + soff + j * a_chunk, bd = b0 + soff + j * b_chunk;
+#pragma unroll
+            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+              const uint32_t acc = (it > 0 || j > 0 || kk > 0) ? 1u : 0u;
+#pragma unroll
+              for (int h = 0; h < MH; ++h)
+#pragma unroll
+                for (int g = 0; g < NG; ++g)
+                  umma_bf16(tacc + h * a.mt + g * a.n_g, ad + h * half_step + kk * kstep,
+                            bd + g * grp_step + kk * kstep, idesc, acc);
+            }
+          }
+          chunk += a.kc;
+          umma_commit(smem_u32(&empty[s]));
+          if (++s == a.stages) {
+            s = 0;
+            ph ^= 1u;
+            soff = 0;
+          } else {
+            soff += stage_step;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&acc_full[ab]));  // fires once every issued MMA has completed
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    // As gemm_tc_kernel's, per tile, from accumulator ab; then the accumulator is
+    // released to the MMA warp.
+    static_assert(MH == 1 || MH == kEpiGroups, "one epilogue warpgroup per weight half");
+    const int egrp = (warp - 2) / 4;
+    const int half = MH == 1 ? 0 : egrp;
+    const int quad = warp & 3;
+    const int f_local = quad * 32 + lane;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * a.mt);
+    const int etid = (threadIdx.x - 64) & 127;
+    const int first_c0 = MH == 1 ? egrp * kRows : 0;
+    constexpr int kStgBufE = kRows * E::W * E::ES;  // one staging buffer
+    constexpr int kChunkStride = (MH == 1 ? kEpiGroups : 1) * kRows;
+    int it = 0;  // chunks staged so far by this warpgroup (alternates its two buffers)
+    for (int tile = tile_first, ti = 0; tile < n_tiles; tile += tile_step, ++ti) {
+      const int tok0 = tile_tok0(tile);
+      const int fbase = tile_feat0(tile) + half * BM;
+      const int feat = fbase + f_local;
+      const int col0 = MODE == KVE_EPI_SILU_MUL ? fbase / 2 : fbase;
+      const float bias_f = ((MODE == KVE_EPI_BIAS || MODE == kEpiQkvRope) && feat < a.n) ? a.e.bias[feat] : 0.f;
+      uint4 res_first[E::NPASS];  // the first chunk's per-row inputs load while the main loop runs
+      if (first_c0 < a.mt) E::load_res(a, tok0 + first_c0, min(kRows, a.mt - first_c0), col0, etid, res_first);
+      const int ab = a.acc_bufs == 2 ? (ti & 1) : 0;
+      const int use = a.acc_bufs == 2 ? (ti >> 1) : ti;
+      const bool have = mbar_wait(smem_u32(&acc_full[ab]), (uint32_t)use & 1u, a.status);
+      fence_after();
+      const uint32_t t_acc = t_lane + (uint32_t)(ab * acc_cols);
+      bool first = true;
+      for (int c0 = first_c0; c0 < a.mt; c0 += kChunkStride, ++it) {
+        const int n = min(kRows, a.mt - c0);
+        uint8_t* buf = stg + (egrp * 2 + (it & 1)) * kStgBufE;
+        uint4 res[E::NPASS];
+        if (first) {
+#pragma unroll
+          for (int i = 0; i < E::NPASS; ++i) res[i] = res_first[i];
+          first = false;
+        } else {
+          E::load_res(a, tok0 + c0, n, col0, etid, res);
+        }
+        float v[32];
+        tmem_load_cols(t_acc + c0, n, have, v);
+        E::template stage<32>(buf, 0, n, f_local, v, bias_f);
+        epi_bar(egrp);
+        E::copy_out(a, buf, tok0 + c0, n, col0, etid, res);
+      }
+      // Every tcgen05.ld of this warp has completed (wait::ld): release the accumulator.
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[ab]));
+      if (!have) break;
+    }
+    fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(epi_done));
+  }
+  if (warp == 1) {
+    // Free TMEM only after the epilogue is done with it (bounded wait; freed either way).
+    mbar_wait(smem_u32(epi_done), 0, a.status);
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
+                 : "memory");
+  }
+}
+
 // ------------------------------------------------------------------ host
 int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int box_rows) {
   EncodeTiledFn fn = encode_fn();
@@ -718,29 +986,42 @@ struct Plan {
   int mt, ng, n_g, token_tiles, feat_tiles, k_blocks, splits, stages, rch, stg_off;
   int mh, kc, tma3d;  // weight halves per CTA, k-chunks per stage, 3-D tensor maps
   uint32_t stage_bytes, w_bytes;
+  int grid_x;         // CTAs without split-K (fewer than the tiles when persistent)
+  int acc_bufs, stg_bytes;
 };
 
 typedef void (*GemmKernel)(CUtensorMap, CUtensorMap, TcArgs);
 
-template <int NG, int MH>
+template <int MODE, bool BF, int NG, int MH, bool P>
+GemmKernel kernel_of() {
+  if constexpr (P) return gemm_tc_persistent_kernel<MODE, BF, NG, MH>;
+  else return gemm_tc_kernel<MODE, BF, NG, MH>;
+}
+
+template <int NG, int MH, bool P>
 GemmKernel kernel_for_shape(int mode, bool bf) {
   switch (mode) {
     case KVE_EPI_BIAS:
-      return bf ? gemm_tc_kernel<KVE_EPI_BIAS, true, NG, MH> : gemm_tc_kernel<KVE_EPI_BIAS, false, NG, MH>;
+      return bf ? kernel_of<KVE_EPI_BIAS, true, NG, MH, P>() : kernel_of<KVE_EPI_BIAS, false, NG, MH, P>();
     case KVE_EPI_RESIDUAL:
-      return bf ? gemm_tc_kernel<KVE_EPI_RESIDUAL, true, NG, MH> : gemm_tc_kernel<KVE_EPI_RESIDUAL, false, NG, MH>;
+      return bf ? kernel_of<KVE_EPI_RESIDUAL, true, NG, MH, P>() : kernel_of<KVE_EPI_RESIDUAL, false, NG, MH, P>();
     case KVE_EPI_SILU_MUL:
-      return bf ? gemm_tc_kernel<KVE_EPI_SILU_MUL, true, NG, MH> : gemm_tc_kernel<KVE_EPI_SILU_MUL, false, NG, MH>;
-    case kEpiQkvRope: return bf ? gemm_tc_kernel<kEpiQkvRope, true, NG, MH> : nullptr;  // bf16 only
-    default: return bf ? gemm_tc_kernel<KVE_EPI_STORE, true, NG, MH> : gemm_tc_kernel<KVE_EPI_STORE, false, NG, MH>;
+      return bf ? kernel_of<KVE_EPI_SILU_MUL, true, NG, MH, P>() : kernel_of<KVE_EPI_SILU_MUL, false, NG, MH, P>();
+    case kEpiQkvRope: return bf ? kernel_of<kEpiQkvRope, true, NG, MH, P>() : nullptr;  // bf16 only
+    default: return bf ? kernel_of<KVE_EPI_STORE, true, NG, MH, P>() : kernel_of<KVE_EPI_STORE, false, NG, MH, P>();
   }
 }
 
-// Token groups x weight halves: (1, 1), (2, 1) for tiles above 256 tokens, (1, 2).
-GemmKernel kernel_for(int mode, int out_dtype, int ng, int mh) {
+// Token groups x weight halves: (1, 1), (2, 1) for tiles above 256 tokens, (1, 2);
+// one tile per CTA or persistent.
+GemmKernel kernel_for(int mode, int out_dtype, int ng, int mh, bool persist) {
   const bool bf = out_dtype == KVE_BF16;
-  if (mh == 2) return kernel_for_shape<1, 2>(mode, bf);
-  return ng == 2 ? kernel_for_shape<2, 1>(mode, bf) : kernel_for_shape<1, 1>(mode, bf);
+  if (persist) {
+    if (mh == 2) return kernel_for_shape<1, 2, true>(mode, bf);
+    return ng == 2 ? kernel_for_shape<2, 1, true>(mode, bf) : kernel_for_shape<1, 1, true>(mode, bf);
+  }
+  if (mh == 2) return kernel_for_shape<1, 2, false>(mode, bf);
+  return ng == 2 ? kernel_for_shape<2, 1, false>(mode, bf) : kernel_for_shape<1, 1, false>(mode, bf);
 }
 
 void configure_kernel() {
@@ -748,10 +1029,11 @@ void configure_kernel() {
   std::call_once(once, [] {
     for (int mode = KVE_EPI_STORE; mode <= kEpiQkvRope; ++mode)
       for (int dt : {KVE_F32, KVE_BF16})
-        for (int shape = 0; shape < 3; ++shape) {
-          GemmKernel kern = kernel_for(mode, dt, shape == 1 ? 2 : 1, shape == 2 ? 2 : 1);
-          if (kern) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
-        }
+        for (int shape = 0; shape < 3; ++shape)
+          for (bool persist : {false, true}) {
+            GemmKernel kern = kernel_for(mode, dt, shape == 1 ? 2 : 1, shape == 2 ? 2 : 1, persist);
+            if (kern) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
+          }
   });
 }
 
@@ -778,7 +1060,7 @@ const int* cluster_capacity() {
       cfg.attrs = &attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(KVE_EPI_STORE, KVE_BF16, 1, 1), &cfg) == cudaSuccess && n > 0)
+      if (cudaOccupancyMaxActiveClusters(&n, kernel_for(KVE_EPI_STORE, KVE_BF16, 1, 1, false), &cfg) == cudaSuccess && n > 0)
         cap[s] = n * s;
     }
     cudaGetLastError();
@@ -795,9 +1077,18 @@ const int* cluster_capacity() {
 // * a cluster exchange costs a fixed part plus a part per token of the tile;
 // * the epilogue costs a fixed part plus a part per token each warpgroup drains.
 constexpr double kLoadLatencyUs = 2.0;
-double stage_us(int mh, int ng, int mt, int kc) {
+constexpr size_t kAvail = kSmemLimit - 2048;  // stage ring budget (alignment slack, barriers, margin)
+// Output staging a CTA that walks several tiles keeps beside its stage ring (the
+// ring is never drained between tiles): two buffers of kRows staged output rows
+// per epilogue warpgroup; row_bytes is one staged row (128 outputs, 64 for SwiGLU).
+size_t persist_staging(int row_bytes) { return (size_t)kEpiGroups * 2 * kRows * row_bytes; }
+// A CTA's fixed cost outside its main loop: barrier and TMEM set-up and the first
+// load round trip (measured: a persistent walk over 9 tiles saved about 2.3 us per
+// tile against nine waves of one-tile CTAs with the same stages).
+constexpr double kStartUs = 2.0;
+double stage_us(int mh, int ng, int mt, int kc, size_t avail) {
   const size_t bytes = (size_t)(mh * BM + mt) * BK * 2 * kc;
-  int stages = (int)((kSmemLimit - 2048) / bytes);
+  int stages = (int)(avail / bytes);
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return 1e9;
   const double issue = 0.12 + 0.10 * (1 + ng) * kc;
@@ -814,17 +1105,29 @@ inline int round16(int x) { return (x + 15) / 16 * 16; }
 // 128 rows per CTA, kc k-chunks of 64 per pipeline stage.
 struct TileConfig {
   int token_tiles, ng, n_g, mh, kc;
+  bool persist;  // CTAs walk several tiles (no split-K, more tiles than resident CTAs)
   double us;
 };
 
-double config_us(int feat_tiles, int k_blocks, int s, const TileConfig& c) {
+// A persistent launch: each CTA walks ceil(tiles / CTAs) tiles with its stage ring
+// running on across tiles; the epilogue overlaps the next tile's main loop when
+// two TMEM accumulators fit, else it follows every tile. The staging it keeps
+// beside the ring leaves fewer stages in flight. `legacy` prices the one-tile-per-
+// CTA launches only, without start costs (the model the split factor is chosen by).
+double config_us(int feat_tiles, int k_blocks, int s, const TileConfig& c, int row_bytes, bool legacy) {
   const int* cap = cluster_capacity();
   const long long ctas = (long long)((feat_tiles + c.mh - 1) / c.mh) * c.token_tiles * s;
   const long long waves = (ctas + cap[s] - 1) / cap[s];
   const int mt = c.ng * c.n_g;
   const int iters = ((k_blocks + s - 1) / s + c.kc - 1) / c.kc;
   const int per_group = c.mh == 1 ? (mt + kEpiGroups - 1) / kEpiGroups : mt;
-  return waves * (iters * stage_us(c.mh, c.ng, mt, c.kc) + exchange_us(mt, s) + epilogue_us(per_group));
+  const double epi = epilogue_us(per_group);
+  if (c.persist) {
+    const double main = iters * stage_us(c.mh, c.ng, mt, c.kc, kAvail - persist_staging(row_bytes));
+    return kStartUs + (2 * c.mh * mt <= 512 ? waves * fmax(main, epi) + epi : waves * (main + epi));
+  }
+  const double per_wave = iters * stage_us(c.mh, c.ng, mt, c.kc, kAvail) + exchange_us(mt, s) + epi;
+  return waves * (per_wave + (legacy ? 0.0 : kStartUs));
 }
 
 TileConfig token_tiling(int m, int t) {
@@ -851,18 +1154,20 @@ TileConfig token_tiling(int m, int t) {
 // activation tile) measured faster only for prompt-sized batches (m >= kLargeM).
 // None of these choices changes a row's reduction order.
 constexpr int kLargeM = 2048;
-int chunks_for(int mh, int mt, int s, bool tma3d) {
+int chunks_for(int mh, int mt, int s, bool tma3d, size_t avail) {
   if (s > 1 || !tma3d) return 1;
   for (int kc = 4; kc > 1; kc /= 2)
-    if ((size_t)(mh * BM + mt) * BK * 2 * kc * 2 <= kSmemLimit - 2048) return kc;
+    if ((size_t)(mh * BM + mt) * BK * 2 * kc * 2 <= avail) return kc;
   return 1;
 }
 
-TileConfig best_config(int m, int feat_tiles, int k_blocks, int s, bool tma3d) {
+TileConfig best_config(int m, int feat_tiles, int k_blocks, int s, bool tma3d, int row_bytes, bool legacy) {
   int t_min = (m + 383) / 384;
   if (t_min < 1) t_min = 1;
-  TileConfig best = token_tiling(m, t_min);
-  best.us = 1e30;
+  // The best one-tile-per-CTA shape (by the model without start costs, which
+  // ranks those shapes as measured) and the best persistent shape.
+  TileConfig best = token_tiling(m, t_min), best_p = best;
+  best.us = best_p.us = 1e30;
   for (int t = t_min; t <= (m + 15) / 16; ++t) {
     TileConfig c = token_tiling(m, t);
     const int mt = c.ng * c.n_g;
@@ -870,12 +1175,22 @@ TileConfig best_config(int m, int feat_tiles, int k_blocks, int s, bool tma3d) {
     for (int mh = 1; mh <= (m >= kLargeM ? 2 : 1); ++mh) {
       if (mh == 2 && (s > 1 || c.ng == 2 || mt > 256 || feat_tiles < 2)) continue;
       c.mh = mh;
-      c.kc = chunks_for(mh, mt, s, tma3d);
-      c.us = config_us(feat_tiles, k_blocks, s, c);
+      c.persist = false;
+      c.kc = chunks_for(mh, mt, s, tma3d, kAvail);
+      c.us = config_us(feat_tiles, k_blocks, s, c, row_bytes, true);
       if (c.us < best.us * 0.97) best = c;
+      const long long ctas = (long long)((feat_tiles + mh - 1) / mh) * t * s;
+      if (!legacy && s == 1 && ctas > cluster_capacity()[1]) {
+        c.persist = true;
+        c.kc = chunks_for(mh, mt, s, tma3d, kAvail - persist_staging(row_bytes));
+        c.us = config_us(feat_tiles, k_blocks, s, c, row_bytes, false);
+        if (c.us < best_p.us * 0.97) best_p = c;
+      }
     }
   }
-  return best;
+  if (legacy) return best;
+  best.us = config_us(feat_tiles, k_blocks, s, best, row_bytes, false);  // with its start costs
+  return best_p.us < best.us * 0.97 ? best_p : best;
 }
 
 // Split-K factor: a function of (n, k) only, so a row's reduction order never
@@ -890,7 +1205,7 @@ int choose_splits(int feat_tiles, int k_blocks, bool tma3d) {
   for (int s = 1; s <= kMaxSplits; ++s) {
     if (s > 1 && k_blocks / s < 2) break;
     double t = 0;
-    for (int m_ref : {16, 64, 256}) t += best_config(m_ref, feat_tiles, k_blocks, s, tma3d).us;
+    for (int m_ref : {16, 64, 256}) t += best_config(m_ref, feat_tiles, k_blocks, s, tma3d, 256, true).us;
     if (t < best_t - 1e-9) {
       best_t = t;
       best = s;
@@ -902,13 +1217,13 @@ int choose_splits(int feat_tiles, int k_blocks, bool tma3d) {
 // Shape forced through kve_gemm_force_shape (0 = the model's choice).
 std::atomic<int> g_force_t{0}, g_force_mh{0}, g_force_kc{0};
 
-Plan make_plan_uncached(int m, int n, int k) {
+Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
   Plan p{};
   p.feat_tiles = (n + BM - 1) / BM;
   p.k_blocks = (k + BK - 1) / BK;
   p.tma3d = k % BK == 0;
   p.splits = choose_splits(p.feat_tiles, p.k_blocks, p.tma3d);
-  TileConfig c = best_config(m, p.feat_tiles, p.k_blocks, p.splits, p.tma3d);
+  TileConfig c = best_config(m, p.feat_tiles, p.k_blocks, p.splits, p.tma3d, row_bytes, false);
   // A forced shape applies where it is valid for this GEMM; it never touches the
   // split factor, so results are the same bits either way.
   const int ft = g_force_t.load(), fmh = g_force_mh.load(), fkc = g_force_kc.load();
@@ -916,6 +1231,7 @@ Plan make_plan_uncached(int m, int n, int k) {
     TileConfig f = token_tiling(m, ft < (m + 15) / 16 ? ft : (m + 15) / 16);
     f.mh = c.mh;
     f.kc = c.kc;
+    f.persist = c.persist;
     if (f.ng == 2 || (long long)f.ng * f.n_g > 256) f.mh = 1;
     c = f;
   }
@@ -923,11 +1239,20 @@ Plan make_plan_uncached(int m, int n, int k) {
   if (fmh == 2 && p.splits == 1 && c.ng == 1 && c.n_g <= 256 && p.feat_tiles >= 2) c.mh = 2;
   if (fkc > 0 && (fkc == 1 || (p.splits == 1 && p.tma3d))) c.kc = fkc;
   // ... and is shrunk until two pipeline stages fit in shared memory.
+  // A forced shape with no more tiles than resident CTAs runs one tile per CTA.
+  auto tiles_of = [&](const TileConfig& t) { return (long long)((p.feat_tiles + t.mh - 1) / t.mh) * t.token_tiles; };
+  auto persist_of = [&](const TileConfig& t) {
+    return t.persist && p.splits == 1 && tiles_of(t) > cluster_capacity()[1];
+  };
+  auto avail_of = [&](const TileConfig& t) { return kAvail - (persist_of(t) ? persist_staging(row_bytes) : 0); };
   auto fits = [&](const TileConfig& t) {
-    return (size_t)(t.mh * BM + t.ng * t.n_g) * BK * 2 * t.kc * 2 <= kSmemLimit - 2048;
+    return (size_t)(t.mh * BM + t.ng * t.n_g) * BK * 2 * t.kc * 2 <= avail_of(t);
   };
   while (!fits(c) && c.kc > 1) c.kc /= 2;
-  if (!fits(c)) c.mh = 1;
+  if (!fits(c)) {
+    c.mh = 1;
+    while (!fits(c) && c.kc > 1) c.kc /= 2;
+  }
   p.token_tiles = c.token_tiles;
   p.ng = c.ng;
   p.n_g = c.n_g;
@@ -936,7 +1261,18 @@ Plan make_plan_uncached(int m, int n, int k) {
   p.mt = p.ng * p.n_g;
   p.w_bytes = (uint32_t)(p.mh * BM * BK * 2 * p.kc);
   p.stage_bytes = (uint32_t)(p.w_bytes + p.mt * BK * 2 * p.kc);
-  size_t avail = kSmemLimit - 2048 /*align slack + barriers + margin*/;
+  const long long tiles = tiles_of(c);
+  const bool persist = persist_of(c);
+  size_t avail = avail_of(c);
+  p.stg_bytes = persist ? (int)persist_staging(row_bytes) : 0;
+  p.acc_bufs = persist && 2 * p.mh * p.mt <= 512 ? 2 : 1;
+  if (persist) {
+    const long long cap = cluster_capacity()[1];
+    const long long rounds = (tiles + cap - 1) / cap;
+    p.grid_x = (int)((tiles + rounds - 1) / rounds);  // balanced: every CTA walks rounds or rounds - 1 tiles
+  } else {
+    p.grid_x = (int)tiles;
+  }
   p.stages = (int)(avail / p.stage_bytes);
   if (p.stages > kMaxStages) p.stages = kMaxStages;
   p.rch = p.mt;
@@ -965,17 +1301,18 @@ Plan make_plan_uncached(int m, int n, int k) {
 std::mutex g_plan_mu;
 std::unordered_map<uint64_t, Plan> g_plan_cache;
 
-Plan make_plan(int m, int n, int k) {
+Plan make_plan(int m, int n, int k, int row_bytes) {
   std::mutex& mu = g_plan_mu;
   std::unordered_map<uint64_t, Plan>& cache = g_plan_cache;
-  const bool key_ok = m < (1 << 20) && n < (1 << 24) && k < (1 << 20);
-  const uint64_t key = ((uint64_t)m << 44) | ((uint64_t)n << 20) | (uint64_t)k;
+  const bool key_ok = m < (1 << 18) && n < (1 << 24) && k < (1 << 20) && row_bytes >= 128 && row_bytes <= 512;
+  const uint64_t rb_code = row_bytes == 128 ? 1 : row_bytes == 256 ? 2 : 3;  // 128 / 256 / 512
+  const uint64_t key = (rb_code << 62) | ((uint64_t)m << 44) | ((uint64_t)n << 20) | (uint64_t)k;
   if (key_ok) {
     std::lock_guard<std::mutex> g(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  Plan p = make_plan_uncached(m, n, k);
+  Plan p = make_plan_uncached(m, n, k, row_bytes);
   if (key_ok) {
     std::lock_guard<std::mutex> g(mu);
     if (cache.size() > 4096) cache.clear();
@@ -996,7 +1333,9 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   if (e.mode == KVE_EPI_SILU_MUL && (n % 2))
     return set_error(KVE_ERR_SHAPE, "kve_gemm: SILU_MUL needs an even n");
   configure_kernel();
-  Plan p = make_plan(m, n, k);
+  // Bytes of one staged output row: 128 outputs (64 for SwiGLU) of the output type.
+  const int row_bytes = (e.mode == KVE_EPI_SILU_MUL ? BM / 2 : BM) * (e.out_dtype == KVE_BF16 ? 2 : 4);
+  Plan p = make_plan(m, n, k, row_bytes);
   if (p.stages < 2 || (p.splits > 1 && p.rch == 0))
     return set_error(KVE_ERR_SHAPE, "kve_gemm(tcgen05): tile does not fit shared memory");
   TcArgs a{};
@@ -1005,10 +1344,13 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   a.rch = p.rch; a.stg_off = p.stg_off;
   a.w_static = e.w_static;
   a.kc = p.kc; a.tma3d = p.tma3d; a.w_bytes = p.w_bytes;
+  a.token_tiles = p.token_tiles; a.feat_ctas = (p.feat_tiles + p.mh - 1) / p.mh;
+  a.acc_bufs = p.acc_bufs; a.stg_bytes = p.stg_bytes;
   const int es = e.out_dtype == KVE_BF16 ? 2 : 4;
   a.out_vec_ok = ((uintptr_t)e.out % 16 == 0) && ((size_t)e.ld_out * es % 16 == 0) &&
                  (e.mode != KVE_EPI_RESIDUAL || (uintptr_t)e.residual % 16 == 0);
-  GemmKernel kern = kernel_for(e.mode, e.out_dtype, p.ng, p.mh);
+  const bool persist = p.stg_bytes > 0;
+  GemmKernel kern = kernel_for(e.mode, e.out_dtype, p.ng, p.mh, persist);
   if (!kern) return set_error(KVE_ERR_DTYPE, "kve_gemm(tcgen05): epilogue %d needs bf16 output", e.mode);
   CUtensorMap mw, mx;
   int rc = p.tma3d ? make_map3(&mw, w, n, k, BM * p.mh, p.kc) : make_map(&mw, w, n, k, BM * p.mh);
@@ -1020,9 +1362,9 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   attr.val.clusterDim.x = 1;
   attr.val.clusterDim.y = 1;
   attr.val.clusterDim.z = p.splits;
-  cudaError_t err = launch_kernel_ex(kern,
-                                     dim3(p.token_tiles, (p.feat_tiles + p.mh - 1) / p.mh, p.splits),
-                                     dim3(kThreads), (size_t)p.stages * p.stage_bytes + 1024 + 512, stream, &attr,
+  const dim3 grid = persist ? dim3(p.grid_x, 1, 1) : dim3(p.token_tiles, a.feat_ctas, p.splits);
+  cudaError_t err = launch_kernel_ex(kern, grid, dim3(kThreads),
+                                     (size_t)p.stages * p.stage_bytes + p.stg_bytes + 1024 + 512, stream, &attr,
                                      p.splits > 1 ? 1 : 0, mw, mx, a);
   if (err != cudaSuccess) {
     cudaGetLastError();
@@ -1065,9 +1407,10 @@ extern "C" int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_ch
 extern "C" int kve_gemm_plan_info(int m, int n, int k, int* out) {
   using namespace kve;
   if (m < 1 || n < 1 || k < 1 || !out) return set_error(KVE_ERR_ARG, "kve_gemm_plan_info: bad arguments");
-  const Plan p = make_plan(m, n, k);
-  const int v[9] = {p.splits, p.token_tiles, p.ng, p.n_g, p.mh, p.kc, p.stages, p.tma3d,
-                    (p.feat_tiles + p.mh - 1) / p.mh};
-  for (int i = 0; i < 9; ++i) out[i] = v[i];
+  const Plan p = make_plan(m, n, k, BM * 2);
+  const int v[11] = {p.splits, p.token_tiles, p.ng, p.n_g, p.mh, p.kc, p.stages, p.tma3d,
+                     (p.feat_tiles + p.mh - 1) / p.mh, p.splits > 1 ? p.token_tiles * ((p.feat_tiles + p.mh - 1) / p.mh) * p.splits : p.grid_x,
+                     p.acc_bufs};
+  for (int i = 0; i < 11; ++i) out[i] = v[i];
   return KVE_OK;
 }

@@ -210,8 +210,9 @@ class SpecEngine:
             r.tokens.extend(em)
             res.new_token_ids.extend(em)
             keep = len(r.tokens) - 1
-            r.d_seq.commit_and_keep(r.u_d + k - 1, keep)
+            # target before draft: the order rejected blocks return to the free list
             r.t_seq.commit_and_keep(r.u_t + k, keep)
+            r.d_seq.commit_and_keep(r.u_d + k - 1, keep)
             if eos and any(t in eos for t in em):
                 first = next(j for j, t in enumerate(em) if t in eos)
                 trim = len(em) - (first + 1)

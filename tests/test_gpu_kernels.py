@@ -358,9 +358,11 @@ def test_gemm_tcgen05_bf16(cuda_device, m, n, k):
 
 
 @pytest.mark.parametrize("algo", [L.GEMM_SIMT, L.GEMM_TCGEN05])
-@pytest.mark.parametrize("m,n,k", [(33, 512, 256), (40, 19200, 256), (320, 2560, 2048), (7, 1000, 136)])
+@pytest.mark.parametrize("m,n,k", [(33, 512, 256), (40, 19200, 256), (320, 2560, 2048), (7, 1000, 136),
+                                   (330, 40000, 128)])
 def test_gemm_epilogues(cuda_device, algo, m, n, k):
-    """BIAS / RESIDUAL (in place) / SILU_MUL on split-K (cluster) and unsplit tilings."""
+    """BIAS / RESIDUAL (in place) / SILU_MUL on split-K (cluster) and unsplit tilings,
+    and on persistent launches (more tiles than SMs: 150 and 939 tiles)."""
     dt = torch.bfloat16 if algo == L.GEMM_TCGEN05 else torch.float32
     g = torch.Generator().manual_seed(11)
     x = torch.randn(m, k, generator=g).to(dt)
@@ -390,7 +392,7 @@ def test_gemm_epilogues(cuda_device, algo, m, n, k):
 def test_gemm_rows_are_batch_invariant(cuda_device, algo, dt):
     """Row r of x @ w^T is bit-identical for m = 1, 5, 64, 320, 600 (with split-K shapes too)."""
     g = torch.Generator().manual_seed(12)
-    for n, k in ((2560, 2048), (896, 4864), (1024, 256)):
+    for n, k in ((2560, 2048), (896, 4864), (1024, 256), (19200, 256)):
         x = torch.randn(600, k, generator=g).to(dt).to(cuda_device)
         w = (torch.randn(n, k, generator=g) * 0.05).to(dt).to(cuda_device)
         full = ops.gemm(x, w, out_dtype=torch.float32, algo=algo)
@@ -404,12 +406,14 @@ def test_gemm_rows_are_batch_invariant(cuda_device, algo, dt):
 @pytest.mark.gpu
 def test_gemm_launch_shapes_give_identical_bits(cuda_device):
     """Token tiles, weight halves per CTA and k-chunks per pipeline stage change
-    speed only: every forced shape reproduces the model-chosen result exactly."""
+    speed only: every forced shape reproduces the model-chosen result exactly
+    (the last three cases run persistent CTAs, with one or two TMEM accumulators)."""
     lib = L.load()
     g = torch.Generator(device=cuda_device).manual_seed(11)
     cases = [(320, 2560, 2048, L.EPI_BIAS), (64, 9728, 896, L.EPI_SILU_MUL), (320, 4096, 2048, L.EPI_SILU_MUL),
              (300, 1000, 136, L.EPI_STORE), (64, 896, 4864, L.EPI_RESIDUAL), (17, 512, 256, L.EPI_STORE),
-             (160, 1024, 512, L.EPI_RESIDUAL)]
+             (160, 1024, 512, L.EPI_RESIDUAL), (330, 40000, 128, L.EPI_STORE), (64, 19200, 256, L.EPI_RESIDUAL),
+             (300, 20000, 192, L.EPI_SILU_MUL)]
     shapes = [(1, 1, 1), (1, 2, 1), (2, 2, 2), (4, 1, 4), (3, 2, 4), (7, 1, 2), (2, 1, 2)]
     try:
         for m, n, k, epi in cases:
