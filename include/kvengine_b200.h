@@ -177,11 +177,18 @@ int kve_gemm_ex(const void* x, const void* w, int dtype, int m, int n, int k, in
  * every shape; only speed changes. */
 int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_chunks);
 
+/* Tuning and test hook (no kvengine counterpart): whether later tcgen05 GEMMs
+ * without split-K run as CTA pairs (2-CTA MMA on 256-row tiles): 0 = the cost
+ * model's choice, 1 = never, 2 = wherever the shape allows. Results are
+ * bit-identical either way. */
+int kve_gemm_force_pair(int mode);
+
 /* The tcgen05 GEMM's launch plan for an [m, k] x [n, k]^T product with a bf16
- * output (no kvengine counterpart): out[0..10] = split-K factor, token tiles,
+ * output (no kvengine counterpart): out[0..11] = split-K factor, token tiles,
  * token groups per tile, tokens per group, weight halves, k-chunks per stage,
- * pipeline stages, 3-D tensor maps (0/1), feature tiles, CTAs launched (fewer
- * than the tiles when CTAs walk several tiles), TMEM accumulators per CTA. */
+ * pipeline stages, 3-D tensor maps (0/1), tiles along the features (of 128 x
+ * weight halves rows, or 256 rows for CTA pairs), CTAs launched (fewer than the
+ * tiles when CTAs walk several tiles), TMEM accumulators per CTA, CTA pairs (0/1). */
 int kve_gemm_plan_info(int m, int n, int k, int* out);
 
 /* ------------------------------------------------------------------------

@@ -949,6 +949,309 @@ gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap map_w, const __gri
   }
 }
 
+// ---------------------------------------------------------- CTA-pair variant
+// 2-CTA MMA (tcgen05 cta_group::2): the two CTAs of a cluster pair compute one
+// 256-weight-row tile. Each holds its own 128 weight rows and HALF of the tile's
+// tokens in shared memory; one MMA of M = 256 reads both CTAs' operands, and each
+// CTA's TMEM receives its 128 rows x all tokens. Per SM this loads half the
+// activation bytes of gemm_tc_kernel for the same work, which is what bounds the
+// wide projections (gate_up, the vocabulary projection) at verify batches.
+// Protocol: both CTAs' TMA loads signal the leader's (rank 0) full barriers, for
+// which the leader expects both CTAs' bytes; the leader's single MMA thread issues
+// every MMA and commits each stage's release and each tile's completion to the
+// barriers of both CTAs (two commits, one per CTA); both epilogues drain their
+// own TMEM and arrive on the leader's accumulator-empty barrier. Tiles are walked
+// as in gemm_tc_persistent_kernel; a tile's arithmetic per output element is the
+// same K-ordered MMA chain as gemm_tc_kernel's.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                               uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Arrive (once the issuing thread's earlier MMAs complete) on an mbarrier of
+// either CTA of the pair, given by its shared::cluster address.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+// TMA into this CTA's shared memory, completing bytes on an mbarrier of either CTA of the pair.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// Instruction descriptor, kind::f16: D fp32, A/B bf16, both K-major, M = 256 (pair), N = n.
+__device__ __forceinline__ uint32_t umma_idesc_pair(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
+}
+
+template <int MODE, bool BF, int NG>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, TcArgs a) {
+  using E = Epi<MODE, BF>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // [stages][stage_bytes] | output staging [stg_bytes] | barriers; the same offsets in both CTAs.
+  uint8_t* stg = smem + (size_t)a.stages * a.stage_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stg + a.stg_bytes);
+  uint64_t* full = bars;                            // leader's: both CTAs' bytes of a stage
+  uint64_t* empty = bars + kMaxStages;              // each CTA's own: stage consumed
+  uint64_t* acc_full = bars + 2 * kMaxStages;       // [2] each CTA's own: accumulator ready
+  uint64_t* acc_empty = bars + 2 * kMaxStages + 2;  // [2] leader's: drained by both epilogues
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int half_n = a.n_g >> 1;                             // tokens of a group held by each CTA
+  const int n_tiles = a.token_tiles * a.feat_ctas;           // pair tiles of 256 weight rows
+  const int n_stages_work = (a.k_blocks + a.kc - 1) / a.kc;
+  const int acc_cols = a.mt;
+  uint32_t tmem_cols = 32;
+  while ((int)tmem_cols < a.acc_bufs * acc_cols) tmem_cols <<= 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 2 * 4 * kEpiGroups);  // every epilogue warp of both CTAs
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  // Both CTAs' barriers are initialised (and TMEM allocated) before either CTA
+  // signals the other's.
+  fence_before();
+  cluster_sync();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t lead_full = map_to(smem_u32(full), 0);  // leader's full[0]; entries 8 bytes apart
+  const uint32_t lead_acc_empty = map_to(smem_u32(acc_empty), 0);
+  const uint32_t peer_empty = map_to(smem_u32(empty), rank ^ 1u);
+  const uint32_t peer_acc_full = map_to(smem_u32(acc_full), rank ^ 1u);
+  auto tile_tok0 = [&](int t) { return (t % a.token_tiles) * a.mt; };
+  auto tile_feat0 = [&](int t) { return (t / a.token_tiles) * 2 * BM + (int)rank * BM; };  // this CTA's rows
+  // Stage layout: weights [kc][128][64], then per token group this CTA's half
+  // [kc][n_g / 2][64] (SW128 K-major slabs).
+  auto load_w = [&](uint8_t* dst, int chunk, int feat0, uint32_t fb) {
+    if (a.tma3d) tma_load_3d_pair(smem_u32(dst), &map_w, 0, feat0, chunk, fb);
+    else tma_load_2d_pair(smem_u32(dst), &map_w, chunk * BK, feat0, fb);
+  };
+  auto load_x = [&](uint8_t* dst, int chunk, int tok0, uint32_t fb) {
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      uint8_t* d = dst + (size_t)g * a.kc * half_n * BK * 2;
+      const int row = tok0 + g * a.n_g + (int)rank * half_n;
+      if (a.tma3d) tma_load_3d_pair(smem_u32(d), &map_x, 0, row, chunk, fb);
+      else tma_load_2d_pair(smem_u32(d), &map_x, chunk * BK, row, fb);
+    }
+  };
+  const int pre = a.w_static ? min(n_stages_work, a.stages) : 0;
+  const int pair_idx = (int)(blockIdx.x >> 1);
+  if (warp == 0 && lane == 0) {
+    prefetch_map(&map_w);
+    prefetch_map(&map_x);
+    uint8_t* sa = smem;
+    for (int it = 0; it < pre; ++it, sa += a.stage_bytes) {
+      if (leader) mbar_add_tx(smem_u32(&full[it]), 2 * a.w_bytes);
+      load_w(sa, it * a.kc, tile_feat0(pair_idx), lead_full + 8u * it);
+    }
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
+  const int tile_first = aborted ? n_tiles : pair_idx;
+  const int tile_step = (int)(gridDim.x >> 1);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- producer
+      int issued = 0, s = 0;
+      uint32_t ph = 0;
+      uint8_t* sa = smem;
+      bool ok = true;
+      for (int tile = tile_first, ti = 0; ok && tile < n_tiles; tile += tile_step, ++ti) {
+        const int tok0 = tile_tok0(tile), feat0 = tile_feat0(tile);
+        int chunk = 0;
+        for (int it = 0; it < n_stages_work; ++it) {
+          if (issued >= a.stages && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, a.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = lead_full + 8u * s;
+          if (ti == 0 && it < pre) {
+            if (leader) mbar_expect_tx(smem_u32(&full[s]), 2 * (a.stage_bytes - a.w_bytes));
+          } else {
+            if (leader) mbar_expect_tx(smem_u32(&full[s]), 2 * a.stage_bytes);
+            load_w(sa, chunk, feat0, fb);
+          }
+          load_x(sa + a.w_bytes, chunk, tok0, fb);
+          ++issued;
+          chunk += a.kc;
+          if (++s == a.stages) {
+            s = 0;
+            ph ^= 1u;
+            sa = smem;
+          } else {
+            sa += a.stage_bytes;
+          }
+        }
+      }
+      if (leader) {
+        // Early weight loads of stages the loop never reached (abort): arrive so
+        // their phase completes once the bytes land. Then wait for the bytes of
+        // the last stages of both CTAs, so that neither leaves with a copy in flight.
+        for (int it = issued; it < pre; ++it) mbar_arrive(smem_u32(&full[it]));
+        if (issued < pre) issued = pre;
+        for (int it = issued - a.stages < 0 ? 0 : issued - a.stages; it < issued; ++it)
+          mbar_wait(smem_u32(&full[it % a.stages]), (uint32_t)(it / a.stages) & 1u, a.status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue (leader)
+    if (leader && lane == 0) {
+      const uint32_t idesc = umma_idesc_pair(a.n_g);
+      const uint64_t a0 = umma_desc(smem_u32(smem));
+      const uint64_t b0 = umma_desc(smem_u32(smem) + a.w_bytes);
+      const uint64_t stage_step = (uint64_t)(a.stage_bytes >> 4);
+      const uint64_t a_chunk = (uint64_t)((BM * BK * 2) >> 4);
+      const uint64_t b_chunk = (uint64_t)((half_n * BK * 2) >> 4);
+      const uint64_t grp_step = (uint64_t)((a.kc * half_n * BK * 2) >> 4);
+      constexpr uint64_t kstep = (UMMA_K * 2) >> 4;
+      int s = 0;
+      uint32_t ph = 0;
+      uint64_t soff = 0;
+      bool ok = true;
+      for (int tile = tile_first, ti = 0; ok && tile < n_tiles; tile += tile_step, ++ti) {
+        const int ab = a.acc_bufs == 2 ? (ti & 1) : 0;
+        const int use = a.acc_bufs == 2 ? (ti >> 1) : ti;
+        if (use > 0) {
+          if (!mbar_wait(smem_u32(&acc_empty[ab]), (uint32_t)(use - 1) & 1u, a.status)) break;
+          fence_after();
+        }
+        const uint32_t tacc = tmem_base + (uint32_t)(ab * acc_cols);
+        int chunk = 0;
+        for (int it = 0; it < n_stages_work; ++it) {
+          if (!mbar_wait(smem_u32(&full[s]), ph, a.status)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const int nch = min(a.kc, a.k_blocks - chunk);
+          for (int j = 0; j < nch; ++j) {
+            const uint64_t ad = a0 + soff + j * a_chunk, bd = b0 + soff + j * b_chunk;
+#pragma unroll
+            for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+              const uint32_t acc = (it > 0 || j > 0 || kk > 0) ? 1u : 0u;
+#pragma unroll
+              for (int g = 0; g < NG; ++g)
+                umma_bf16_pair(tacc + g * a.n_g, ad + kk * kstep, bd + g * grp_step + kk * kstep, idesc, acc);
+            }
+          }
+          chunk += a.kc;
+          umma_commit_pair(smem_u32(&empty[s]));
+          umma_commit_pair(peer_empty + 8u * s);
+          if (++s == a.stages) {
+            s = 0;
+            ph ^= 1u;
+            soff = 0;
+          } else {
+            soff += stage_step;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&acc_full[ab]));
+        umma_commit_pair(peer_acc_full + 8u * ab);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int egrp = (warp - 2) / 4;
+    const int quad = warp & 3;
+    const int f_local = quad * 32 + lane;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);
+    const int etid = (threadIdx.x - 64) & 127;
+    const int first_c0 = egrp * kRows;
+    constexpr int kStgBufE = kRows * E::W * E::ES;
+    constexpr int kChunkStride = kEpiGroups * kRows;
+    int it = 0;
+    for (int tile = tile_first, ti = 0; tile < n_tiles; tile += tile_step, ++ti) {
+      const int tok0 = tile_tok0(tile);
+      const int fbase = tile_feat0(tile);
+      const int feat = fbase + f_local;
+      const int col0 = MODE == KVE_EPI_SILU_MUL ? fbase / 2 : fbase;
+      const float bias_f = ((MODE == KVE_EPI_BIAS || MODE == kEpiQkvRope) && feat < a.n) ? a.e.bias[feat] : 0.f;
+      uint4 res_first[E::NPASS];
+      if (first_c0 < a.mt) E::load_res(a, tok0 + first_c0, min(kRows, a.mt - first_c0), col0, etid, res_first);
+      const int ab = a.acc_bufs == 2 ? (ti & 1) : 0;
+      const int use = a.acc_bufs == 2 ? (ti >> 1) : ti;
+      const bool have = mbar_wait(smem_u32(&acc_full[ab]), (uint32_t)use & 1u, a.status);
+      fence_after();
+      const uint32_t t_acc = t_lane + (uint32_t)(ab * acc_cols);
+      bool first = true;
+      for (int c0 = first_c0; c0 < a.mt; c0 += kChunkStride, ++it) {
+        const int n = min(kRows, a.mt - c0);
+        uint8_t* buf = stg + (egrp * 2 + (it & 1)) * kStgBufE;
+        uint4 res[E::NPASS];
+        if (first) {
+#pragma unroll
+          for (int i = 0; i < E::NPASS; ++i) res[i] = res_first[i];
+          first = false;
+        } else {
+          E::load_res(a, tok0 + c0, n, col0, etid, res);
+        }
+        float v[32];
+        tmem_load_cols(t_acc + c0, n, have, v);
+        E::template stage<32>(buf, 0, n, f_local, v, bias_f);
+        epi_bar(egrp);
+        E::copy_out(a, buf, tok0 + c0, n, col0, etid, res);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(lead_acc_empty + 8u * ab);
+      if (!have) break;
+    }
+  }
+  // Both CTAs are done with every MMA, copy and barrier of the pair before TMEM
+  // is released and either CTA exits.
+  fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols)
+                 : "memory");
+  }
+}
+
 // ------------------------------------------------------------------ host
 int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int box_rows) {
   EncodeTiledFn fn = encode_fn();
@@ -988,6 +1291,7 @@ struct Plan {
   uint32_t stage_bytes, w_bytes;
   int grid_x;         // CTAs without split-K (fewer than the tiles when persistent)
   int acc_bufs, stg_bytes;
+  bool pair;          // CTA pairs with the 2-CTA MMA (gemm_tc_pair_kernel)
 };
 
 typedef void (*GemmKernel)(CUtensorMap, CUtensorMap, TcArgs);
@@ -1012,6 +1316,23 @@ GemmKernel kernel_for_shape(int mode, bool bf) {
   }
 }
 
+template <int MODE, bool BF>
+GemmKernel pair_kernel_of(int ng) {
+  return ng == 2 ? gemm_tc_pair_kernel<MODE, BF, 2> : gemm_tc_pair_kernel<MODE, BF, 1>;
+}
+GemmKernel pair_kernel_for(int mode, int out_dtype, int ng) {
+  const bool bf = out_dtype == KVE_BF16;
+  switch (mode) {
+    case KVE_EPI_BIAS: return bf ? pair_kernel_of<KVE_EPI_BIAS, true>(ng) : pair_kernel_of<KVE_EPI_BIAS, false>(ng);
+    case KVE_EPI_RESIDUAL:
+      return bf ? pair_kernel_of<KVE_EPI_RESIDUAL, true>(ng) : pair_kernel_of<KVE_EPI_RESIDUAL, false>(ng);
+    case KVE_EPI_SILU_MUL:
+      return bf ? pair_kernel_of<KVE_EPI_SILU_MUL, true>(ng) : pair_kernel_of<KVE_EPI_SILU_MUL, false>(ng);
+    case kEpiQkvRope: return bf ? pair_kernel_of<kEpiQkvRope, true>(ng) : nullptr;
+    default: return bf ? pair_kernel_of<KVE_EPI_STORE, true>(ng) : pair_kernel_of<KVE_EPI_STORE, false>(ng);
+  }
+}
+
 // Token groups x weight halves: (1, 1), (2, 1) for tiles above 256 tokens, (1, 2);
 // one tile per CTA or persistent.
 GemmKernel kernel_for(int mode, int out_dtype, int ng, int mh, bool persist) {
@@ -1033,6 +1354,10 @@ void configure_kernel() {
           for (bool persist : {false, true}) {
             GemmKernel kern = kernel_for(mode, dt, shape == 1 ? 2 : 1, shape == 2 ? 2 : 1, persist);
             if (kern) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
+            if (shape < 2 && persist) {
+              GemmKernel pk = pair_kernel_for(mode, dt, shape == 1 ? 2 : 1);
+              if (pk) cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
+            }
           }
   });
 }
@@ -1086,8 +1411,12 @@ size_t persist_staging(int row_bytes) { return (size_t)kEpiGroups * 2 * kRows * 
 // load round trip (measured: a persistent walk over 9 tiles saved about 2.3 us per
 // tile against nine waves of one-tile CTAs with the same stages).
 constexpr double kStartUs = 2.0;
-double stage_us(int mh, int ng, int mt, int kc, size_t avail) {
-  const size_t bytes = (size_t)(mh * BM + mt) * BK * 2 * kc;
+// x_rows: activation rows a CTA stages per k-chunk (all mt tokens, or half of
+// them in a CTA pair); the MMA term is this SM's share (mh x 128 rows x mt).
+double stage_us(int mh, int ng, int mt, int kc, size_t avail, int x_rows);
+double stage_us(int mh, int ng, int mt, int kc, size_t avail) { return stage_us(mh, ng, mt, kc, avail, mt); }
+double stage_us(int mh, int ng, int mt, int kc, size_t avail, int x_rows) {
+  const size_t bytes = (size_t)(mh * BM + x_rows) * BK * 2 * kc;
   int stages = (int)(avail / bytes);
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return 1e9;
@@ -1106,8 +1435,27 @@ inline int round16(int x) { return (x + 15) / 16 * 16; }
 struct TileConfig {
   int token_tiles, ng, n_g, mh, kc;
   bool persist;  // CTAs walk several tiles (no split-K, more tiles than resident CTAs)
+  bool pair;     // CTA pairs (2-CTA MMA) on 256-row tiles; always tile-walking
   double us;
 };
+
+// Pair forcing through kve_gemm_force_pair: 0 = the model's choice, 1 = never, 2 = where valid.
+std::atomic<int> g_force_pair{0};
+
+// Launch of CTA pairs: pair tiles of 256 weight rows x mt tokens walked by the
+// resident pairs; per SM a stage holds 128 weight rows and mt / 2 token rows.
+constexpr double kPairStartUs = 0.5;  // cluster barrier after set-up
+double pair_us(int feat_tiles, int k_blocks, const TileConfig& c, int row_bytes) {
+  const int* cap = cluster_capacity();
+  const long long tiles = (long long)((feat_tiles + 1) / 2) * c.token_tiles;
+  const long long pairs = cap[2] / 2 > 0 ? cap[2] / 2 : 1;
+  const long long rounds = (tiles + pairs - 1) / pairs;
+  const int mt = c.ng * c.n_g;
+  const int iters = (k_blocks + c.kc - 1) / c.kc;
+  const double main = iters * stage_us(1, c.ng, mt, c.kc, kAvail - persist_staging(row_bytes), mt / 2);
+  const double epi = epilogue_us((mt + kEpiGroups - 1) / kEpiGroups);
+  return kStartUs + kPairStartUs + (2 * mt <= 512 ? rounds * fmax(main, epi) + epi : rounds * (main + epi));
+}
 
 // A persistent launch: each CTA walks ceil(tiles / CTAs) tiles with its stage ring
 // running on across tiles; the epilogue overlaps the next tile's main loop when
@@ -1161,6 +1509,12 @@ int chunks_for(int mh, int mt, int s, bool tma3d, size_t avail) {
   return 1;
 }
 
+// A pair tile needs an even number of tokens per group on each CTA's 8-row
+// swizzle atoms: n_g a multiple of 16 (always) and at least 16.
+bool pair_ok(const TileConfig& c, int s, int feat_tiles) {
+  return s == 1 && c.mh == 1 && feat_tiles >= 2 && c.n_g >= 16 && c.n_g % 16 == 0;
+}
+
 TileConfig best_config(int m, int feat_tiles, int k_blocks, int s, bool tma3d, int row_bytes, bool legacy) {
   int t_min = (m + 383) / 384;
   if (t_min < 1) t_min = 1;
@@ -1185,6 +1539,15 @@ TileConfig best_config(int m, int feat_tiles, int k_blocks, int s, bool tma3d, i
         c.kc = chunks_for(mh, mt, s, tma3d, kAvail - persist_staging(row_bytes));
         c.us = config_us(feat_tiles, k_blocks, s, c, row_bytes, false);
         if (c.us < best_p.us * 0.97) best_p = c;
+      }
+      c.persist = false;
+      const int fp = g_force_pair.load();
+      if (!legacy && fp != 1 && pair_ok(c, s, feat_tiles)) {
+        TileConfig q = c;
+        q.pair = true;
+        q.kc = chunks_for(1, mt / 2, s, tma3d, kAvail - persist_staging(row_bytes));
+        q.us = pair_us(feat_tiles, k_blocks, q, row_bytes) * (fp == 2 ? 0.0 : 1.0);
+        if (q.us < best_p.us * 0.97) best_p = q;
       }
     }
   }
@@ -1239,14 +1602,20 @@ Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
   if (fmh == 2 && p.splits == 1 && c.ng == 1 && c.n_g <= 256 && p.feat_tiles >= 2) c.mh = 2;
   if (fkc > 0 && (fkc == 1 || (p.splits == 1 && p.tma3d))) c.kc = fkc;
   // ... and is shrunk until two pipeline stages fit in shared memory.
-  // A forced shape with no more tiles than resident CTAs runs one tile per CTA.
-  auto tiles_of = [&](const TileConfig& t) { return (long long)((p.feat_tiles + t.mh - 1) / t.mh) * t.token_tiles; };
+  // A forced shape with no more tiles than resident CTAs runs one tile per CTA;
+  // a pair launch stays a pair launch where its tiling allows.
+  if (c.pair && !pair_ok(c, p.splits, p.feat_tiles)) c.pair = false;
+  auto tiles_of = [&](const TileConfig& t) {
+    return t.pair ? (long long)((p.feat_tiles + 1) / 2) * t.token_tiles
+                  : (long long)((p.feat_tiles + t.mh - 1) / t.mh) * t.token_tiles;
+  };
   auto persist_of = [&](const TileConfig& t) {
-    return t.persist && p.splits == 1 && tiles_of(t) > cluster_capacity()[1];
+    return t.pair || (t.persist && p.splits == 1 && tiles_of(t) > cluster_capacity()[1]);
   };
   auto avail_of = [&](const TileConfig& t) { return kAvail - (persist_of(t) ? persist_staging(row_bytes) : 0); };
   auto fits = [&](const TileConfig& t) {
-    return (size_t)(t.mh * BM + t.ng * t.n_g) * BK * 2 * t.kc * 2 <= avail_of(t);
+    const int x_rows = t.pair ? t.ng * t.n_g / 2 : t.ng * t.n_g;
+    return (size_t)(t.mh * BM + x_rows) * BK * 2 * t.kc * 2 <= avail_of(t);
   };
   while (!fits(c) && c.kc > 1) c.kc /= 2;
   if (!fits(c)) {
@@ -1259,14 +1628,19 @@ Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
   p.mh = c.mh;
   p.kc = c.kc;
   p.mt = p.ng * p.n_g;
+  p.pair = c.pair;
   p.w_bytes = (uint32_t)(p.mh * BM * BK * 2 * p.kc);
-  p.stage_bytes = (uint32_t)(p.w_bytes + p.mt * BK * 2 * p.kc);
+  p.stage_bytes = (uint32_t)(p.w_bytes + (p.pair ? p.mt / 2 : p.mt) * BK * 2 * p.kc);
   const long long tiles = tiles_of(c);
   const bool persist = persist_of(c);
   size_t avail = avail_of(c);
   p.stg_bytes = persist ? (int)persist_staging(row_bytes) : 0;
   p.acc_bufs = persist && 2 * p.mh * p.mt <= 512 ? 2 : 1;
-  if (persist) {
+  if (p.pair) {
+    const long long pairs = cluster_capacity()[2] / 2 > 0 ? cluster_capacity()[2] / 2 : 1;
+    const long long rounds = (tiles + pairs - 1) / pairs;
+    p.grid_x = (int)(2 * ((tiles + rounds - 1) / rounds));  // CTAs: two per pair
+  } else if (persist) {
     const long long cap = cluster_capacity()[1];
     const long long rounds = (tiles + cap - 1) / cap;
     p.grid_x = (int)((tiles + rounds - 1) / rounds);  // balanced: every CTA walks rounds or rounds - 1 tiles
@@ -1344,28 +1718,29 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   a.rch = p.rch; a.stg_off = p.stg_off;
   a.w_static = e.w_static;
   a.kc = p.kc; a.tma3d = p.tma3d; a.w_bytes = p.w_bytes;
-  a.token_tiles = p.token_tiles; a.feat_ctas = (p.feat_tiles + p.mh - 1) / p.mh;
+  a.token_tiles = p.token_tiles; a.feat_ctas = p.pair ? (p.feat_tiles + 1) / 2 : (p.feat_tiles + p.mh - 1) / p.mh;
   a.acc_bufs = p.acc_bufs; a.stg_bytes = p.stg_bytes;
   const int es = e.out_dtype == KVE_BF16 ? 2 : 4;
   a.out_vec_ok = ((uintptr_t)e.out % 16 == 0) && ((size_t)e.ld_out * es % 16 == 0) &&
                  (e.mode != KVE_EPI_RESIDUAL || (uintptr_t)e.residual % 16 == 0);
   const bool persist = p.stg_bytes > 0;
-  GemmKernel kern = kernel_for(e.mode, e.out_dtype, p.ng, p.mh, persist);
+  GemmKernel kern = p.pair ? pair_kernel_for(e.mode, e.out_dtype, p.ng) : kernel_for(e.mode, e.out_dtype, p.ng, p.mh, persist);
   if (!kern) return set_error(KVE_ERR_DTYPE, "kve_gemm(tcgen05): epilogue %d needs bf16 output", e.mode);
   CUtensorMap mw, mx;
   int rc = p.tma3d ? make_map3(&mw, w, n, k, BM * p.mh, p.kc) : make_map(&mw, w, n, k, BM * p.mh);
   if (rc) return rc;
-  rc = p.tma3d ? make_map3(&mx, x, m, k, p.n_g, p.kc) : make_map(&mx, x, m, k, p.n_g);
+  const int x_box = p.pair ? p.n_g / 2 : p.n_g;  // a pair CTA stages half of each token group
+  rc = p.tma3d ? make_map3(&mx, x, m, k, x_box, p.kc) : make_map(&mx, x, m, k, x_box);
   if (rc) return rc;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.x = p.pair ? 2 : 1;  // a CTA pair, or the split-K CTAs of one tile
   attr.val.clusterDim.y = 1;
   attr.val.clusterDim.z = p.splits;
   const dim3 grid = persist ? dim3(p.grid_x, 1, 1) : dim3(p.token_tiles, a.feat_ctas, p.splits);
   cudaError_t err = launch_kernel_ex(kern, grid, dim3(kThreads),
                                      (size_t)p.stages * p.stage_bytes + p.stg_bytes + 1024 + 512, stream, &attr,
-                                     p.splits > 1 ? 1 : 0, mw, mx, a);
+                                     (p.splits > 1 || p.pair) ? 1 : 0, mw, mx, a);
   if (err != cudaSuccess) {
     cudaGetLastError();
     count_launch();
@@ -1404,13 +1779,22 @@ extern "C" int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_ch
   return KVE_OK;
 }
 
+extern "C" int kve_gemm_force_pair(int mode) {
+  using namespace kve;
+  if (mode < 0 || mode > 2) return set_error(KVE_ERR_ARG, "kve_gemm_force_pair: mode 0 (model), 1 (never) or 2 (where valid)");
+  std::lock_guard<std::mutex> g(g_plan_mu);
+  g_force_pair.store(mode);
+  g_plan_cache.clear();
+  return KVE_OK;
+}
+
 extern "C" int kve_gemm_plan_info(int m, int n, int k, int* out) {
   using namespace kve;
   if (m < 1 || n < 1 || k < 1 || !out) return set_error(KVE_ERR_ARG, "kve_gemm_plan_info: bad arguments");
   const Plan p = make_plan(m, n, k, BM * 2);
-  const int v[11] = {p.splits, p.token_tiles, p.ng, p.n_g, p.mh, p.kc, p.stages, p.tma3d,
-                     (p.feat_tiles + p.mh - 1) / p.mh, p.splits > 1 ? p.token_tiles * ((p.feat_tiles + p.mh - 1) / p.mh) * p.splits : p.grid_x,
-                     p.acc_bufs};
-  for (int i = 0; i < 11; ++i) out[i] = v[i];
+  const int feat_ctas = p.pair ? (p.feat_tiles + 1) / 2 : (p.feat_tiles + p.mh - 1) / p.mh;
+  const int v[12] = {p.splits, p.token_tiles, p.ng, p.n_g, p.mh, p.kc, p.stages, p.tma3d, feat_ctas,
+                     p.splits > 1 ? p.token_tiles * feat_ctas * p.splits : p.grid_x, p.acc_bufs, p.pair ? 1 : 0};
+  for (int i = 0; i < 12; ++i) out[i] = v[i];
   return KVE_OK;
 }

@@ -405,9 +405,10 @@ def test_gemm_rows_are_batch_invariant(cuda_device, algo, dt):
 
 @pytest.mark.gpu
 def test_gemm_launch_shapes_give_identical_bits(cuda_device):
-    """Token tiles, weight halves per CTA and k-chunks per pipeline stage change
-    speed only: every forced shape reproduces the model-chosen result exactly
-    (the last three cases run persistent CTAs, with one or two TMEM accumulators)."""
+    """Token tiles, weight halves per CTA, k-chunks per pipeline stage and CTA
+    pairs (2-CTA MMA) change speed only: every forced shape reproduces the
+    model-chosen result exactly (the last three cases run persistent CTAs, with
+    one or two TMEM accumulators)."""
     lib = L.load()
     g = torch.Generator(device=cuda_device).manual_seed(11)
     cases = [(320, 2560, 2048, L.EPI_BIAS), (64, 9728, 896, L.EPI_SILU_MUL), (320, 4096, 2048, L.EPI_SILU_MUL),
@@ -428,13 +429,18 @@ def test_gemm_launch_shapes_give_identical_bits(cuda_device):
                 return ops.gemm(x, w, epilogue=epi, bias=bias, residual=out, out=out)
 
             L.check(lib.kve_gemm_force_shape(0, 0, 0))
+            L.check(lib.kve_gemm_force_pair(0))
             ref = run()
-            for t, mh, kc in shapes:
-                L.check(lib.kve_gemm_force_shape(t, mh, kc))
-                got = run()
-                assert torch.equal(got, ref), (m, n, k, epi, t, mh, kc)
+            for pair in (1, 2):  # one-CTA tiles only / CTA pairs wherever valid
+                L.check(lib.kve_gemm_force_pair(pair))
+                for t, mh, kc in [(0, 0, 0)] + shapes:
+                    L.check(lib.kve_gemm_force_shape(t, mh, kc))
+                    got = run()
+                    assert torch.equal(got, ref), (m, n, k, epi, pair, t, mh, kc)
+                L.check(lib.kve_gemm_force_shape(0, 0, 0))
     finally:
         L.check(lib.kve_gemm_force_shape(0, 0, 0))
+        L.check(lib.kve_gemm_force_pair(0))
 
 
 def test_gemm_repeatable_and_no_workspace(cuda_device):
