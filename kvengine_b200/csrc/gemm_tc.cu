@@ -1587,6 +1587,11 @@ Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
   p.tma3d = k % BK == 0;
   p.splits = choose_splits(p.feat_tiles, p.k_blocks, p.tma3d);
   TileConfig c = best_config(m, p.feat_tiles, p.k_blocks, p.splits, p.tma3d, row_bytes, false);
+  // Split-K stages carry several k-chunks too (the split factor itself is chosen
+  // with one-chunk stages): fewer, larger TMA boxes measured 15 % faster for the
+  // split-K down projections. A stage's last box may run past the split's range;
+  // only its own chunks are multiplied.
+  if (p.splits > 1 && !c.pair && p.tma3d) c.kc = chunks_for(c.mh, c.ng * c.n_g, 1, true, kAvail);
   // A forced shape applies where it is valid for this GEMM; it never touches the
   // split factor, so results are the same bits either way.
   const int ft = g_force_t.load(), fmh = g_force_mh.load(), fkc = g_force_kc.load();
@@ -1595,12 +1600,13 @@ Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
     f.mh = c.mh;
     f.kc = c.kc;
     f.persist = c.persist;
+    f.pair = c.pair;
     if (f.ng == 2 || (long long)f.ng * f.n_g > 256) f.mh = 1;
     c = f;
   }
   if (fmh == 1) c.mh = 1;
   if (fmh == 2 && p.splits == 1 && c.ng == 1 && c.n_g <= 256 && p.feat_tiles >= 2) c.mh = 2;
-  if (fkc > 0 && (fkc == 1 || (p.splits == 1 && p.tma3d))) c.kc = fkc;
+  if (fkc > 0 && (fkc == 1 || p.tma3d)) c.kc = fkc;
   // ... and is shrunk until two pipeline stages fit in shared memory.
   // A forced shape with no more tiles than resident CTAs runs one tile per CTA;
   // a pair launch stays a pair launch where its tiling allows.
