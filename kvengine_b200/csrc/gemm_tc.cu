@@ -118,6 +118,8 @@ __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::be
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 // Named barrier of one epilogue warpgroup (ids 1 and up; 0 is __syncthreads).
 __device__ __forceinline__ void epi_bar(int group) { asm volatile("bar.sync %0, 128;" ::"r"(group + 1) : "memory"); }
+// Named barrier of both epilogue warpgroups.
+__device__ __forceinline__ void epi_bar_all() { asm volatile("bar.sync %0, %1;" ::"r"(kEpiGroups + 1), "r"(128 * kEpiGroups) : "memory"); }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -613,10 +615,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       // the cluster has finished its main loop (and, in later rounds, its reads).
       cluster_sync();
       const int my_lo = (int)((long long)rank * ch / S), my_hi = (int)((long long)(rank + 1) * ch / S);
-      if (epi && egrp == 0) {
-        // Owner u's tokens [lo_u, hi_u) are contiguous rows of pout.
+      if (epi) {
+        // Both warpgroups drain alternate 32-token chunks; owner u's tokens
+        // [lo_u, hi_u) are contiguous rows of pout.
         float* prow = pout + f_local;
-        for (int c = 0; c < ch; c += kRows) {
+        for (int c = egrp * kRows; c < ch; c += kEpiGroups * kRows) {
           const int n = min(kRows, ch - c);
           float v[32];
           tmem_load_cols(t_lane + r0 + c, n, have, v);
@@ -625,8 +628,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
             if (j < n) prow[(c + j) * BM] = v[j];
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        epi_bar(0);
-        if (etid == 0) {
+        epi_bar_all();
+        if (egrp == 0 && etid == 0) {
           const uint32_t mine = (uint32_t)(my_hi - my_lo);
           mbar_expect_tx(smem_u32(recv_bar), (uint32_t)(S - 1) * mine * BM * 4);
           for (int u = 0; u < S; ++u) {
@@ -640,16 +643,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
           asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
         mbar_wait(smem_u32(recv_bar), (uint32_t)(round & 1), a.status);
-        // Sum the S partials of each owned token in rank order (own slice from pout).
+        // Sum the S partials of each owned token in rank order (own slice from
+        // pout), 32-token chunks alternating between the warpgroups when both
+        // groups' double-buffered staging fits (16-bit outputs).
+        constexpr int kStgBufC = kRows * E::W * E::ES;
+        constexpr int kSumGroups = 2 * kEpiGroups * kStgBufC <= kStageBytes ? kEpiGroups : 1;
         const float* src[kMaxSplits];
 #pragma unroll
         for (int u = 0; u < kMaxSplits; ++u)
           src[u] = (u == (int)rank ? pout + (size_t)my_lo * BM : recv + (size_t)u * slm * BM) + f_local;
         const int mine = my_hi - my_lo;
         int it = 0;
-        for (int t0 = 0; t0 < mine; t0 += kRows, ++it) {
+        for (int t0 = egrp * kRows; egrp < kSumGroups && t0 < mine; t0 += kSumGroups * kRows, ++it) {
           const int n = min(kRows, mine - t0);
-          uint8_t* buf = stg + (it & 1) * kStgBuf;
+          uint8_t* buf = stg + (egrp * 2 + (it & 1)) * kStgBufC;
           uint4 res[E::NPASS];
           E::load_res(a, tok0 + r0 + my_lo + t0, n, col0, etid, res);
           for (int j0 = 0; j0 < n; j0 += 4) {
@@ -664,11 +671,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
             }
             E::template stage<4>(buf, j0, n, f_local, acc, bias_f);
           }
-          epi_bar(0);
+          epi_bar(egrp);
           E::copy_out(a, buf, tok0 + r0 + my_lo + t0, n, col0, etid, res);
         }
-        if (etid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-        epi_bar(0);
+        if (egrp == 0 && etid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        epi_bar_all();
       }
     }
   }
