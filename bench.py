@@ -602,7 +602,8 @@ def run_serve(args):
                        "target": "3B-arch seed 2", "max_batch_per_gpu": args.serve_batch,
                        "kv_blocks_per_pool": blocks, "block_size": BLOCK},
             "server": {"steps": srv.stats.steps, "admitted": srv.stats.admitted, "preempted": srv.stats.preempted,
-                       "peak_running": srv.stats.peak_running},
+                       "peak_running": srv.stats.peak_running,
+                       "prefix_tokens_reused": srv.stats.prefix_tokens_reused},
             "dtype": "bf16", "data": "synthetic (seeded random ids, random-init weights)"}), flush=True)
 
 

@@ -12,9 +12,18 @@ newly admitted (or resumed) request's prompt rides in the same ragged verify
 pass as the other requests' k+1 rows, and finished requests free their blocks
 before the next admission.
 
+Prefix sharing (the reference engine's `share_prefixes`, engine.py:204-207,
+312-318, 362-369, 413-419): an admitted request adopts the longest run of
+published full blocks matching its tokens in both the target and the draft pool
+(`PagedSequenceCache.adopt_prefix`), so its first ragged pass computes only the
+rest; after every step each running request publishes its newly full blocks of
+verified tokens (`register_prefix_blocks`). Rollback never reaches a published
+block: both caches are truncated only past len(tokens) - 1, and only blocks below
+that are published.
+
 Greedy output depends only on a request's own tokens, so every request's tokens
 equal `speculative_greedy` on that request alone, whatever the admission order,
-batch composition or preemptions.
+batch composition, preemptions or shared prefixes.
 """
 
 from __future__ import annotations
@@ -36,6 +45,7 @@ class ServeStats:
     finished: int = 0
     peak_running: int = 0
     new_tokens: int = 0
+    prefix_tokens_reused: int = 0  # prompt tokens whose target K/V came from shared blocks
 
 
 class SpecServer:
@@ -43,11 +53,12 @@ class SpecServer:
 
     max_batch caps the running set; watermark is the fraction of each pool kept
     free at admission (headroom for running requests' growth, as the reference's
-    engine does). `engine` may be given (tests inject a host-only fake)."""
+    engine does); share_prefixes adopts and publishes full blocks of common
+    prefixes. `engine` may be given (tests inject a host-only fake)."""
 
     def __init__(self, target=None, draft=None, target_pool=None, draft_pool=None, k: int = 4,
                  max_batch: int = 64, watermark: float = 0.02, eos_token_id=AUTO_EOS,
-                 engine: SpecEngine | None = None):
+                 engine: SpecEngine | None = None, share_prefixes: bool = True):
         if max_batch < 1:
             raise ValueError("max_batch must be at least 1")
         self.eng = engine or SpecEngine(target, draft, target_pool, draft_pool, k)
@@ -56,6 +67,7 @@ class SpecServer:
         self.eos = _resolve_eos(self.eng.target, eos_token_id)
         self.max_batch = max_batch
         self.watermark = watermark
+        self.share_prefixes = share_prefixes
         self.waiting: deque[_Request] = deque()
         self.running: list[_Request] = []
         self.results: dict[object, SpecDecodeResult] = {}
@@ -105,6 +117,10 @@ class SpecServer:
             rid = self._ids[id(r)]
             r.t_seq = self.t_pool.new_sequence(("t", rid))
             r.d_seq = self.d_pool.new_sequence(("d", rid))
+            if self.share_prefixes:
+                # The step's ragged pass then feeds only tokens[seq.length:].
+                self.stats.prefix_tokens_reused += r.t_seq.adopt_prefix(r.tokens)
+                r.d_seq.adopt_prefix(r.tokens)
             self.running.append(r)
             self.stats.admitted += 1
         self.stats.peak_running = max(self.stats.peak_running, len(self.running))
@@ -152,6 +168,10 @@ class SpecServer:
             if r.done:
                 self._finish(r)
             else:
+                if self.share_prefixes:
+                    # Both caches hold len(tokens) - 1 verified tokens: publish their full blocks.
+                    r.t_seq.register_prefix_blocks(r.tokens)
+                    r.d_seq.register_prefix_blocks(r.tokens)
                 still.append(r)
         self.running = still
 

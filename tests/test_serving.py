@@ -112,3 +112,35 @@ def test_zero_budget_finishes_on_arrival():
     srv = SpecServer(engine=FakeEngine(t_pool, d_pool, 4), eos_token_id=None)
     rid = srv.add_request([1, 2, 3], 0)
     assert srv.run()[rid].new_token_ids == []
+
+
+def test_shared_prefixes_are_adopted_and_outputs_unchanged():
+    """Requests repeating a common prompt prefix adopt its published blocks in both
+    pools (reference engine.py:312-318, 362-369): the first ragged pass feeds only
+    the rest, outputs equal the unshared run, and every block comes back."""
+    common = [7] * 13 + [9] * 6                      # 19 tokens: 4 full blocks of 4
+    reqs = [(common + [i + 1] * (2 + i % 3), 3 + i % 4) for i in range(8)]
+    outs = {}
+    for share in (False, True):
+        t_pool, d_pool = _pools(128)
+        eng = FakeEngine(t_pool, d_pool, 4)
+        fed = []
+        orig = eng.step
+
+        def step(rs, eos, orig=orig, fed=fed):
+            fed.append(sum(len(r.tokens) - r.t_seq.length for r in rs))
+            orig(rs, eos)
+        eng.step = step
+        srv = SpecServer(engine=eng, max_batch=2, eos_token_id=None, share_prefixes=share)
+        ids = [srv.add_request(p, n) for p, n in reqs]
+        res = srv.run()
+        outs[share] = ([res[i].new_token_ids for i in ids], sum(fed), srv.stats.prefix_tokens_reused)
+        for rid, (p, n) in zip(ids, reqs):
+            assert res[rid].new_token_ids == _expected(p, n)
+        assert t_pool.manager.num_free == 128 and d_pool.manager.num_free == 128
+        t_pool.manager.check_invariants()
+        d_pool.manager.check_invariants()
+    assert outs[True][0] == outs[False][0]
+    assert outs[False][2] == 0
+    # Requests admitted after the first step find the common prefix published.
+    assert outs[True][2] >= 6 * 16 and outs[True][1] == outs[False][1] - outs[True][2]
