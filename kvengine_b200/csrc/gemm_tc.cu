@@ -293,9 +293,11 @@ struct Epi {
             report(a.e.status, KVE_ERR_BOUNDS);
             pos = 0;
           }
+          // Read-only path: the tables are constant during the kernel, so these loads
+          // may be issued ahead of the previous rows' stores.
           const float4* cs = reinterpret_cast<const float4*>(a.e.rope_cos + (size_t)pos * half + dd);
           const float4* sn = reinterpret_cast<const float4*>(a.e.rope_sin + (size_t)pos * half + dd);
-          const float4 c0 = cs[0], c1 = cs[1], s0 = sn[0], s1 = sn[1];
+          const float4 c0 = __ldg(cs), c1 = __ldg(cs + 1), s0 = __ldg(sn), s1 = __ldg(sn + 1);
           const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
           const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
           const uint4 pv = *reinterpret_cast<const uint4*>(srow + cp);

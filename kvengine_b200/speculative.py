@@ -149,8 +149,6 @@ class SpecEngine:
             r.u_d = len(r.tokens) - r.d_seq.length
             r.u_t = len(r.tokens) - r.t_seq.length
             r.d_seq.reserve(r.u_d + k - 1)
-        for r in reqs:
-            r.t_seq.reserve(r.u_t + k)
         bs_d, bs_t = self.d_pool.block_size, self.t_pool.block_size
         # --- upload 1: the first draft pass's plan and ids, so the GPU starts while
         # the host builds the other plans (upload 2 queues behind that pass).
@@ -160,6 +158,10 @@ class SpecEngine:
         # --- draft: k passes, argmax feeding the next pass on the device
         self.dr.forward(plan0, d_ids_dev, self.dlog[:S], plan_dev=plan0_dev)
         ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S])
+        # The target reservations follow the draft ones with no allocator call in
+        # between, as in the reference's order, while the first draft pass runs.
+        for r in reqs:
+            r.t_seq.reserve(r.u_t + k)
         plans = [plan0]
         for j in range(1, k):
             plans.append(ForwardPlan([SeqSpec(r.d_seq.length + r.u_d + j - 1, 1, r.d_seq.blocks, 1)
