@@ -1,6 +1,6 @@
 """Benchmark: accepted tokens/s of greedy speculative decoding, 0.5B-arch draft -> 3B-arch target, k=4.
 
-Workload (BASELINE config 4 at k=4): draft Qwen2.5-0.5B architecture (seed 1),
+Workload (benchmark config 4 at k=4): draft Qwen2.5-0.5B architecture (seed 1),
 target Qwen2.5-3B architecture (seed 2), random-init bf16, 64 requests per
 GPU with 128 uniform-random prompt ids each, 64 new tokens per request, KV
 block size 16. One step = one full batched speculative decode of those
@@ -429,7 +429,7 @@ VERIFY_PASS_DRAM_BYTES = 7_286_600_000
 
 
 def run_micro(args):
-    """Per-kernel microbenchmarks (one JSON line each) on the BASELINE configs
+    """Per-kernel microbenchmarks (one JSON line each) on the benchmark configurations
     2 (attention), 3 (accept) and the verify GEMM shapes, timed with CUDA events."""
     from kvengine_b200 import ops, workloads
 

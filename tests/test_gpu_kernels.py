@@ -2,7 +2,7 @@
 
 Bit-exact for integer/copy work (accept, argmax, append, gather, embed, RoPE);
 fp32 kernels within 1e-5 relative of an fp64/fp32 reference; bf16 attention
-within the 2e-2 absolute tolerance BASELINE.json states for bf16 logits.
+within the 2e-2 absolute tolerance the task states for bf16 logits.
 """
 
 import hashlib
