@@ -183,12 +183,20 @@ int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_chunks);
  * bit-identical either way. */
 int kve_gemm_force_pair(int mode);
 
+/* Tuning and test hook (no kvengine counterpart): whether later tcgen05 GEMMs
+ * that run one tile per CTA may use 64-row MMA tiles: 0 = only where a CTA's
+ * 128-row weight slab would overflow its stage ring and a 64-row one fits
+ * (the default), 64 = wherever the shape allows, 128 = never. Results are
+ * bit-identical either way. */
+int kve_gemm_force_rows(int rows);
+
 /* The tcgen05 GEMM's launch plan for an [m, k] x [n, k]^T product with a bf16
- * output (no kvengine counterpart): out[0..11] = split-K factor, token tiles,
+ * output (no kvengine counterpart): out[0..12] = split-K factor, token tiles,
  * token groups per tile, tokens per group, weight halves, k-chunks per stage,
  * pipeline stages, 3-D tensor maps (0/1), tiles along the features (of 128 x
  * weight halves rows, or 256 rows for CTA pairs), CTAs launched (fewer than the
- * tiles when CTAs walk several tiles), TMEM accumulators per CTA, CTA pairs (0/1). */
+ * tiles when CTAs walk several tiles), TMEM accumulators per CTA, CTA pairs (0/1),
+ * weight rows per MMA tile (128 or 64). */
 int kve_gemm_plan_info(int m, int n, int k, int* out);
 
 /* ------------------------------------------------------------------------

@@ -28,6 +28,7 @@
 #include <cuda.h>
 #include <math.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <unordered_map>
@@ -84,8 +85,8 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t addr) {
 }
 
 // Instruction descriptor, kind::f16: D fp32, A/B bf16, both K-major, M=128, N=n.
-__device__ __forceinline__ uint32_t umma_idesc(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+__device__ __forceinline__ uint32_t umma_idesc(int n, int m = BM) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
@@ -160,11 +161,12 @@ __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, int n, bool have,
   }
 }
 
-template <int MODE, bool BF>
+// BMT: weight rows per tile (128, or 64 for the 64-row one-tile kernel).
+template <int MODE, bool BF, int BMT = BM>
 struct Epi {
   using T = typename std::conditional<BF, __nv_bfloat16, float>::type;
   static constexpr int ES = BF ? 2 : 4;
-  static constexpr int W = MODE == KVE_EPI_SILU_MUL ? BM / 2 : BM;  // output columns per tile
+  static constexpr int W = MODE == KVE_EPI_SILU_MUL ? BMT / 2 : BMT;  // output columns per tile
   static constexpr int VE = 16 / ES;                                 // elements per 16-byte vector
   static constexpr int VPR = W / VE;                                 // vectors per staged row
 
@@ -376,10 +378,17 @@ __device__ __forceinline__ uint32_t map_to(uint32_t local, uint32_t rank) {
 
 // Rows of weights per CTA: MH halves of 128 (one MMA M-tile each) sharing the
 // activation tile, so each activation byte a CTA loads serves 128 * MH features.
-template <int MODE, bool BF, int NG, int MH>
+//
+// BMT = 64 (one weight half, no split-K): 64-row MMA tiles (M = 64), for GEMMs
+// whose 128-row weight slab per CTA would overflow the stage ring while a 64-row
+// slab fits, so all of a CTA's weights can be requested before the dependency
+// wait. The accumulator's 64 rows sit in TMEM lanes 0-15 of each 32-lane
+// quarter: epilogue threads 0-15 of each warp own a row, 16-31 write nothing.
+template <int MODE, bool BF, int NG, int MH, int BMT = BM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, TcArgs a) {
-  using E = Epi<MODE, BF>;
+  static_assert(BMT == BM || (BMT == 64 && MH == 1), "64-row tiles carry one weight half");
+  using E = Epi<MODE, BF, BMT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Stage buffers need 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -395,7 +404,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * a.mt;
-  const int feat0 = blockIdx.y * BM * MH;
+  const int feat0 = blockIdx.y * BMT * MH;
   const int split = blockIdx.z;
   const int kb0 = (int)((long long)split * a.k_blocks / a.splits);
   const int kb1 = (int)((long long)(split + 1) * a.k_blocks / a.splits);
@@ -504,12 +513,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     // loop only adds precomputed descriptor deltas (the 14-bit start-address
     // field counts 16-byte units; stages, k-steps and N groups are offsets).
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc(a.n_g);
+      const uint32_t idesc = umma_idesc(a.n_g, BMT);
       const uint64_t a0 = umma_desc(smem_u32(smem));
       const uint64_t b0 = umma_desc(smem_u32(smem) + a.w_bytes);
       const uint64_t stage_step = (uint64_t)(a.stage_bytes >> 4);
-      constexpr uint64_t half_step = (uint64_t)((BM * BK * 2) >> 4);             // next 128 weight rows
-      const uint64_t a_chunk = (uint64_t)((MH * BM * BK * 2) >> 4);              // next k-chunk of weights
+      constexpr uint64_t half_step = (uint64_t)((BMT * BK * 2) >> 4);            // next 128 weight rows
+      const uint64_t a_chunk = (uint64_t)((MH * BMT * BK * 2) >> 4);             // next k-chunk of weights
       const uint64_t b_chunk = (uint64_t)((a.n_g * BK * 2) >> 4);                // next k-chunk of a group
       const uint64_t grp_step = (uint64_t)((a.kc * a.n_g * BK * 2) >> 4);        // next token group
       constexpr uint64_t kstep = (UMMA_K * 2) >> 4;  // 32 bytes along K
@@ -560,8 +569,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   const int egrp = epi ? (warp - 2) / 4 : 0;
   const int half = MH == 1 ? 0 : egrp;
   const int quad = warp & 3;
-  const int f_local = quad * 32 + lane;
-  const int fbase = feat0 + half * BM;  // first feature of this warpgroup's rows
+  const int f_local = BMT == BM ? quad * 32 + lane : quad * 16 + (lane & 15);
+  const bool live = BMT == BM || lane < 16;  // this thread's TMEM lane holds a row of the tile
+  const int fbase = feat0 + half * BMT;  // first feature of this warpgroup's rows
   const int feat = fbase + f_local;
   const int col0 = MODE == KVE_EPI_SILU_MUL ? fbase / 2 : fbase;
   const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(half * a.mt);
@@ -596,12 +606,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
         }
         float v[32];
         tmem_load_cols(t_lane + c0, n, have, v);
-        E::template stage<32>(buf, 0, n, f_local, v, bias_f);
+        E::template stage<32>(buf, 0, live ? n : 0, f_local, v, bias_f);
         epi_bar(egrp);
         E::copy_out(a, buf, tok0 + c0, n, col0, etid, res);
       }
     }
-  } else {
+  } else if constexpr (BMT == BM) {
     // Split-K over the cluster: each CTA writes its fp32 partial, grouped by the
     // CTA that owns each token (contiguous slices of the round), and sends every
     // peer its group with one bulk shared-memory copy; the owner then sums the
@@ -1301,6 +1311,7 @@ struct Plan {
   int grid_x;         // CTAs without split-K (fewer than the tiles when persistent)
   int acc_bufs, stg_bytes;
   bool pair;          // CTA pairs with the 2-CTA MMA (gemm_tc_pair_kernel)
+  int bmt;            // weight rows per MMA tile: 128, or 64 (rows64)
 };
 
 typedef void (*GemmKernel)(CUtensorMap, CUtensorMap, TcArgs);
@@ -1342,6 +1353,18 @@ GemmKernel pair_kernel_for(int mode, int out_dtype, int ng) {
   }
 }
 
+// 64-row one-tile kernels (bf16 output, one token group, one weight half).
+GemmKernel rows64_kernel_for(int mode, int out_dtype) {
+  if (out_dtype != KVE_BF16) return nullptr;
+  switch (mode) {
+    case KVE_EPI_BIAS: return gemm_tc_kernel<KVE_EPI_BIAS, true, 1, 1, 64>;
+    case KVE_EPI_RESIDUAL: return gemm_tc_kernel<KVE_EPI_RESIDUAL, true, 1, 1, 64>;
+    case KVE_EPI_SILU_MUL: return gemm_tc_kernel<KVE_EPI_SILU_MUL, true, 1, 1, 64>;
+    case kEpiQkvRope: return gemm_tc_kernel<kEpiQkvRope, true, 1, 1, 64>;
+    default: return gemm_tc_kernel<KVE_EPI_STORE, true, 1, 1, 64>;
+  }
+}
+
 // Token groups x weight halves: (1, 1), (2, 1) for tiles above 256 tokens, (1, 2);
 // one tile per CTA or persistent.
 GemmKernel kernel_for(int mode, int out_dtype, int ng, int mh, bool persist) {
@@ -1366,6 +1389,10 @@ void configure_kernel() {
             if (shape < 2 && persist) {
               GemmKernel pk = pair_kernel_for(mode, dt, shape == 1 ? 2 : 1);
               if (pk) cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
+            }
+            if (shape == 0 && !persist) {
+              GemmKernel rk = rows64_kernel_for(mode, dt);
+              if (rk) cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
             }
           }
   });
@@ -1637,6 +1664,7 @@ Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
     c.mh = 1;
     while (!fits(c) && c.kc > 1) c.kc /= 2;
   }
+  p.bmt = BM;
   p.token_tiles = c.token_tiles;
   p.ng = c.ng;
   p.n_g = c.n_g;
@@ -1710,6 +1738,44 @@ Plan make_plan(int m, int n, int k, int row_bytes) {
   return p;
 }
 
+// 64-row tiles through kve_gemm_force_rows: 0 = the rule below, 128 = never, 64 = where valid.
+std::atomic<int> g_force_rows{0};
+
+// A one-tile, single-group plan whose 128-row weight slab per CTA (plus its
+// tokens) overflows the stage ring, while a 64-row slab fits whole, in one wave
+// of CTAs: with 64-row tiles every weight byte of a CTA can be requested before
+// the dependency wait (the draft's K = 896 projections at decode batches).
+// Results are the same bits: each output is the same K-ordered MMA chain.
+void try_rows64(Plan& p, int m, int n, int k, int mode, int out_dtype, int hd) {
+  const int force = g_force_rows.load();
+  if (force == 128) return;
+  if (p.splits != 1 || p.pair || p.stg_bytes || p.mh != 1 || p.ng != 1 || !p.tma3d || out_dtype != KVE_BF16) return;
+  if (mode == kEpiQkvRope && (hd <= 0 || 64 % hd)) return;
+  const size_t x_row = (size_t)p.mt * BK * 2;  // token bytes per k-chunk
+  int kc = 0, stages = 0;
+  for (int c = 4; c >= 1; c /= 2) {
+    const size_t bytes = (64 * (size_t)BK * 2 + x_row) * c;
+    const int st = (int)std::min<size_t>(kMaxStages, kAvail / bytes);
+    if (st >= 2) {
+      kc = c;
+      stages = st;
+      break;
+    }
+  }
+  if (!kc) return;
+  const bool whole64 = (long long)stages * kc >= p.k_blocks;
+  const bool over128 = ((size_t)BM * BK * 2 + x_row) * (size_t)p.k_blocks > kAvail;
+  const long long ctas = (long long)((n + 63) / 64) * p.token_tiles;
+  if (force != 64 && !(whole64 && over128 && ctas <= cluster_capacity()[1])) return;
+  p.bmt = 64;
+  p.kc = kc;
+  p.stages = stages;
+  p.w_bytes = (uint32_t)(64 * BK * 2 * kc);
+  p.stage_bytes = (uint32_t)(p.w_bytes + x_row * kc);
+  p.grid_x = (int)ctas;
+  (void)m;
+}
+
 }  // namespace
 
 size_t gemm_tc_workspace_bytes(int, int, int) { return 0; }
@@ -1725,6 +1791,7 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   // Bytes of one staged output row: 128 outputs (64 for SwiGLU) of the output type.
   const int row_bytes = (e.mode == KVE_EPI_SILU_MUL ? BM / 2 : BM) * (e.out_dtype == KVE_BF16 ? 2 : 4);
   Plan p = make_plan(m, n, k, row_bytes);
+  try_rows64(p, m, n, k, e.mode, e.out_dtype, e.hd);
   if (p.stages < 2 || (p.splits > 1 && p.rch == 0))
     return set_error(KVE_ERR_SHAPE, "kve_gemm(tcgen05): tile does not fit shared memory");
   TcArgs a{};
@@ -1733,16 +1800,18 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   a.rch = p.rch; a.stg_off = p.stg_off;
   a.w_static = e.w_static;
   a.kc = p.kc; a.tma3d = p.tma3d; a.w_bytes = p.w_bytes;
-  a.token_tiles = p.token_tiles; a.feat_ctas = p.pair ? (p.feat_tiles + 1) / 2 : (p.feat_tiles + p.mh - 1) / p.mh;
+  a.token_tiles = p.token_tiles;
+  a.feat_ctas = p.bmt == 64 ? (n + 63) / 64 : p.pair ? (p.feat_tiles + 1) / 2 : (p.feat_tiles + p.mh - 1) / p.mh;
   a.acc_bufs = p.acc_bufs; a.stg_bytes = p.stg_bytes;
   const int es = e.out_dtype == KVE_BF16 ? 2 : 4;
   a.out_vec_ok = ((uintptr_t)e.out % 16 == 0) && ((size_t)e.ld_out * es % 16 == 0) &&
                  (e.mode != KVE_EPI_RESIDUAL || (uintptr_t)e.residual % 16 == 0);
   const bool persist = p.stg_bytes > 0;
-  GemmKernel kern = p.pair ? pair_kernel_for(e.mode, e.out_dtype, p.ng) : kernel_for(e.mode, e.out_dtype, p.ng, p.mh, persist);
+  GemmKernel kern = p.bmt == 64 ? rows64_kernel_for(e.mode, e.out_dtype)
+                  : p.pair ? pair_kernel_for(e.mode, e.out_dtype, p.ng) : kernel_for(e.mode, e.out_dtype, p.ng, p.mh, persist);
   if (!kern) return set_error(KVE_ERR_DTYPE, "kve_gemm(tcgen05): epilogue %d needs bf16 output", e.mode);
   CUtensorMap mw, mx;
-  int rc = p.tma3d ? make_map3(&mw, w, n, k, BM * p.mh, p.kc) : make_map(&mw, w, n, k, BM * p.mh);
+  int rc = p.tma3d ? make_map3(&mw, w, n, k, p.bmt * p.mh, p.kc) : make_map(&mw, w, n, k, p.bmt * p.mh);
   if (rc) return rc;
   const int x_box = p.pair ? p.n_g / 2 : p.n_g;  // a pair CTA stages half of each token group
   rc = p.tma3d ? make_map3(&mx, x, m, k, x_box, p.kc) : make_map(&mx, x, m, k, x_box);
@@ -1794,6 +1863,14 @@ extern "C" int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_ch
   return KVE_OK;
 }
 
+extern "C" int kve_gemm_force_rows(int rows) {
+  using namespace kve;
+  if (!(rows == 0 || rows == 64 || rows == 128))
+    return set_error(KVE_ERR_ARG, "kve_gemm_force_rows: rows 0 (rule), 64 (where valid) or 128 (never 64)");
+  g_force_rows.store(rows);
+  return KVE_OK;
+}
+
 extern "C" int kve_gemm_force_pair(int mode) {
   using namespace kve;
   if (mode < 0 || mode > 2) return set_error(KVE_ERR_ARG, "kve_gemm_force_pair: mode 0 (model), 1 (never) or 2 (where valid)");
@@ -1806,10 +1883,12 @@ extern "C" int kve_gemm_force_pair(int mode) {
 extern "C" int kve_gemm_plan_info(int m, int n, int k, int* out) {
   using namespace kve;
   if (m < 1 || n < 1 || k < 1 || !out) return set_error(KVE_ERR_ARG, "kve_gemm_plan_info: bad arguments");
-  const Plan p = make_plan(m, n, k, BM * 2);
-  const int feat_ctas = p.pair ? (p.feat_tiles + 1) / 2 : (p.feat_tiles + p.mh - 1) / p.mh;
-  const int v[12] = {p.splits, p.token_tiles, p.ng, p.n_g, p.mh, p.kc, p.stages, p.tma3d, feat_ctas,
-                     p.splits > 1 ? p.token_tiles * feat_ctas * p.splits : p.grid_x, p.acc_bufs, p.pair ? 1 : 0};
-  for (int i = 0; i < 12; ++i) out[i] = v[i];
+  Plan p = make_plan(m, n, k, BM * 2);
+  try_rows64(p, m, n, k, KVE_EPI_STORE, KVE_BF16, 0);
+  const int feat_ctas = p.bmt == 64 ? (n + 63) / 64 : p.pair ? (p.feat_tiles + 1) / 2 : (p.feat_tiles + p.mh - 1) / p.mh;
+  const int v[13] = {p.splits, p.token_tiles, p.ng, p.n_g, p.mh, p.kc, p.stages, p.tma3d, feat_ctas,
+                     p.splits > 1 ? p.token_tiles * feat_ctas * p.splits : p.grid_x, p.acc_bufs, p.pair ? 1 : 0,
+                     p.bmt};
+  for (int i = 0; i < 13; ++i) out[i] = v[i];
   return KVE_OK;
 }

@@ -405,16 +405,17 @@ def test_gemm_rows_are_batch_invariant(cuda_device, algo, dt):
 
 @pytest.mark.gpu
 def test_gemm_launch_shapes_give_identical_bits(cuda_device):
-    """Token tiles, weight halves per CTA, k-chunks per pipeline stage and CTA
-    pairs (2-CTA MMA) change speed only: every forced shape reproduces the
-    model-chosen result exactly (the last three cases run persistent CTAs, with
-    one or two TMEM accumulators)."""
+    """Token tiles, weight halves per CTA, k-chunks per pipeline stage, CTA
+    pairs (2-CTA MMA) and 64-row MMA tiles change speed only: every forced shape
+    reproduces the model-chosen result exactly (cases 8-10 run persistent CTAs,
+    with one or two TMEM accumulators; the last two are the draft's decode
+    projections, which pick 64-row tiles)."""
     lib = L.load()
     g = torch.Generator(device=cuda_device).manual_seed(11)
     cases = [(320, 2560, 2048, L.EPI_BIAS), (64, 9728, 896, L.EPI_SILU_MUL), (320, 4096, 2048, L.EPI_SILU_MUL),
              (300, 1000, 136, L.EPI_STORE), (64, 896, 4864, L.EPI_RESIDUAL), (17, 512, 256, L.EPI_STORE),
              (160, 1024, 512, L.EPI_RESIDUAL), (330, 40000, 128, L.EPI_STORE), (64, 19200, 256, L.EPI_RESIDUAL),
-             (300, 20000, 192, L.EPI_SILU_MUL)]
+             (300, 20000, 192, L.EPI_SILU_MUL), (64, 1152, 896, L.EPI_BIAS), (64, 896, 896, L.EPI_RESIDUAL)]
     shapes = [(1, 1, 1), (1, 2, 1), (2, 2, 2), (4, 1, 4), (3, 2, 4), (7, 1, 2), (2, 1, 2)]
     try:
         for m, n, k, epi in cases:
@@ -438,9 +439,19 @@ def test_gemm_launch_shapes_give_identical_bits(cuda_device):
                     got = run()
                     assert torch.equal(got, ref), (m, n, k, epi, pair, t, mh, kc)
                 L.check(lib.kve_gemm_force_shape(0, 0, 0))
+            L.check(lib.kve_gemm_force_pair(0))
+            for rows in (128, 64):  # 128-row MMA tiles only / 64-row tiles wherever valid
+                L.check(lib.kve_gemm_force_rows(rows))
+                for t, mh, kc in [(0, 0, 0), (1, 0, 0), (4, 0, 4), (2, 0, 2)]:
+                    L.check(lib.kve_gemm_force_shape(t, mh, kc))
+                    got = run()
+                    assert torch.equal(got, ref), (m, n, k, epi, rows, t, kc)
+                L.check(lib.kve_gemm_force_shape(0, 0, 0))
+            L.check(lib.kve_gemm_force_rows(0))
     finally:
         L.check(lib.kve_gemm_force_shape(0, 0, 0))
         L.check(lib.kve_gemm_force_pair(0))
+        L.check(lib.kve_gemm_force_rows(0))
 
 
 def test_gemm_repeatable_and_no_workspace(cuda_device):
