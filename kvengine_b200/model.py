@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import ctypes as C
 from dataclasses import dataclass, field
+from itertools import chain
 from types import SimpleNamespace
 
 import numpy as np
@@ -101,10 +102,11 @@ class ForwardPlan:
         seqs = self.seqs
         S = len(seqs)
         bs = self.block_size
-        q = np.fromiter((s.q_len for s in seqs), dtype=np.int64, count=S)
-        start = np.fromiter((s.start for s in seqs), dtype=np.int64, count=S)
-        n_out = np.fromiter((s.n_out for s in seqs), dtype=np.int64, count=S)
-        nblk = np.fromiter((len(s.blocks) for s in seqs), dtype=np.int64, count=S)
+        q = np.array([s.q_len for s in seqs], dtype=np.int64)
+        start = np.array([s.start for s in seqs], dtype=np.int64)
+        n_out = np.array([s.n_out for s in seqs], dtype=np.int64)
+        nb = [len(s.blocks) for s in seqs]
+        nblk = np.array(nb, dtype=np.int64)
         M = int(q.sum())
         self.n_tokens = M
         self.max_q_len = int(q.max()) if S else 0
@@ -112,22 +114,26 @@ class ForwardPlan:
         self.max_ctx = int(ctx.max()) if S else 0
         if S and bool((nblk * bs < ctx).any()):
             raise ValueError("block table does not cover the sequence (reserve first)")
-        width = self.width = max(1, int(nblk.max()) if S else 1)
+        width = self.width = max(1, max(nb) if S else 1)
         q_off = np.zeros(S + 1, dtype=np.int64)
         np.cumsum(q, out=q_off[1:])
-        seq_of_tok = np.repeat(np.arange(S), q)
-        pos = (np.arange(M) - q_off[:-1][seq_of_tok]) + start[seq_of_tok]
+        if M == S and bool((q == 1).all()):      # one row per sequence (decode passes)
+            seq_of_tok, pos = np.arange(S), start
+        else:
+            seq_of_tok = np.repeat(np.arange(S), q)
+            pos = (np.arange(M) - q_off[:-1][seq_of_tok]) + start[seq_of_tok]
         # [S, width] block table, zero-padded
         tables = np.zeros((S, width), dtype=np.int64)
         if S:
-            flat = np.fromiter((b for s in seqs for b in s.blocks), dtype=np.int64, count=int(nblk.sum()))
-            row = np.repeat(np.arange(S), nblk)
-            col = np.arange(flat.shape[0]) - np.repeat(np.cumsum(nblk) - nblk, nblk)
-            tables[row, col] = flat
+            tables[np.arange(width) < nblk[:, None]] = list(chain.from_iterable(s.blocks for s in seqs))
         slots = tables[seq_of_tok, pos // bs] * bs + pos % bs
         # logits rows: the last n_out rows of every sequence
         n_tot = int(n_out.sum())
-        out_rows = np.repeat(q_off[1:] - n_out, n_out) + (np.arange(n_tot) - np.repeat(np.cumsum(n_out) - n_out, n_out))
+        if n_tot == S and bool((n_out == 1).all()):
+            out_rows = q_off[1:] - 1
+        else:
+            out_rows = (np.repeat(q_off[1:] - n_out, n_out)
+                        + (np.arange(n_tot) - np.repeat(np.cumsum(n_out) - n_out, n_out)))
         self.n_out = n_tot
         parts = {"positions": pos, "slots": slots, "q_lens": q, "q_offsets": q_off, "ctx_lens": ctx,
                  "out_rows": out_rows, "tables": tables.reshape(-1)}

@@ -120,8 +120,7 @@ class PagedSequenceCache:
     # ------------------------------------------------------- allocation
     def reserve(self, n_tokens: int) -> None:
         """Grow the table to cover length + n_tokens (atomic: OutOfBlocks leaves it untouched)."""
-        need = self.pool.manager.blocks_needed(self._length + n_tokens)
-        extra = need - len(self.blocks)
+        extra = -(-(self._length + n_tokens) // self.pool.block_size) - len(self.blocks)
         if extra > 0:
             self.blocks.extend(self.pool.manager.allocate(extra, owner=self.request_id))
         self._pending_start = self._length  # slots are listed only if write() needs them
@@ -179,13 +178,27 @@ class PagedSequenceCache:
         """commit(n_tokens) followed by truncate(min(length, keep)) - the per-iteration
         bookkeeping of the spec loop in one call."""
         new_len = self._length + n_tokens
-        if new_len > self.capacity:
-            raise OutOfBlocks(self.pool.manager.blocks_needed(new_len) - len(self.blocks),
+        bs = self.pool.block_size
+        blocks = self.blocks
+        if new_len > len(blocks) * bs:
+            raise OutOfBlocks(self.pool.manager.blocks_needed(new_len) - len(blocks),
                               self.pool.manager.num_free)
-        self._length = new_len
         self._pending_start = None
         self._pending_n = 0
-        if keep < new_len:
+        if keep >= new_len:
+            self._length = new_len
+        elif 0 <= keep and self._registered <= keep // bs:
+            # the spec loop's rollback: no published block is touched, so this is
+            # truncate(keep) without its unregister walk
+            need = -(-keep // bs)
+            if need < len(blocks):
+                self.pool.manager.free(blocks[need:])
+                del blocks[need:]
+            if len(self._digest_chain) > keep // bs:
+                del self._digest_chain[keep // bs:]
+            self._length = keep
+        else:
+            self._length = new_len
             self.truncate(keep)
 
     def truncate(self, n_tokens: int) -> None:

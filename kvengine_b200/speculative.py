@@ -120,6 +120,8 @@ class SpecEngine:
         self.preds = torch.empty(S * (k + 1), dtype=torch.int32, device=dev)
         # emitted [S, k+1] then n_accepted [S]: read back by one copy
         self.accepted = torch.empty(S * (k + 2), dtype=torch.int32, device=dev)
+        self.accepted_host = torch.empty(S * (k + 2), dtype=torch.int32, pin_memory=True)
+        self.accepted_ready = torch.cuda.Event()
 
     def _upload(self, slot: int, arrays: list[np.ndarray]) -> list[torch.Tensor]:
         """Copy int32 host arrays to the device in one transfer through pinned
@@ -194,7 +196,12 @@ class SpecEngine:
         ne = S * (k + 1)
         out = (self.preds[:ne].view(S, k + 1), self.accepted[ne:ne + S], self.accepted[:ne].view(S, k + 1))
         ops.greedy_accept(tlog.view(S, k + 1, self.V), drafts.t(), self.accept_ws, out=out)
-        back = self.accepted[:ne + S].cpu().numpy()
+        # pinned readback, waited on by an event (no pageable staging, no device-wide sync)
+        back_t = self.accepted_host[:ne + S]
+        back_t.copy_(self.accepted[:ne + S], non_blocking=True)
+        self.accepted_ready.record()
+        self.accepted_ready.synchronize()
+        back = back_t.numpy()
         n_host = back[ne:].tolist()
         em_host = back[:ne].reshape(S, k + 1).tolist()
         self.stats["d2h_bytes"] += back.nbytes

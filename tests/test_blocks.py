@@ -153,3 +153,59 @@ def test_prefix_registry_and_shared_truncate_guard():
     a.free()
     assert pool.manager.num_reclaimable == 3
     pool.manager.check_invariants()
+
+
+def test_commit_and_keep_matches_commit_then_truncate():
+    """`commit_and_keep` (the spec loop's per-iteration commit + rollback, with a fast path
+    when no published block is rolled back) leaves the same table, free list, length and
+    prefix chain as `commit` followed by `truncate` (kvengine paged.py:344-380), including
+    rollbacks into published blocks."""
+    import random
+
+    import torch
+
+    from kvengine_b200.paged import PagedKVCache
+
+    rng = random.Random(7)
+    for bs in (1, 3, 4, 16):
+        pools = [PagedKVCache(1, 1, 8, 96, bs, torch.float32, "cpu") for _ in range(2)]
+        seqs = [[p.new_sequence(i) for i in range(4)] for p in pools]
+        toks = [[rng.randrange(50) for _ in range(400)] for _ in range(4)]
+        for _ in range(300):
+            i = rng.randrange(4)
+            fast, slow = seqs[0][i], seqs[1][i]
+            op = rng.random()
+            if op < 0.1:
+                fast.free()
+                slow.free()
+                continue
+            n = rng.randint(1, 6)
+            try:
+                fast.reserve(n)
+            except Exception as e:       # out of blocks: both must refuse
+                with pytest.raises(type(e)):
+                    slow.reserve(n)
+                continue
+            slow.reserve(n)
+            keep = rng.randint(max(0, fast.length - 2), fast.length + n)
+            errs = []
+            for s, f in ((fast, lambda s: s.commit_and_keep(n, keep)),
+                         (slow, lambda s: (s.commit(n), s.truncate(keep) if keep < s.length else None))):
+                try:
+                    f(s)
+                    errs.append(None)
+                except ValueError as e:
+                    errs.append(str(e))
+            assert errs[0] == errs[1]
+            if op < 0.5 and errs[0] is None:
+                for s in (fast, slow):
+                    s.register_prefix_blocks(toks[i][: s.length])
+            if errs[0] is not None:      # a refused rollback leaves the committed length
+                for s in (fast, slow):
+                    s.free()
+            for s in (fast, slow):
+                s.pool.manager.check_invariants()
+            assert (fast.blocks, fast.length, fast._digest_chain, fast._registered) == \
+                (slow.blocks, slow.length, slow._digest_chain, slow._registered)
+            assert pools[0].manager._free == pools[1].manager._free
+            assert list(pools[0].manager._reclaimable) == list(pools[1].manager._reclaimable)
