@@ -475,6 +475,32 @@ def run_micro(args):
         out.append({"micro": "paged_verify_attention (config 2)", "seqs": B, "q_len": w.q_len,
                     "mean_ctx": round(sum(w.ctx_lens) / B, 1), "ms": round(ms, 4), "alg_bytes": kvb + qob,
                     "gbs": round((kvb + qob) / ms / 1e6, 1), "frac_hbm": round((kvb + qob) / ms / 1e6 / pk["hbm_gbs"], 4)})
+    if "attention_decode" in which:
+        # Config 4's decode attention: the draft pass (0.5B: 14 query / 2 kv heads, hd 64,
+        # one row per sequence) and the verify pass (3B: 16 / 2 heads, hd 128, k + 1 = 5 rows),
+        # 64 sequences at context 190, block size 16; 8 disjoint block sets, cycled.
+        for name, nq, nkv, hd, qlen in (("draft", 14, 2, 64, 1), ("verify", 16, 2, 128, 5)):
+            B, ctx_len, bs = 64, 190, 16
+            nbs = -(-ctx_len // bs)
+            shape = (B * nbs * 8, bs, nkv, hd)
+            dk = torch.randn(shape, device=dev).to(torch.bfloat16)  # timing only: any finite contents
+            dv = torch.randn(shape, device=dev).to(torch.bfloat16)
+            tables = torch.arange(B * nbs, dtype=torch.int32, device=dev).view(B, nbs)
+            shifted = [(tables + r * B * nbs).to(torch.int32) for r in range(8)]
+            ctx = torch.full((B,), ctx_len, dtype=torch.int32, device=dev)
+            ql = torch.full((B,), qlen, dtype=torch.int32, device=dev)
+            qo = (torch.arange(B + 1, dtype=torch.int32) * qlen).to(dev)
+            q = torch.randn(B * qlen, nq, hd, device=dev).to(torch.bfloat16)
+            o = torch.empty_like(q)
+            ws = ops.Workspace(dev)
+            ms = _time_launches([(lambda tb=tb: ops.paged_attention(q, dk, dv, tb, ctx, ql, qo, qlen, ctx_len,
+                                                                    hd ** -0.5, out=o, workspace=ws))
+                                 for tb in shifted], args.steps)
+            kvb = B * ctx_len * nkv * hd * 2 * 2
+            out.append({"micro": f"paged_verify_attention decode (config 4 {name})", "seqs": B, "q_len": qlen,
+                        "ctx": ctx_len, "heads": [nq, nkv, hd], "ms": round(ms, 4), "alg_bytes": kvb + 2 * q.numel() * 2,
+                        "gbs": round((kvb + 2 * q.numel() * 2) / ms / 1e6, 1)})
+            del dk, dv
     if "gemm" in which:
         g = torch.Generator(device=dev).manual_seed(0)
         from kvengine_b200 import _lib as L
@@ -614,7 +640,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="kvengine_b200", choices=["kvengine_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--micro", default=None, help="comma list of accept,attention,gemm microbenchmarks")
+    ap.add_argument("--micro", default=None, help="comma list of accept,attention,attention_decode,gemm microbenchmarks")
     ap.add_argument("--gemm-case", default=None, help="restrict --micro gemm to these shapes (comma list)")
     ap.add_argument("--profile-iteration", action="store_true")
     ap.add_argument("--serve", type=int, default=0, help="config 5: continuous batching over this many requests")
