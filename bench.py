@@ -425,7 +425,7 @@ L2_BYTES = 126 * 2**20
 # DRAM bytes (read + write) of one steady verify pass of the config-4 workload, summed
 # over its kernels from an ncu launch list of `bench.py --profile-iteration` with
 # dram__bytes_read.sum and dram__bytes_write.sum (measured, not modelled).
-VERIFY_PASS_DRAM_BYTES = 7_286_600_000
+VERIFY_PASS_DRAM_BYTES = 7_270_500_000
 
 
 def run_micro(args):
@@ -512,7 +512,11 @@ def run_micro(args):
                  ("lm_head", 320, 151936, 2048, L.EPI_STORE),
                  ("draft_qkv", 64, 1152, 896, L.EPI_BIAS), ("draft_o_proj", 64, 896, 896, L.EPI_RESIDUAL),
                  ("draft_gate_up", 64, 9728, 896, L.EPI_SILU_MUL), ("draft_down", 64, 896, 4864, L.EPI_RESIDUAL),
-                 ("draft_lm_head", 64, 151936, 896, L.EPI_STORE))
+                 ("draft_lm_head", 64, 151936, 896, L.EPI_STORE),
+                 # the prompt pass fused into the first verify (64 requests x 132 rows)
+                 ("prefill_qkv", 8448, 2560, 2048, L.EPI_BIAS), ("prefill_o_proj", 8448, 2048, 2048, L.EPI_RESIDUAL),
+                 ("prefill_gate_up", 8448, 22016, 2048, L.EPI_SILU_MUL),
+                 ("prefill_down", 8448, 2048, 11008, L.EPI_RESIDUAL))
         for name, m, n, k, epi in cases:
             if args.gemm_case and name not in args.gemm_case.split(","):
                 continue
