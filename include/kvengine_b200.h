@@ -271,6 +271,15 @@ size_t kve_forward_attn_ws_bytes(const kve_model_t* model, int n_seqs, int max_q
 int kve_forward(const kve_model_t* model, const kve_batch_t* batch, const kve_scratch_t* scratch,
                 cudaStream_t stream);
 
+/* kve_forward recorded into a CUDA graph and launched as one graph (no kvengine
+ * counterpart; same results, fewer launch costs on the GPU). *graph_slot holds the
+ * caller's executable graph: NULL on the first call, then updated in place by later
+ * calls of the same launch sequence. The stream must not be the legacy default
+ * stream (it cannot be captured). Free the slot with kve_forward_graph_free. */
+int kve_forward_graphed(const kve_model_t* model, const kve_batch_t* batch, const kve_scratch_t* scratch,
+                        void** graph_slot, cudaStream_t stream);
+int kve_forward_graph_free(void* graph);
+
 #ifdef __cplusplus
 }
 #endif

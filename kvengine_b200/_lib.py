@@ -85,6 +85,9 @@ _SIGNATURES = {
     "kve_forward_gemm_ws_bytes": (sz, [C.POINTER(ModelT), i32, i32]),
     "kve_forward_attn_ws_bytes": (sz, [C.POINTER(ModelT), i32, i32, i32]),
     "kve_forward": (i32, [C.POINTER(ModelT), C.POINTER(BatchT), C.POINTER(ScratchT), vp]),
+    "kve_forward_graphed": (i32, [C.POINTER(ModelT), C.POINTER(BatchT), C.POINTER(ScratchT),
+                                  C.POINTER(C.c_void_p), vp]),
+    "kve_forward_graph_free": (i32, [vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

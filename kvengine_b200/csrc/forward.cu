@@ -96,3 +96,59 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
                    b->logits, b->logits_dtype, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
   return KVE_OK;
 }
+
+// kve_forward recorded into a CUDA graph and launched as one: the pass's ~170 kernel
+// launches (programmatic dependent launches become programmatic graph edges) reach
+// the GPU without the per-launch work of a stream launch. The executable graph lives
+// in the caller's slot and is updated in place on later calls (the same launch
+// sequence with new pointers and sizes), or rebuilt when the update is refused.
+extern "C" int kve_forward_graphed(const kve_model_t* m, const kve_batch_t* b, const kve_scratch_t* s,
+                                   void** graph_slot, cudaStream_t stream) {
+  if (!graph_slot) return set_error(KVE_ERR_ARG, "kve_forward_graphed: null graph slot");
+  if (!m || !b || !s) return set_error(KVE_ERR_ARG, "kve_forward_graphed: null argument");
+  if (b->n_tokens == 0) return KVE_OK;
+  cudaError_t e = cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(KVE_ERR_CUDA, "kve_forward_graphed: stream capture: %s", cudaGetErrorString(e));
+  }
+  const int rc = kve_forward(m, b, s, stream);
+  cudaGraph_t graph = nullptr;
+  e = cudaStreamEndCapture(stream, &graph);
+  if (rc != KVE_OK || e != cudaSuccess || !graph) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return rc != KVE_OK ? rc : set_error(KVE_ERR_CUDA, "kve_forward_graphed: end capture: %s", cudaGetErrorString(e));
+  }
+  cudaGraphExec_t exec = static_cast<cudaGraphExec_t>(*graph_slot);
+  if (exec) {
+    cudaGraphExecUpdateResultInfo info;
+    if (cudaGraphExecUpdate(exec, graph, &info) != cudaSuccess) {
+      cudaGetLastError();
+      cudaGraphExecDestroy(exec);
+      exec = nullptr;
+      *graph_slot = nullptr;
+    }
+  }
+  if (!exec) {
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    if (e != cudaSuccess) {
+      cudaGraphDestroy(graph);
+      cudaGetLastError();
+      return set_error(KVE_ERR_CUDA, "kve_forward_graphed: instantiate: %s", cudaGetErrorString(e));
+    }
+    *graph_slot = exec;
+  }
+  cudaGraphDestroy(graph);
+  e = cudaGraphLaunch(exec, stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(KVE_ERR_CUDA, "kve_forward_graphed: launch: %s", cudaGetErrorString(e));
+  }
+  return KVE_OK;
+}
+
+extern "C" int kve_forward_graph_free(void* graph) {
+  if (graph) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph));
+  return KVE_OK;
+}

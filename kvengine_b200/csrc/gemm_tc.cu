@@ -1275,14 +1275,22 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_cons
 int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(KVE_ERR_CUDA, "kve_gemm: cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(KVE_ERR_CUDA, "kve_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  CUresult r = CUDA_SUCCESS;
+  auto encode = [&](CUtensorMap* m) {
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+  };
+  // key: rows (24 bits) | k (20) | box rows (9)
+  const bool packable = rows >= 0 && rows < (1 << 24) && k >= 0 && k < (1 << 20) && box_rows >= 0 && box_rows < 512;
+  const bool ok = packable ? cached_map(map, ptr, (uint64_t)rows | (uint64_t)k << 24 | (uint64_t)box_rows << 44, encode)
+                           : encode(map);
+  if (!ok) return set_error(KVE_ERR_CUDA, "kve_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return KVE_OK;
 }
 
@@ -1293,14 +1301,26 @@ int make_map(CUtensorMap* map, const void* ptr, int rows, int k, int box_rows) {
 int make_map3(CUtensorMap* map, const void* ptr, int rows, int k, int box_rows, int kc) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(KVE_ERR_CUDA, "kve_gemm: cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[3] = {(cuuint64_t)BK, (cuuint64_t)rows, (cuuint64_t)(k / BK)};
-  cuuint64_t strides[2] = {(cuuint64_t)k * 2, (cuuint64_t)BK * 2};
-  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)kc};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(KVE_ERR_CUDA, "kve_gemm: cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  CUresult r = CUDA_SUCCESS;
+  auto encode = [&](CUtensorMap* m) {
+    cuuint64_t dims[3] = {(cuuint64_t)BK, (cuuint64_t)rows, (cuuint64_t)(k / BK)};
+    cuuint64_t strides[2] = {(cuuint64_t)k * 2, (cuuint64_t)BK * 2};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)kc};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+  };
+  // key: rows (24 bits) | k (20) | box rows (9) | k-chunks per box (3)
+  const bool packable = rows >= 0 && rows < (1 << 24) && k >= 0 && k < (1 << 20) && box_rows >= 0 &&
+                        box_rows < 512 && kc >= 0 && kc < 8;
+  const bool ok = packable ? cached_map(map, ptr,
+                                        (uint64_t)rows | (uint64_t)k << 24 | (uint64_t)box_rows << 44 |
+                                            (uint64_t)kc << 53,
+                                        encode)
+                           : encode(map);
+  if (!ok) return set_error(KVE_ERR_CUDA, "kve_gemm: cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
   return KVE_OK;
 }
 

@@ -4,7 +4,9 @@
 
 #include <cuda.h>
 
+#include <cstdint>
 #include <mutex>
+#include <unordered_map>
 
 #include "kve_common.cuh"
 
@@ -97,6 +99,38 @@ inline EncodeTiledFn encode_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
   });
   return fn;
+}
+
+// Encoded tensor maps by their parameters: the forward pass asks for the same few
+// (pointer, shape, box) maps on every layer and every pass, and an encoding costs
+// host time on the launch path. A map holds only the address, shape, strides and
+// box, so a hit is exactly the map the encoder would return. `shape` packs the
+// rest of the parameters of one call site (each call site has its own cache).
+struct MapCacheKey {
+  uint64_t ptr, shape;
+  bool operator==(const MapCacheKey& o) const { return ptr == o.ptr && shape == o.shape; }
+};
+struct MapCacheHash {
+  size_t operator()(const MapCacheKey& k) const { return std::hash<uint64_t>()(k.ptr * 0x9E3779B97F4A7C15ull ^ k.shape); }
+};
+template <typename Encode>
+inline bool cached_map(CUtensorMap* map, const void* ptr, uint64_t shape, Encode&& encode) {
+  static std::mutex mu;
+  static std::unordered_map<MapCacheKey, CUtensorMap, MapCacheHash> cache;
+  const MapCacheKey key{reinterpret_cast<uint64_t>(ptr), shape};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *map = it->second;
+      return true;
+    }
+  }
+  if (!encode(map)) return false;
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() > 16384) cache.clear();
+  cache.emplace(key, *map);
+  return true;
 }
 
 }  // namespace kve

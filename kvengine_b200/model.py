@@ -176,6 +176,15 @@ class Runner:
         self.attn_ws = torch.zeros(256, dtype=torch.uint8, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.plan_dev = torch.zeros(1024, dtype=torch.int32, device=self.device)
+        self._graphs: dict[str, C.c_void_p] = {}  # executable graphs of kve_forward_graphed, by slot name
+
+    def __del__(self):
+        graphs = getattr(self, "_graphs", None)
+        if graphs and L._lib is not None:
+            for h in graphs.values():
+                if h.value:
+                    L._lib.kve_forward_graph_free(h)
+            graphs.clear()
 
     def _refresh_rope(self, max_pos: int):
         w = self.model.weights
@@ -241,8 +250,10 @@ class Runner:
                         plan.width, plan.n_out if logits is not None else 0, p("out_rows"), logits_ptr, ldt)
 
     def forward(self, plan: ForwardPlan, ids: torch.Tensor, logits: torch.Tensor | None,
-                plan_dev: torch.Tensor | None = None) -> None:
-        """Launch one model pass. `ids`: int32 device [n_tokens]; logits: [n_out, V] or None."""
+                plan_dev: torch.Tensor | None = None, graph: str | None = None) -> None:
+        """Launch one model pass. `ids`: int32 device [n_tokens]; logits: [n_out, V] or None.
+        With `graph` (a slot name) the pass is recorded into that slot's CUDA graph and
+        launched as one graph (the current stream must not be the legacy default stream)."""
         if plan.n_tokens == 0:
             return
         self.ensure(plan.n_tokens, plan.n_out, len(plan.seqs), plan.max_q_len, plan.max_ctx)
@@ -250,8 +261,14 @@ class Runner:
             plan_dev = self.upload(plan)
         batch = self.batch_struct(plan, plan_dev, ids, logits)
         scratch = self.scratch()
-        L.check(L.load().kve_forward(C.byref(self._model_c), C.byref(batch), C.byref(scratch),
-                                     L.stream_handle(self.device)))
+        lib = L.load()
+        if graph is None:
+            L.check(lib.kve_forward(C.byref(self._model_c), C.byref(batch), C.byref(scratch),
+                                    L.stream_handle(self.device)))
+        else:
+            slot = self._graphs.setdefault(graph, C.c_void_p())
+            L.check(lib.kve_forward_graphed(C.byref(self._model_c), C.byref(batch), C.byref(scratch),
+                                            C.byref(slot), L.stream_handle(self.device)))
 
     def check_status(self) -> None:
         code = int(self.status.item())

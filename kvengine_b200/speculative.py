@@ -89,7 +89,7 @@ class _Request:
 class SpecEngine:
     """Batched draft/verify/accept loop over one target and one draft model."""
 
-    def __init__(self, target, draft, target_pool, draft_pool, k: int):
+    def __init__(self, target, draft, target_pool, draft_pool, k: int, graphs: bool = True):
         assert k >= 1, "k must be at least 1"
         self.target = as_model(target)
         self.draft = as_model(draft)
@@ -107,6 +107,13 @@ class SpecEngine:
         # When a list, every verify pass appends (start_event, end_event, plan) so a
         # caller can time the verify step on the stream it runs on.
         self.verify_events: list | None = None
+        # Steps run on the engine's own stream (ordered after, and followed by, the
+        # caller's current stream), so that the third and later draft passes and the
+        # verify pass can be launched as CUDA graphs (the first two draft passes of a step
+        # stay stream launches: the GPU waits on the first, and recording the second
+        # would delay it).
+        self.graphs = graphs
+        self.stream = torch.cuda.Stream(device=self.device)
 
     def _ensure(self, S: int):
         if S <= self._cap:
@@ -144,6 +151,13 @@ class SpecEngine:
 
     def step(self, reqs: list[_Request], eos: set[int]) -> None:
         """One draft/verify/accept iteration for every request in `reqs`."""
+        caller = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(caller)
+        with torch.cuda.stream(self.stream):
+            self._step(reqs, eos)
+        caller.wait_stream(self.stream)
+
+    def _step(self, reqs: list[_Request], eos: set[int]) -> None:
         k, S = self.k, len(reqs)
         self._ensure(S)
         # --- block reservation, in the reference's order: draft feeds, then the verify feed.
@@ -179,7 +193,10 @@ class SpecEngine:
                                                                 dst.reshape(-1).astype(np.int32)])
         v_ids_dev, dst_dev = views[-2], views[-1].long()
         for j in range(1, k):
-            self.dr.forward(plans[j], self.drafts[j - 1, :S], self.dlog[:S], plan_dev=views[j - 1])
+            # Pass 1 is a stream launch too: the host records a graph in about the time the
+            # GPU needs for pass 0, which is when it builds the remaining plans.
+            self.dr.forward(plans[j], self.drafts[j - 1, :S], self.dlog[:S], plan_dev=views[j - 1],
+                            graph="draft" if self.graphs and j >= 2 else None)
             ops.argmax_rows(self.dlog[:S], out=self.drafts[j, :S])
         # --- verify: one target pass over every request's u+k rows
         drafts = self.drafts[:, :S]
@@ -188,7 +205,7 @@ class SpecEngine:
         if self.verify_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
-        self.tr.forward(vplan, v_ids_dev, tlog, plan_dev=views[k - 1])
+        self.tr.forward(vplan, v_ids_dev, tlog, plan_dev=views[k - 1], graph="verify" if self.graphs else None)
         if self.verify_events is not None:
             ev1.record()
             self.verify_events.append((ev0, ev1, vplan))
