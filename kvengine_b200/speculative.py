@@ -108,10 +108,9 @@ class SpecEngine:
         # caller can time the verify step on the stream it runs on.
         self.verify_events: list | None = None
         # Steps run on the engine's own stream (ordered after, and followed by, the
-        # caller's current stream), so that the third and later draft passes and the
-        # verify pass can be launched as CUDA graphs (the first two draft passes of a step
-        # stay stream launches: the GPU waits on the first, and recording the second
-        # would delay it).
+        # caller's current stream), so that the draft passes after the first and the
+        # verify pass can be launched as CUDA graphs (the first draft pass of a step stays
+        # a stream launch: the GPU waits on it, and recording would delay its first kernel).
         self.graphs = graphs
         self.stream = torch.cuda.Stream(device=self.device)
 
@@ -167,7 +166,7 @@ class SpecEngine:
             r.d_seq.reserve(r.u_d + k - 1)
         bs_d, bs_t = self.d_pool.block_size, self.t_pool.block_size
         # --- upload 1: the first draft pass's plan and ids, so the GPU starts while
-        # the host builds the other plans (upload 2 queues behind that pass).
+        # the host builds the other plans (the later uploads queue behind that pass).
         plan0 = ForwardPlan([SeqSpec(r.d_seq.length, r.u_d, r.d_seq.blocks, 1) for r in reqs], bs_d)
         d_ids = [t for r in reqs for t in r.tokens[len(r.tokens) - r.u_d:]]
         (plan0_dev, d_ids_dev) = self._upload(0, [plan0.host, np.asarray(d_ids, np.int32)])
@@ -178,8 +177,16 @@ class SpecEngine:
         # between, as in the reference's order, while the first draft pass runs.
         for r in reqs:
             r.t_seq.reserve(r.u_t + k)
+        gd = "draft" if self.graphs else None
         plans = [plan0]
-        for j in range(1, k):
+        # Pass 1 goes first, with its own upload, so that it is recorded and launched
+        # while the GPU still runs pass 0; the other plans are built while pass 1 runs.
+        if k > 1:
+            plans.append(ForwardPlan([SeqSpec(r.d_seq.length + r.u_d, 1, r.d_seq.blocks, 1) for r in reqs], bs_d))
+            (plan1_dev,) = self._upload(1, [plans[1].host])
+            self.dr.forward(plans[1], self.drafts[0, :S], self.dlog[:S], plan_dev=plan1_dev, graph=gd)
+            ops.argmax_rows(self.dlog[:S], out=self.drafts[1, :S])
+        for j in range(2, k):
             plans.append(ForwardPlan([SeqSpec(r.d_seq.length + r.u_d + j - 1, 1, r.d_seq.blocks, 1)
                                       for r in reqs], bs_d))
         vplan = ForwardPlan([SeqSpec(r.t_seq.length, r.u_t + k, r.t_seq.blocks, k + 1) for r in reqs], bs_t)
@@ -189,14 +196,12 @@ class SpecEngine:
             v_ids.extend(r.tokens[len(r.tokens) - r.u_t:])
             v_ids.extend([0] * k)
             dst[:, i] = base + np.arange(k)
-        views = self._upload(1, [p.host for p in plans[1:]] + [vplan.host, np.asarray(v_ids, np.int32),
+        views = self._upload(2, [p.host for p in plans[2:]] + [vplan.host, np.asarray(v_ids, np.int32),
                                                                 dst.reshape(-1).astype(np.int32)])
         v_ids_dev, dst_dev = views[-2], views[-1].long()
-        for j in range(1, k):
-            # Pass 1 is a stream launch too: the host records a graph in about the time the
-            # GPU needs for pass 0, which is when it builds the remaining plans.
-            self.dr.forward(plans[j], self.drafts[j - 1, :S], self.dlog[:S], plan_dev=views[j - 1],
-                            graph="draft" if self.graphs and j >= 2 else None)
+        vplan_dev = views[-3]
+        for j in range(2, k):
+            self.dr.forward(plans[j], self.drafts[j - 1, :S], self.dlog[:S], plan_dev=views[j - 2], graph=gd)
             ops.argmax_rows(self.dlog[:S], out=self.drafts[j, :S])
         # --- verify: one target pass over every request's u+k rows
         drafts = self.drafts[:, :S]
@@ -205,7 +210,7 @@ class SpecEngine:
         if self.verify_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
-        self.tr.forward(vplan, v_ids_dev, tlog, plan_dev=views[k - 1], graph="verify" if self.graphs else None)
+        self.tr.forward(vplan, v_ids_dev, tlog, plan_dev=vplan_dev, graph="verify" if self.graphs else None)
         if self.verify_events is not None:
             ev1.record()
             self.verify_events.append((ev0, ev1, vplan))
