@@ -280,6 +280,16 @@ int kve_forward_graphed(const kve_model_t* model, const kve_batch_t* batch, cons
                         void** graph_slot, cudaStream_t stream);
 int kve_forward_graph_free(void* graph);
 
+/* Layers [l0, l1) of a kve_forward pass, as stream launches or recorded into a graph
+ * (no kvengine counterpart): l0 == 0 includes the embedding, l1 == num_layers the
+ * final norm and vocabulary projection. A pass split in two ranges, run in order on
+ * one stream, computes exactly what kve_forward computes; the split lets a caller
+ * start the first layers at once while it records the rest. */
+int kve_forward_layers(const kve_model_t* model, const kve_batch_t* batch, const kve_scratch_t* scratch, int l0,
+                       int l1, cudaStream_t stream);
+int kve_forward_layers_graphed(const kve_model_t* model, const kve_batch_t* batch, const kve_scratch_t* scratch,
+                               int l0, int l1, void** graph_slot, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -88,6 +88,9 @@ _SIGNATURES = {
     "kve_forward_graphed": (i32, [C.POINTER(ModelT), C.POINTER(BatchT), C.POINTER(ScratchT),
                                   C.POINTER(C.c_void_p), vp]),
     "kve_forward_graph_free": (i32, [vp]),
+    "kve_forward_layers": (i32, [C.POINTER(ModelT), C.POINTER(BatchT), C.POINTER(ScratchT), i32, i32, vp]),
+    "kve_forward_layers_graphed": (i32, [C.POINTER(ModelT), C.POINTER(BatchT), C.POINTER(ScratchT), i32, i32,
+                                         C.POINTER(C.c_void_p), vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

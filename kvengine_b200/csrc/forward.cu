@@ -36,9 +36,13 @@ extern "C" size_t kve_forward_attn_ws_bytes(const kve_model_t* m, int n_seqs, in
   return kve_paged_attn_workspace_bytes(n_seqs, max_q_len, max_ctx, m->num_heads, m->num_kv_heads, m->head_dim);
 }
 
-extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve_scratch_t* s,
-                           cudaStream_t stream) {
+// Layers [l0, l1) of a pass: the embedding when l0 == 0, the final norm and the
+// vocabulary projection when l1 == num_layers (kve_forward is the whole range).
+extern "C" int kve_forward_layers(const kve_model_t* m, const kve_batch_t* b, const kve_scratch_t* s, int l0,
+                                  int l1, cudaStream_t stream) {
   if (!m || !b || !s || !m->layers) return set_error(KVE_ERR_ARG, "kve_forward: null argument");
+  if (l0 < 0 || l1 > m->num_layers || l0 > l1)
+    return set_error(KVE_ERR_ARG, "kve_forward_layers: bad layer range [%d, %d)", l0, l1);
   if (b->n_tokens < 0 || b->n_seqs < 0 || b->n_out < 0)
     return set_error(KVE_ERR_ARG, "kve_forward: bad batch sizes");
   if (b->n_tokens == 0) return KVE_OK;
@@ -56,8 +60,8 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
                          (uintptr_t)s->q % 16 == 0 && (uintptr_t)m->rope_cos % 16 == 0 &&
                          (uintptr_t)m->rope_sin % 16 == 0;
 
-  KVE_TRY(kve_embed(b->ids, M, m->embed, dt, H, m->vocab, s->hidden, s->dev_status, stream));
-  for (int l = 0; l < m->num_layers; ++l) {
+  if (l0 == 0) KVE_TRY(kve_embed(b->ids, M, m->embed, dt, H, m->vocab, s->hidden, s->dev_status, stream));
+  for (int l = l0; l < l1; ++l) {
     const kve_layer_t& L = m->layers[l];
     KVE_TRY(rmsnorm_run(s->hidden, dt, L.ln1, M, H, m->rms_eps, nullptr, s->normed, true, stream));
     if (fused_qkv) {
@@ -90,11 +94,17 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
     KVE_TRY(gemm_run(s->act, L.w_down, dt, M, H, m->intermediate, KVE_EPI_RESIDUAL, nullptr, s->hidden,
                      s->hidden, dt, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
   }
-  if (b->n_out == 0) return KVE_OK;
+  if (b->n_out == 0 || l1 < m->num_layers) return KVE_OK;
   KVE_TRY(rmsnorm_run(s->hidden, dt, m->final_norm, b->n_out, H, m->rms_eps, b->out_rows, s->out_normed, true, stream));
   KVE_TRY(gemm_run(s->out_normed, m->lm_head, dt, b->n_out, m->vocab, H, KVE_EPI_STORE, nullptr, nullptr,
                    b->logits, b->logits_dtype, s->gemm_ws, s->gemm_ws_bytes, s->dev_status, KVE_GEMM_AUTO, true, stream));
   return KVE_OK;
+}
+
+extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve_scratch_t* s,
+                           cudaStream_t stream) {
+  if (!m) return set_error(KVE_ERR_ARG, "kve_forward: null argument");
+  return kve_forward_layers(m, b, s, 0, m->num_layers, stream);
 }
 
 // kve_forward recorded into a CUDA graph and launched as one: the pass's ~170 kernel
@@ -102,17 +112,19 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
 // the GPU without the per-launch work of a stream launch. The executable graph lives
 // in the caller's slot and is updated in place on later calls (the same launch
 // sequence with new pointers and sizes), or rebuilt when the update is refused.
-extern "C" int kve_forward_graphed(const kve_model_t* m, const kve_batch_t* b, const kve_scratch_t* s,
-                                   void** graph_slot, cudaStream_t stream) {
+extern "C" int kve_forward_layers_graphed(const kve_model_t* m, const kve_batch_t* b, const kve_scratch_t* s,
+                                          int l0, int l1, void** graph_slot, cudaStream_t stream) {
   if (!graph_slot) return set_error(KVE_ERR_ARG, "kve_forward_graphed: null graph slot");
   if (!m || !b || !s) return set_error(KVE_ERR_ARG, "kve_forward_graphed: null argument");
+  if (l0 < 0 || l1 > m->num_layers || l0 > l1)
+    return set_error(KVE_ERR_ARG, "kve_forward_layers_graphed: bad layer range [%d, %d)", l0, l1);
   if (b->n_tokens == 0) return KVE_OK;
   cudaError_t e = cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return set_error(KVE_ERR_CUDA, "kve_forward_graphed: stream capture: %s", cudaGetErrorString(e));
   }
-  const int rc = kve_forward(m, b, s, stream);
+  const int rc = kve_forward_layers(m, b, s, l0, l1, stream);
   cudaGraph_t graph = nullptr;
   e = cudaStreamEndCapture(stream, &graph);
   if (rc != KVE_OK || e != cudaSuccess || !graph) {
@@ -146,6 +158,12 @@ extern "C" int kve_forward_graphed(const kve_model_t* m, const kve_batch_t* b, c
     return set_error(KVE_ERR_CUDA, "kve_forward_graphed: launch: %s", cudaGetErrorString(e));
   }
   return KVE_OK;
+}
+
+extern "C" int kve_forward_graphed(const kve_model_t* m, const kve_batch_t* b, const kve_scratch_t* s,
+                                   void** graph_slot, cudaStream_t stream) {
+  if (!m) return set_error(KVE_ERR_ARG, "kve_forward_graphed: null argument");
+  return kve_forward_layers_graphed(m, b, s, 0, m->num_layers, graph_slot, stream);
 }
 
 extern "C" int kve_forward_graph_free(void* graph) {

@@ -250,10 +250,12 @@ class Runner:
                         plan.width, plan.n_out if logits is not None else 0, p("out_rows"), logits_ptr, ldt)
 
     def forward(self, plan: ForwardPlan, ids: torch.Tensor, logits: torch.Tensor | None,
-                plan_dev: torch.Tensor | None = None, graph: str | None = None) -> None:
+                plan_dev: torch.Tensor | None = None, graph: str | None = None, eager_layers: int = 0) -> None:
         """Launch one model pass. `ids`: int32 device [n_tokens]; logits: [n_out, V] or None.
         With `graph` (a slot name) the pass is recorded into that slot's CUDA graph and
-        launched as one graph (the current stream must not be the legacy default stream)."""
+        launched as one graph (the current stream must not be the legacy default stream);
+        `eager_layers` > 0 launches that many first layers as stream launches before
+        recording the rest, so the GPU starts at once."""
         if plan.n_tokens == 0:
             return
         self.ensure(plan.n_tokens, plan.n_out, len(plan.seqs), plan.max_q_len, plan.max_ctx)
@@ -267,8 +269,14 @@ class Runner:
                                     L.stream_handle(self.device)))
         else:
             slot = self._graphs.setdefault(graph, C.c_void_p())
-            L.check(lib.kve_forward_graphed(C.byref(self._model_c), C.byref(batch), C.byref(scratch),
-                                            C.byref(slot), L.stream_handle(self.device)))
+            n_layers = self.model.cfg.num_layers
+            e = min(max(eager_layers, 0), n_layers)
+            stream = L.stream_handle(self.device)
+            if e:
+                L.check(lib.kve_forward_layers(C.byref(self._model_c), C.byref(batch), C.byref(scratch), 0, e,
+                                               stream))
+            L.check(lib.kve_forward_layers_graphed(C.byref(self._model_c), C.byref(batch), C.byref(scratch), e,
+                                                   n_layers, C.byref(slot), stream))
 
     def check_status(self) -> None:
         code = int(self.status.item())

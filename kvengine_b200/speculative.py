@@ -108,11 +108,15 @@ class SpecEngine:
         # caller can time the verify step on the stream it runs on.
         self.verify_events: list | None = None
         # Steps run on the engine's own stream (ordered after, and followed by, the
-        # caller's current stream), so that the draft passes after the first and the
-        # verify pass can be launched as CUDA graphs (the first draft pass of a step stays
-        # a stream launch: the GPU waits on it, and recording would delay its first kernel).
+        # caller's current stream), so that the draft passes and the verify pass can be
+        # launched as CUDA graphs (the first layers of the first draft pass of a step stay
+        # stream launches: the GPU waits on them, and recording would delay its first kernel).
         self.graphs = graphs
         self.stream = torch.cuda.Stream(device=self.device)
+        # Layers of draft pass 0 launched before the rest is recorded: enough that
+        # recording the rest (about a third of the host time of launching it) ends
+        # before the GPU has run them.
+        self.eager0 = max(1, self.draft.cfg.num_layers * 5 // 12)
 
     def _ensure(self, S: int):
         if S <= self._cap:
@@ -171,7 +175,10 @@ class SpecEngine:
         d_ids = [t for r in reqs for t in r.tokens[len(r.tokens) - r.u_d:]]
         (plan0_dev, d_ids_dev) = self._upload(0, [plan0.host, np.asarray(d_ids, np.int32)])
         # --- draft: k passes, argmax feeding the next pass on the device
-        self.dr.forward(plan0, d_ids_dev, self.dlog[:S], plan_dev=plan0_dev)
+        # Pass 0: the first draft layers as stream launches (the GPU is idle until they
+        # arrive), the rest recorded into a graph while those run.
+        self.dr.forward(plan0, d_ids_dev, self.dlog[:S], plan_dev=plan0_dev,
+                        graph="draft0" if self.graphs else None, eager_layers=self.eager0)
         ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S])
         # The target reservations follow the draft ones with no allocator call in
         # between, as in the reference's order, while the first draft pass runs.
