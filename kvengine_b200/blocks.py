@@ -1,19 +1,26 @@
 """Host-side block allocator for the paged KV pool.
 
-Same contract as the reference's `BlockManager` (kvengine/blocks.py:70-353), so
-block tables come out identical for the same sequence of calls:
+Observable contract shared with the reference's `BlockManager`
+(kvengine/blocks.py:70-353), which block tables depend on, so the same call
+sequence yields the same tables:
 
-* the free list starts as [N-1, ..., 1, 0] and hands out from its end, so the
-  first allocation gets block 0 (blocks.py:91-93);
-* `allocate(n)` is atomic: it checks capacity before taking anything and raises
-  `OutOfBlocks(requested, available)` (blocks.py:150-174), spending truly free
-  blocks before evicting least-recently-released cached ones;
-* `free(ids)` is atomic across the batch, raises `DoubleFree` for an
-  unreferenced id, and appends released blocks in argument order
-  (blocks.py:194-213), which makes reuse LIFO;
-* reference counts and the content-addressed prefix registry (blake2b chain,
-  blocks.py:42-50, 217-310) are kept so `PagedSequenceCache.truncate` can apply
-  the reference's shared-block guard.
+* the first allocation of a fresh pool gets block 0, then 1, 2, ... (blocks.py:91-93);
+* released blocks are reused last-released-first, and one `free(ids)` call
+  releases in argument order (blocks.py:194-213);
+* `allocate(n)` changes nothing unless all n blocks can be handed out, else it
+  raises `OutOfBlocks(requested, available)` (blocks.py:150-174); blocks that
+  were never cached go first, then cached prefix blocks, least recently
+  released or looked up first;
+* a block whose reference count drops to zero while it holds a registered
+  prefix stays cached (findable by `lookup_prefix`) instead of becoming free.
+
+Design (not the reference's): every per-block fact lives in a flat list indexed
+by block id - reference count, owner, allocation serial, registered digest and
+tokens, and the links of an intrusive doubly linked LRU list threaded through
+the cached blocks (sentinel node at index `num_blocks`). Never-cached free
+blocks sit on a plain stack. Every operation is O(blocks touched); there are
+no per-block dict entries to create or delete on the spec loop's per-step
+allocate/free traffic.
 
 Tensor-free: the device pool lives in `kvengine_b200.paged`.
 """
@@ -22,14 +29,15 @@ from __future__ import annotations
 
 import hashlib
 import struct
-from collections import OrderedDict
-from collections.abc import Sequence
+from collections.abc import Iterable, Sequence
 
 ROOT_DIGEST = bytes(16)
 
 
 def chain_digest(parent: bytes, token_ids: Sequence[int]) -> bytes:
-    """Content address of a block: its int32 little-endian tokens chained on the parent digest."""
+    """Content address of a full block: blake2b-128 over the parent block's
+    address followed by the block's token ids as int32 little-endian, so a
+    block's address depends on every token before it (kvengine/blocks.py:42-50)."""
     h = hashlib.blake2b(parent, digest_size=16)
     h.update(struct.pack(f"<{len(token_ids)}i", *token_ids))
     return h.digest()
@@ -49,159 +57,229 @@ class DoubleFree(RuntimeError):
 
 
 class BlockManager:
+    """Reference-counted fixed-size blocks with an LRU cache of released prefix blocks."""
+
     def __init__(self, num_blocks: int, block_size: int):
         if num_blocks <= 0 or block_size <= 0:
             raise ValueError("num_blocks and block_size must be positive")
         self.num_blocks = num_blocks
         self.block_size = block_size
-        self._free: list[int] = list(range(num_blocks - 1, -1, -1))
-        self._refcount: dict[int, int] = {}
-        self._owner: dict[int, object] = {}
-        self._reclaimable: OrderedDict[int, None] = OrderedDict()
-        self._by_digest: dict[bytes, int] = {}
-        self._digest_of: dict[int, bytes] = {}
-        self._tokens_of: dict[int, tuple[int, ...]] = {}
         self.prefix_hits = 0
         self.prefix_misses = 0
         self.evictions = 0
+        self.reset()
 
-    # ------------------------------------------------------------- state
+    def reset(self) -> None:
+        """Every block free and uncached, as after construction."""
+        n = self.num_blocks
+        self._stack: list[int] = list(range(n - 1, -1, -1))   # never-cached free blocks; pop() hands out
+        self._refs = [0] * n                                   # > 0: referenced by that many sequences
+        self._owner: list[object] = [None] * n
+        self._serial = [0] * n                                 # allocation order, for free_owner
+        self._next_serial = 0
+        self._key: list[bytes | None] = [None] * n             # registered digest
+        self._toks: list[tuple | None] = [None] * n            # its tokens
+        self._where: dict[bytes, int] = {}                     # digest -> block
+        self._cached = bytearray(n)                            # 1: unreferenced, kept for its prefix
+        self._lru_prev = list(range(n + 1))                    # LRU links, sentinel at index n
+        self._lru_next = list(range(n + 1))
+        self._live = 0
+        self._n_cached = 0
+
+    # ------------------------------------------------------------- counts
     @property
     def num_free(self) -> int:
-        return len(self._free) + len(self._reclaimable)
+        """Blocks `allocate` can hand out: never-cached free ones plus cached ones."""
+        return len(self._stack) + self._n_cached
 
     @property
     def num_unused(self) -> int:
-        return len(self._free)
+        return len(self._stack)
 
     @property
     def num_reclaimable(self) -> int:
-        return len(self._reclaimable)
+        return self._n_cached
 
     @property
     def num_allocated(self) -> int:
-        return len(self._refcount)
+        return self._live
 
     @property
     def total_slots(self) -> int:
         return self.num_blocks * self.block_size
 
     def pool_utilization(self) -> float:
-        return self.num_allocated / self.num_blocks
+        return self._live / self.num_blocks
 
     def owner_of(self, block_id: int):
-        return self._owner.get(block_id)
+        return self._owner[block_id] if 0 <= block_id < self.num_blocks else None
 
     def refcount(self, block_id: int) -> int:
-        return self._refcount.get(block_id, 0)
+        return self._refs[block_id] if 0 <= block_id < self.num_blocks else 0
 
     def blocks_needed(self, n_tokens: int) -> int:
         return -(-n_tokens // self.block_size)
 
-    # -------------------------------------------------------- alloc/free
+    @property
+    def free_list(self) -> list[int]:
+        """The never-cached free blocks, next to be handed out LAST (a copy)."""
+        return list(self._stack)
+
+    def reclaimable_order(self) -> list[int]:
+        """Cached blocks from the next to be evicted to the most recently used."""
+        out, nxt, end = [], self._lru_next, self.num_blocks
+        b = nxt[end]
+        while b != end:
+            out.append(b)
+            b = nxt[b]
+        return out
+
+    # ----------------------------------------------------- LRU list links
+    def _lru_push(self, b: int) -> None:
+        end = self.num_blocks
+        last = self._lru_prev[end]
+        self._lru_next[last] = b
+        self._lru_prev[b] = last
+        self._lru_next[b] = end
+        self._lru_prev[end] = b
+        self._cached[b] = 1
+        self._n_cached += 1
+
+    def _lru_unlink(self, b: int) -> None:
+        p, n = self._lru_prev[b], self._lru_next[b]
+        self._lru_next[p] = n
+        self._lru_prev[n] = p
+        self._cached[b] = 0
+        self._n_cached -= 1
+
+    def _forget_prefix(self, b: int) -> None:
+        key = self._key[b]
+        if key is not None and self._where.get(key) == b:
+            del self._where[key]
+        self._key[b] = None
+        self._toks[b] = None
+
+    # --------------------------------------------------------- alloc/free
+    def _check_ids(self, ids: Iterable[int]) -> None:
+        for b in ids:
+            if not 0 <= b < self.num_blocks:
+                raise DoubleFree(f"block {b} is not referenced")
+
     def allocate(self, n_blocks: int, owner: object = None) -> list[int]:
         if n_blocks < 0:
             raise ValueError("n_blocks must be non-negative")
-        available = self.num_free
+        available = len(self._stack) + self._n_cached
         if n_blocks > available:
             raise OutOfBlocks(n_blocks, available)
-        taken = []
-        for _ in range(n_blocks):
-            taken.append(self._free.pop() if self._free else self._evict_lru())
+        from_stack = min(n_blocks, len(self._stack))
+        taken = self._stack[len(self._stack) - from_stack:][::-1]
+        del self._stack[len(self._stack) - from_stack:]
+        end = self.num_blocks
+        for _ in range(n_blocks - from_stack):
+            b = self._lru_next[end]         # least recently used cached block
+            self._lru_unlink(b)
+            self._forget_prefix(b)
+            self.evictions += 1
+            taken.append(b)
+        refs, own, serial = self._refs, self._owner, self._serial
         for b in taken:
-            self._refcount[b] = 1
-            self._owner[b] = owner
+            refs[b] = 1
+            own[b] = owner
+            serial[b] = self._next_serial
+            self._next_serial += 1
+        self._live += n_blocks
         return taken
 
     def incref(self, block_ids: Sequence[int]) -> None:
+        """One more reference on each id (prefix sharing); cached blocks come back into use."""
         ids = list(block_ids)
-        bad = [b for b in ids if b not in self._refcount and b not in self._reclaimable]
-        if bad:
-            raise DoubleFree(f"block {bad[0]} is neither referenced nor reclaimable")
+        self._check_ids(ids)
         for b in ids:
-            if b in self._reclaimable:
-                del self._reclaimable[b]
-                self._refcount[b] = 1
+            if self._refs[b] == 0 and not self._cached[b]:
+                raise DoubleFree(f"block {b} is neither referenced nor reclaimable")
+        for b in ids:
+            if self._cached[b]:
+                self._lru_unlink(b)
+                self._refs[b] = 1
+                self._live += 1
             else:
-                self._refcount[b] += 1
+                self._refs[b] += 1
 
     def free(self, block_ids) -> None:
+        """Drop one reference per id, in argument order; nothing changes if any id
+        (counting repeats) has no reference left to drop."""
         ids = list(block_ids)
-        # Validate the whole batch first (counting repeats) so a bad id frees nothing.
-        pending: dict[int, int] = {}
+        self._check_ids(ids)
+        refs = self._refs
+        if len(ids) == len(set(ids)):
+            for b in ids:
+                if refs[b] <= 0:
+                    raise DoubleFree(f"block {b} is not referenced")
+        else:
+            need: dict[int, int] = {}
+            for b in ids:
+                need[b] = need.get(b, 0) + 1
+            for b, c in need.items():
+                if refs[b] < c:
+                    raise DoubleFree(f"block {b} is not referenced")
         for b in ids:
-            pending[b] = pending.get(b, 0) + 1
-            if self._refcount.get(b, 0) < pending[b]:
-                raise DoubleFree(f"block {b} is not referenced")
-        for b in ids:
-            c = self._refcount[b] - 1
-            if c:
-                self._refcount[b] = c
+            refs[b] -= 1
+            if refs[b]:
                 continue
-            del self._refcount[b]
-            if b in self._digest_of:
-                self._reclaimable[b] = None
+            self._live -= 1
+            if self._key[b] is not None:
+                self._lru_push(b)           # stays findable until evicted
             else:
-                self._owner.pop(b, None)
-                self._free.append(b)
+                self._owner[b] = None
+                self._stack.append(b)
 
     def free_owner(self, owner: object) -> list[int]:
-        ids = [b for b, o in self._owner.items() if o == owner and b in self._refcount]
+        """Release every referenced block of `owner`, in the order they were allocated."""
+        ids = [b for b in range(self.num_blocks) if self._refs[b] > 0 and self._owner[b] == owner]
+        ids.sort(key=self._serial.__getitem__)
         self.free(ids)
         return ids
 
-    def reset(self) -> None:
-        self._free = list(range(self.num_blocks - 1, -1, -1))
-        for d in (self._refcount, self._owner, self._reclaimable, self._by_digest, self._digest_of,
-                  self._tokens_of):
-            d.clear()
-
-    # -------------------------------------------------- prefix registry
+    # --------------------------------------------------- prefix registry
     def register_prefix(self, block_id: int, digest: bytes, token_ids: Sequence[int]) -> bool:
+        """Publish a full, referenced block under its chain digest. Returns False when
+        the digest already names a different block (the caller keeps its own copy)."""
         if len(token_ids) != self.block_size:
-            raise ValueError(
-                f"only full blocks are shareable: got {len(token_ids)} tokens, block_size is {self.block_size}")
-        if digest in self._by_digest:
-            return self._by_digest[digest] == block_id
+            raise ValueError(f"a shared block must be full: {len(token_ids)} of {self.block_size} tokens")
+        holder = self._where.get(digest)
+        if holder is not None:
+            return holder == block_id
         if self.refcount(block_id) <= 0:
-            raise ValueError(f"cannot register unreferenced block {block_id}")
-        self._by_digest[digest] = block_id
-        self._digest_of[block_id] = digest
-        self._tokens_of[block_id] = tuple(token_ids)
+            raise ValueError(f"block {block_id} is not referenced and cannot be published")
+        self._forget_prefix(block_id)
+        self._where[digest] = block_id
+        self._key[block_id] = digest
+        self._toks[block_id] = tuple(token_ids)
         return True
 
     def lookup_prefix(self, digest: bytes, token_ids: Sequence[int]) -> int | None:
-        b = self._by_digest.get(digest)
-        if b is None or self._tokens_of.get(b) != tuple(token_ids):
+        """The published block for `digest` holding exactly `token_ids`, or None;
+        a cached hit becomes the most recently used."""
+        b = self._where.get(digest)
+        if b is None or self._toks[b] != tuple(token_ids):
             self.prefix_misses += 1
             return None
         self.prefix_hits += 1
-        if b in self._reclaimable:
-            self._reclaimable.move_to_end(b)
+        if self._cached[b]:
+            self._lru_unlink(b)
+            self._lru_push(b)
         return b
 
     def unregister_prefix(self, block_id: int) -> bool:
-        digest = self._digest_of.pop(block_id, None)
-        if digest is None:
+        """Withdraw a block's published prefix; a cached block becomes plainly free."""
+        if not 0 <= block_id < self.num_blocks or self._key[block_id] is None:
             return False
-        if self._by_digest.get(digest) == block_id:
-            del self._by_digest[digest]
-        self._tokens_of.pop(block_id, None)
-        if block_id in self._reclaimable:
-            del self._reclaimable[block_id]
-            self._owner.pop(block_id, None)
-            self._free.append(block_id)
+        self._forget_prefix(block_id)
+        if self._cached[block_id]:
+            self._lru_unlink(block_id)
+            self._owner[block_id] = None
+            self._stack.append(block_id)
         return True
-
-    def _evict_lru(self) -> int:
-        b, _ = self._reclaimable.popitem(last=False)
-        digest = self._digest_of.pop(b, None)
-        if digest is not None:
-            self._by_digest.pop(digest, None)
-        self._tokens_of.pop(b, None)
-        self._owner.pop(b, None)
-        self.evictions += 1
-        return b
 
     def prefix_hit_rate(self) -> float:
         total = self.prefix_hits + self.prefix_misses
@@ -209,21 +287,34 @@ class BlockManager:
 
     # -------------------------------------------------------- invariants
     def check_invariants(self) -> None:
-        free_set = set(self._free)
-        assert len(free_set) == len(self._free), "duplicate block in free list"
-        reclaim = set(self._reclaimable)
-        live = set(self._refcount)
-        assert not free_set & live, f"blocks both free and referenced: {sorted(free_set & live)}"
-        assert not free_set & reclaim, f"blocks both free and reclaimable: {sorted(free_set & reclaim)}"
-        assert not reclaim & live, f"blocks both reclaimable and referenced: {sorted(reclaim & live)}"
-        assert free_set | reclaim | live == set(range(self.num_blocks)), "blocks leaked"
-        assert all(c > 0 for c in self._refcount.values()), "non-positive refcount"
-        for digest, b in self._by_digest.items():
-            assert self._digest_of.get(b) == digest, f"prefix registry disagrees for block {b}"
-        for b in reclaim:
-            assert b in self._digest_of, f"reclaimable block {b} holds no registered prefix"
+        """Each block is in exactly one state (referenced, cached, stacked free), the
+        counters agree with the per-block facts, and the registry maps both ways."""
+        n = self.num_blocks
+        on_stack = bytearray(n)
+        for b in self._stack:
+            if on_stack[b]:
+                raise AssertionError(f"free stack holds block {b} twice")
+            on_stack[b] = 1
+        lru = self.reclaimable_order()
+        if len(lru) != self._n_cached or sum(self._cached) != self._n_cached:
+            raise AssertionError("cached-block count disagrees with the LRU list")
+        live = 0
+        for b in range(n):
+            states = (self._refs[b] > 0) + bool(self._cached[b]) + on_stack[b]
+            if states != 1:
+                raise AssertionError(f"block {b}: refcount {self._refs[b]}, cached {self._cached[b]}, "
+                                     f"stacked {on_stack[b]}")
+            if self._refs[b] < 0:
+                raise AssertionError(f"block {b} has a negative refcount")
+            live += self._refs[b] > 0
+            if self._cached[b] and self._key[b] is None:
+                raise AssertionError(f"cached block {b} has no published prefix")
+        if live != self._live:
+            raise AssertionError(f"live-block count {self._live}, counted {live}")
+        for key, b in self._where.items():
+            if self._key[b] != key:
+                raise AssertionError(f"registry maps a digest to block {b}, which holds another")
 
     def __repr__(self) -> str:
-        return (f"BlockManager(num_blocks={self.num_blocks}, block_size={self.block_size}, "
-                f"unused={self.num_unused}, reclaimable={self.num_reclaimable}, "
-                f"referenced={self.num_allocated})")
+        return (f"<BlockManager {self.num_blocks} x {self.block_size} tokens: {self._live} live, "
+                f"{self._n_cached} cached, {len(self._stack)} free>")

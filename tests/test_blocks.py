@@ -128,7 +128,7 @@ def test_churn_matches_reference_allocation_sequence():
                 ops.append(["oom", owner, want, e.available])
         m.check_invariants()
     assert ops == g["ops"]
-    assert m._free == g["final_free"]
+    assert m.free_list == g["final_free"]
 
 
 def test_prefix_registry_and_shared_truncate_guard():
@@ -207,5 +207,5 @@ def test_commit_and_keep_matches_commit_then_truncate():
                 s.pool.manager.check_invariants()
             assert (fast.blocks, fast.length, fast._digest_chain, fast._registered) == \
                 (slow.blocks, slow.length, slow._digest_chain, slow._registered)
-            assert pools[0].manager._free == pools[1].manager._free
-            assert list(pools[0].manager._reclaimable) == list(pools[1].manager._reclaimable)
+            assert pools[0].manager.free_list == pools[1].manager.free_list
+            assert pools[0].manager.reclaimable_order() == pools[1].manager.reclaimable_order()
