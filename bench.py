@@ -277,7 +277,8 @@ def run_gpu(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(oracle_models(target, draft), prompts[0])
+        gpu_tokens = [r.res.new_token_ids for r in collected[-1]]
+        cpu = cpu_baseline(oracle_models(target, draft), prompts, gpu_tokens)
 
     if rank == 0:
         line = {
@@ -297,70 +298,97 @@ def run_gpu(args):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if cpu is not None and "tokens_match" in cpu:
+            line["tokens_match"] = cpu["tokens_match"]
+            line["tokens_checked"] = cpu["tokens_checked"]
+            line["near_ties"] = len(cpu["near_ties"])
         print(json.dumps(line), flush=True)
 
 
 CPU_SAMPLE_TOKENS = 24
+CPU_SAMPLES = 5
 
 
 def oracle_models(target=None, draft=None):
-    """CPU oracle models holding the benchmark's weights (copied from the GPU
-    models when given, else the same seeded init generated on the GPU if one
-    is present, else on the CPU)."""
+    """CPU oracle models holding the benchmark's weights: copied from the GPU
+    models when given, else the same seeded init generated on the GPU if one is
+    present, else on the CPU."""
     from kvengine_b200.config import QWEN2_0_5B, QWEN2_3B
     from kvengine_b200.weights import init_state_dict
     from oracle.model import OracleModel
-
-    def from_device(m):
-        w, cfg, i = m.weights, m.cfg, m.cfg.intermediate_size
-        sd = {"model.embed_tokens.weight": w.embed.cpu(), "model.norm.weight": w.norm.cpu().to(m.dtype),
-              "lm_head.weight": w.lm_head.cpu()}
-        qs, ks = cfg.q_size, cfg.kv_size
-        for li, lw in enumerate(w.layers):
-            p = f"model.layers.{li}."
-            qkv, b = lw["w_qkv"].cpu(), lw["b_qkv"].cpu().to(m.dtype)
-            for n, a, z in (("q", 0, qs), ("k", qs, qs + ks), ("v", qs + ks, qs + 2 * ks)):
-                sd[p + f"self_attn.{n}_proj.weight"] = qkv[a:z]
-                sd[p + f"self_attn.{n}_proj.bias"] = b[a:z]
-            sd[p + "self_attn.o_proj.weight"] = lw["w_o"].cpu()
-            gu = lw["w_gu"].cpu().view(i, 2, -1)
-            sd[p + "mlp.gate_proj.weight"], sd[p + "mlp.up_proj.weight"] = gu[:, 0], gu[:, 1]
-            sd[p + "mlp.down_proj.weight"] = lw["w_down"].cpu()
-            sd[p + "input_layernorm.weight"] = lw["ln1"].cpu().to(m.dtype)
-            sd[p + "post_attention_layernorm.weight"] = lw["ln2"].cpu().to(m.dtype)
-        return sd
+    from oracle.spec import config4_oracle_models
 
     if target is not None:
-        t_sd, d_sd = from_device(target), from_device(draft)
-    else:
-        dev = "cuda" if torch.cuda.is_available() else "cpu"
-        t_sd = {k: v.cpu() for k, v in init_state_dict(QWEN2_3B, 2, dtype=torch.bfloat16, device=dev).items()}
-        d_sd = {k: v.cpu() for k, v in init_state_dict(QWEN2_0_5B, 1, dtype=torch.bfloat16, device=dev).items()}
+        return config4_oracle_models(target, draft)
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    t_sd = {k: v.cpu() for k, v in init_state_dict(QWEN2_3B, 2, dtype=torch.bfloat16, device=dev).items()}
+    d_sd = {k: v.cpu() for k, v in init_state_dict(QWEN2_0_5B, 1, dtype=torch.bfloat16, device=dev).items()}
     return OracleModel(QWEN2_3B, t_sd, torch.bfloat16), OracleModel(QWEN2_0_5B, d_sd, torch.bfloat16)
 
 
-def cpu_baseline(models, prompt):
-    """The CPU oracle (a port of the reference's speculative_greedy path) on a
-    bounded sample of the same workload: one request of the benchmark, the
-    prefill-fused first verify plus spec iterations until CPU_SAMPLE_TOKENS new
-    tokens, bf16, on every host thread."""
+def cpu_sample(models, prompt, verify_log=None):
+    """One bounded CPU sample: the oracle (a port of the reference's
+    speculative_greedy path) decodes one request of the benchmark - the
+    prefill-fused first verify, then spec iterations - until CPU_SAMPLE_TOKENS
+    new tokens, bf16, on every host thread. Returns (result, seconds)."""
     from oracle.paged import OraclePool
     from oracle.spec import oracle_speculative_greedy
 
-    cores = len(os.sched_getaffinity(0))
-    torch.set_num_threads(cores)
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     tm, dm = models
     tp = OraclePool(36, 2, 128, 64, BLOCK, torch.bfloat16)
     dp = OraclePool(24, 2, 64, 64, BLOCK, torch.bfloat16)
     t0 = time.perf_counter()
     res = oracle_speculative_greedy(tm, dm, prompt, tp.new_sequence(), dp.new_sequence(), k=K_SPEC,
-                                    max_new_tokens=CPU_SAMPLE_TOKENS)
-    dt = time.perf_counter() - t0
-    n = len(res["new_token_ids"])
-    return {"value": round(n / dt, 3), "unit": "accepted tokens/s", "cores": cores, "kind": "port",
-            "sample": f"1 request (prompt {PROMPT} ids), k={K_SPEC}, {n} new tokens in {res['iterations']} "
-                      f"iterations incl. the prefill-fused first verify; CPU oracle port of kvengine's "
-                      f"speculative_greedy in bf16; {dt:.1f} s"}
+                                    max_new_tokens=CPU_SAMPLE_TOKENS, verify_log=verify_log)
+    return res, time.perf_counter() - t0
+
+
+def _sample_text(n, iters, secs):
+    return (f"median of {CPU_SAMPLES} samples, each 1 request (prompt {PROMPT} ids, requests 0-{CPU_SAMPLES - 1} of "
+            f"the benchmark), k={K_SPEC}, {n} new tokens in {iters} iterations incl. the prefill-fused first "
+            f"verify; CPU oracle port of kvengine's speculative_greedy in bf16; {secs:.1f} s in all")
+
+
+def cpu_baseline(models, prompts, gpu_tokens=None):
+    """The CPU baseline on CPU_SAMPLES bounded samples (requests 0 .. CPU_SAMPLES-1
+    of the workload, one each), reported as the median. With `gpu_tokens` (the
+    GPU's new tokens per request), every GPU token of those requests is also
+    checked against the oracle teacher-forced along the GPU's own sequence (one
+    oracle pass of the full-depth target per request): `tokens_match` is true
+    when each token's oracle logit is within the bf16 logits tolerance (2e-2) of
+    that step's maximum; `tokens_exact` counts the tokens that are the oracle's
+    argmax outright and `near_ties` lists the others (a top-2 margin below the
+    tolerance)."""
+    from oracle.spec import teacher_forced_check
+
+    vals, total, n, iters = [], 0.0, 0, 0
+    checked = exact = 0
+    ok, near_ties, worst = True, [], 0.0
+    for i in range(CPU_SAMPLES):
+        res, dt = cpu_sample(models, prompts[i])
+        n, iters = len(res["new_token_ids"]), res["iterations"]
+        vals.append(n / dt)
+        total += dt
+        if gpu_tokens is not None:
+            tf = teacher_forced_check(models[0], prompts[i], list(gpu_tokens[i]), 2e-2)
+            ok = ok and tf["ok"]
+            checked += tf["checked"]
+            exact += tf["exact"]
+            worst = max(worst, tf["worst"])
+            near_ties += [dict(request=i, **t) for t in tf["near_ties"]]
+    out = {"value": round(statistics.median(vals), 3), "unit": "accepted tokens/s",
+           "cores": len(os.sched_getaffinity(0)), "kind": "port", "sample": _sample_text(n, iters, total),
+           "samples": [round(v, 3) for v in vals]}
+    if gpu_tokens is not None:
+        out["tokens_match"] = ok
+        out["tokens_checked"] = checked
+        out["tokens_exact"] = exact
+        out["near_ties"] = near_ties
+        out["worst_gap"] = worst
+        out["token_rule"] = ("every GPU token of requests 0-%d within 2e-2 of the CPU oracle's max logit, "
+                             "teacher-forced along the GPU's sequence (full-depth 3B target)" % (CPU_SAMPLES - 1))
+    return out
 
 
 def run_reference(args):
@@ -370,21 +398,26 @@ def run_reference(args):
     if rank != 0:
         return
     models = oracle_models()
-    prompt = random_prompts(N_REQ, PROMPT, seed=4)[0].tolist()
-    vals, info = [], None
+    prompts = random_prompts(N_REQ, PROMPT, seed=4).tolist()
+    vals, secs, n, iters = [], 0.0, 0, 0
     for i in range(args.warmup + args.steps):
-        info = cpu_baseline(models, prompt)
+        res, dt = cpu_sample(models, prompts[i % CPU_SAMPLES])
         if i >= args.warmup:
-            vals.append(info["value"])
-    v = statistics.mean(vals)
+            n, iters = len(res["new_token_ids"]), res["iterations"]
+            vals.append(n / dt)
+            secs += dt
+    v = statistics.median(vals)
+    sample = (f"median of {args.steps} steps, each 1 request (prompt {PROMPT} ids, requests 0-{CPU_SAMPLES - 1} of "
+              f"the benchmark in turn), k={K_SPEC}, {n} new tokens in {iters} iterations incl. the prefill-fused "
+              f"first verify; CPU oracle port of kvengine's speculative_greedy in bf16; {secs:.1f} s timed")
     line = {"impl": "reference", "metric": f"accepted tokens/s (0.5B->3B, k={K_SPEC})", "value": round(v, 3),
             "unit": "accepted tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random ids, random-init weights)",
             "config": {"workload": f"config 4 at k={K_SPEC}: 0.5B-arch draft (seed 1) -> 3B-arch target (seed 2), bf16",
-                       "sample_per_step": info["sample"]},
-            "cpu_baseline": {"value": round(v, 3), "unit": "accepted tokens/s", "cores": info["cores"],
-                             "kind": "port", "sample": info["sample"]},
+                       "sample_per_step": sample},
+            "cpu_baseline": {"value": round(v, 3), "unit": "accepted tokens/s",
+                             "cores": len(os.sched_getaffinity(0)), "kind": "port", "sample": sample},
             "e2e": {"value": round(v, 3), "unit": "accepted tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

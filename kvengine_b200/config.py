@@ -8,7 +8,7 @@ accepts anything that looks like a `Qwen2Config` (or a model carrying one).
 
 from __future__ import annotations
 
-from dataclasses import asdict, dataclass
+from dataclasses import asdict, dataclass, replace
 
 VOCAB_QWEN2 = 151936
 
@@ -132,9 +132,18 @@ TINY_HD128 = ModelConfig(
     intermediate_size=512, vocab_size=1024,
 )
 
+# The benchmark models' layer shapes (heads, head_dim, hidden, intermediate,
+# full vocabulary) at two layers: the reference runs them on CPU in well under a
+# second per pass, so the bf16 hot path of the 3B target (head_dim 128, 16/2
+# heads) and of the 0.5B draft is pinned to reference outputs at these shapes.
+QWEN2_3B_L2 = replace(QWEN2_3B, num_layers=2)
+QWEN2_0_5B_L2 = replace(QWEN2_0_5B, num_layers=2)
+
 PRESETS = {
     "qwen2.5-0.5b": QWEN2_0_5B,
     "qwen2.5-3b": QWEN2_3B,
+    "qwen2.5-0.5b-2layer": QWEN2_0_5B_L2,
+    "qwen2.5-3b-2layer": QWEN2_3B_L2,
     "tiny": TINY,
     "tiny-hd128": TINY_HD128,
 }

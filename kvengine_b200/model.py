@@ -177,6 +177,7 @@ class Runner:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.plan_dev = torch.zeros(1024, dtype=torch.int32, device=self.device)
         self._graphs: dict[str, C.c_void_p] = {}  # executable graphs of kve_forward_graphed, by slot name
+        self.graph_fallbacks: list[str] = []  # errors of graph-launched ranges that ran as stream launches
 
     def __del__(self):
         graphs = getattr(self, "_graphs", None)
@@ -275,8 +276,19 @@ class Runner:
             if e:
                 L.check(lib.kve_forward_layers(C.byref(self._model_c), C.byref(batch), C.byref(scratch), 0, e,
                                                stream))
-            L.check(lib.kve_forward_layers_graphed(C.byref(self._model_c), C.byref(batch), C.byref(scratch), e,
-                                                   n_layers, C.byref(slot), stream))
+            rc = lib.kve_forward_layers_graphed(C.byref(self._model_c), C.byref(batch), C.byref(scratch), e,
+                                                n_layers, C.byref(slot), stream)
+            if rc != L.KVE_OK:
+                # Recording or launching the graph failed (the stream is out of capture
+                # again and nothing of the range ran): finish the pass with stream
+                # launches, so a pass whose first layers already ran still completes.
+                msg = lib.kve_last_error().decode(errors="replace")
+                if slot.value:
+                    lib.kve_forward_graph_free(slot)
+                    slot.value = None
+                self.graph_fallbacks.append(msg)
+                L.check(lib.kve_forward_layers(C.byref(self._model_c), C.byref(batch), C.byref(scratch), e,
+                                               n_layers, stream))
 
     def check_status(self) -> None:
         code = int(self.status.item())

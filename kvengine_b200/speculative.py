@@ -89,7 +89,8 @@ class _Request:
 class SpecEngine:
     """Batched draft/verify/accept loop over one target and one draft model."""
 
-    def __init__(self, target, draft, target_pool, draft_pool, k: int, graphs: bool = True):
+    def __init__(self, target, draft, target_pool, draft_pool, k: int, graphs: bool = True,
+                 eager_layers: int | None = None):
         assert k >= 1, "k must be at least 1"
         self.target = as_model(target)
         self.draft = as_model(draft)
@@ -116,7 +117,9 @@ class SpecEngine:
         # Layers of draft pass 0 launched before the rest is recorded: enough that
         # recording the rest ends before the GPU has run them (a quarter of the layers
         # measured best on config 4: 6 of 24; 7, 8, 10 and 12 were 0.2-0.5 % slower).
-        self.eager0 = max(1, self.draft.cfg.num_layers // 4)
+        # `eager_layers` overrides it: 0 records the whole pass, num_layers launches it all.
+        n_layers = self.draft.cfg.num_layers
+        self.eager0 = max(1, n_layers // 4) if eager_layers is None else min(max(int(eager_layers), 0), n_layers)
 
     def _ensure(self, S: int):
         if S <= self._cap:

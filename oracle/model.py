@@ -129,3 +129,28 @@ def oracle_forward(model: OracleModel, ids: list[int], cache, all_logits: bool =
     if hidden_out is not None:
         hidden_out.append(hidden[0].clone())
     return model.lm_head(hidden)[0]
+
+
+def state_dict_from_device(model) -> dict:
+    """HuggingFace-named CPU state dict holding exactly the weights of a
+    kvengine_b200 `Model` (undoes the device packing: stacked q/k/v rows,
+    interleaved gate/up rows, fp32 bias and norm copies), so the oracle can run
+    the same weights the GPU ran."""
+    w, cfg, i = model.weights, model.cfg, model.cfg.intermediate_size
+    dt = model.dtype
+    sd = {"model.embed_tokens.weight": w.embed.cpu(), "model.norm.weight": w.norm.cpu().to(dt),
+          "lm_head.weight": w.lm_head.cpu()}
+    qs, ks = cfg.q_size, cfg.kv_size
+    for li, lw in enumerate(w.layers):
+        p = f"model.layers.{li}."
+        qkv, b = lw["w_qkv"].cpu(), lw["b_qkv"].cpu().to(dt)
+        for n, a, z in (("q", 0, qs), ("k", qs, qs + ks), ("v", qs + ks, qs + 2 * ks)):
+            sd[p + f"self_attn.{n}_proj.weight"] = qkv[a:z]
+            sd[p + f"self_attn.{n}_proj.bias"] = b[a:z]
+        sd[p + "self_attn.o_proj.weight"] = lw["w_o"].cpu()
+        gu = lw["w_gu"].cpu().view(i, 2, -1)
+        sd[p + "mlp.gate_proj.weight"], sd[p + "mlp.up_proj.weight"] = gu[:, 0], gu[:, 1]
+        sd[p + "mlp.down_proj.weight"] = lw["w_down"].cpu()
+        sd[p + "input_layernorm.weight"] = lw["ln1"].cpu().to(dt)
+        sd[p + "post_attention_layernorm.weight"] = lw["ln2"].cpu().to(dt)
+    return sd

@@ -102,3 +102,66 @@ def oracle_greedy_paged(model: OracleModel, prompt: list[int], cache, max_new_to
 def top2_margin(row: torch.Tensor) -> float:
     v = row.float().topk(2).values
     return float(v[0] - v[1])
+
+
+def verify_log_margins(verify_log: list) -> dict:
+    """Top-2 logits of the target row behind every emitted token of an
+    `oracle_speculative_greedy` run that was given `verify_log`: per iteration
+    the rows u-1 .. u-1+n decided the n accepted drafts and the bonus or
+    correction token (kvengine/speculative.py:167-182). Same layout as a greedy
+    run's per-step top-2 record ({"values": [[v0, v1], ...]}), so token-identity
+    checks can tell near-ties from real differences."""
+    values = []
+    for it in verify_log:
+        rows = it["rows"]
+        drafts = it["drafts"]
+        preds = torch.argmax(rows, dim=-1).tolist()
+        n = 0
+        while n < len(drafts) and preds[n] == drafts[n]:
+            n += 1
+        top = rows[: n + 1].float().topk(2, dim=-1).values
+        values.extend(top.tolist())
+    return {"values": values}
+
+
+def config4_oracle_models(target, draft):
+    """Oracle copies (CPU, bf16) of the benchmark's device-resident 3B target and
+    0.5B draft."""
+    from .model import state_dict_from_device
+
+    return (OracleModel(target.cfg, state_dict_from_device(target), torch.bfloat16),
+            OracleModel(draft.cfg, state_dict_from_device(draft), torch.bfloat16))
+
+
+@torch.no_grad()
+def teacher_forced_check(model: OracleModel, prompt: list[int], tokens: list[int], tol: float,
+                         cache_factory=None) -> dict:
+    """Check a generated sequence token by token against the oracle's logits.
+
+    One oracle pass over prompt + tokens[:-1] gives the logits row that predicts
+    every generated token along the sequence's OWN history, so a near-tie early
+    on does not end the comparison. Token j passes when its logit is within
+    `tol` of that row's maximum; `exact` counts tokens that are the row's argmax
+    (first index on ties, as torch.argmax), `near_ties` those that pass only by
+    the tolerance. `worst` is the largest (row max - token logit)."""
+    from .paged import OraclePool
+
+    if not tokens:
+        return {"ok": True, "checked": 0, "exact": 0, "near_ties": [], "worst": 0.0}
+    cfg = model.cfg
+    seq = (cache_factory() if cache_factory else
+           OraclePool(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim,
+                      -(-(len(prompt) + len(tokens)) // 16) + 1, 16, model.dtype).new_sequence())
+    ids = list(prompt) + list(tokens[:-1])
+    logits = oracle_forward(model, ids, seq, all_logits=True).float()
+    rows = logits[len(prompt) - 1:]
+    mx = rows.max(dim=-1).values
+    tok = torch.tensor(tokens, dtype=torch.long)
+    val = rows.gather(1, tok[:, None])[:, 0]
+    gap = (mx - val)
+    arg = rows.argmax(dim=-1)
+    exact = int((arg == tok).sum())
+    near = [{"position": j, "gap": round(float(gap[j]), 5)} for j in range(len(tokens))
+            if int(arg[j]) != tokens[j] and float(gap[j]) <= tol]
+    return {"ok": bool((gap <= tol).all()), "checked": len(tokens), "exact": exact, "near_ties": near,
+            "worst": round(float(gap.max()), 5)}

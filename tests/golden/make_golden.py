@@ -71,6 +71,35 @@ class Hostile:
         return self._head(hidden).roll(shifts=1, dims=-1)
 
 
+class Recording:
+    """Pass-through view of a model whose lm_head keeps every output it returns,
+    so the verify rows of a reference spec run can be read back afterwards."""
+
+    def __init__(self, base):
+        self.model = base.model
+        self.config = base.config
+        self.generation_config = base.generation_config
+        self._head = base.lm_head
+        self.outputs = []
+
+    def lm_head(self, hidden):
+        out = self._head(hidden)
+        self.outputs.append(out.detach().float())
+        return out
+
+
+def spec_margins(outputs, k, accepted_per_iter):
+    """Top-2 logit margin of the target row behind every emitted token: the verify
+    pass of iteration i fed u + k rows; rows u-1 .. u-1+n decided the n accepted
+    drafts and the bonus or correction (kvengine/speculative.py:160-182)."""
+    margins = []
+    for logits, n in zip(outputs, accepted_per_iter):
+        rows = logits[0, logits.shape[1] - k - 1:]
+        top = rows[: n + 1].topk(2, dim=-1).values
+        margins.extend((top[:, 0] - top[:, 1]).tolist())
+    return margins
+
+
 def tiny_fixtures(kv):
     """Spec/greedy sweeps on the two-layer models, fp32 and bf16, with full logits."""
     out = {}
@@ -143,6 +172,126 @@ def tiny_fixtures(kv):
             out[key] = rec
             print(f"  {key} done", flush=True)
     return out, arrays
+
+
+SHAPE3B_PROMPT_LENS = (5, 40, 130, 600)
+SHAPE3B_NEW = 16
+
+
+def shape3b_models():
+    """The two-layer models with the benchmark's layer shapes, bf16: target of the
+    3B architecture (seed 5) and draft of the 0.5B architecture (seed 6), both with
+    non-trivial biases and norm weights so a dropped bias or norm weight shows."""
+    from kvengine_b200.config import QWEN2_0_5B_L2, QWEN2_3B_L2
+
+    t_sd = init_state_dict(QWEN2_3B_L2, seed=5, bias_std=0.02, norm_jitter=0.1)
+    d_sd = init_state_dict(QWEN2_0_5B_L2, seed=6, bias_std=0.02, norm_jitter=0.1)
+    return (QWEN2_3B_L2, t_sd), (QWEN2_0_5B_L2, d_sd)
+
+
+def shape3b_prompts():
+    return [workloads.random_prompts(1, n, seed=50 + n)[0].tolist() for n in SHAPE3B_PROMPT_LENS]
+
+
+def shape3b_fixture(kv):
+    """bf16 greedy and speculative decoding at the benchmark's layer shapes (head_dim
+    128 / 16-2 heads target, head_dim 64 / 14-2 heads draft, full vocabulary), prompts
+    of 5, 40, 130 and 600 ids (the last spans two 512-key attention chunks): greedy
+    tokens with the top-2 logits of every step and a hash of the step logits, spec
+    tokens for k = 1, 2, 4, 8 with the target itself, the 0.5B-shape model and the
+    rolled-head target as drafts, and the rollback tables of one hostile run."""
+    (t_cfg, t_sd), (d_cfg, d_sd) = shape3b_models()
+    tm = hf_model(t_cfg, t_sd, torch.bfloat16)
+    dm = hf_model(d_cfg, d_sd, torch.bfloat16)
+    prompts = shape3b_prompts()
+    rec = {"prompts": prompts, "new_tokens": SHAPE3B_NEW, "greedy": [], "greedy_top2": [],
+           "greedy_logits_sha": [], "spec": {"self": {}, "small": {}, "hostile": {}}}
+    for p in prompts:
+        pool = kv.PagedKVCache.for_model(tm, num_blocks=256, block_size=16)
+        g = kv.greedy_paged(tm, torch.tensor([p]), pool, max_new_tokens=SHAPE3B_NEW, eos_token_id=None,
+                            collect_logits=True)
+        top = g.step_logits.float().topk(2, dim=-1)
+        rec["greedy"].append(g.new_token_ids)
+        rec["greedy_top2"].append({"values": top.values.tolist(), "indices": top.indices.tolist()})
+        rec["greedy_logits_sha"].append(sha(g.step_logits))
+    drafts = {"self": tm, "small": dm, "hostile": Hostile(tm)}
+    for name, draft in drafts.items():
+        for k in (1, 2, 4, 8):
+            rec["spec"][name][k] = []
+            for p in prompts:
+                t_pool = kv.PagedKVCache.for_model(tm, num_blocks=256, block_size=16)
+                d_pool = kv.PagedKVCache.for_model(draft if name != "hostile" else tm, num_blocks=256,
+                                                   block_size=16)
+                target = Recording(tm)
+                s = kv.speculative_greedy(target, draft, torch.tensor([p]), t_pool.new_sequence("t"),
+                                          d_pool.new_sequence("d"), k=k, max_new_tokens=SHAPE3B_NEW,
+                                          eos_token_id=None)
+                rec["spec"][name][k].append({"tokens": s.new_token_ids, "accepted_per_iter": s.accepted_per_iter,
+                                             "target_forwards": s.target_forwards,
+                                             "draft_forwards": s.draft_forwards,
+                                             "margins": spec_margins(target.outputs, k, s.accepted_per_iter)})
+        print(f"  shape3b spec {name} done", flush=True)
+    # Rollback: 0.5B-shape draft, k = 8, block size 4 (every iteration frees blocks).
+    t_pool = kv.PagedKVCache.for_model(tm, num_blocks=512, block_size=4)
+    d_pool = kv.PagedKVCache.for_model(dm, num_blocks=512, block_size=4)
+    t_seq, d_seq = t_pool.new_sequence("target"), d_pool.new_sequence("draft")
+    target = Recording(tm)
+    s = kv.speculative_greedy(target, dm, torch.tensor([prompts[1]]), t_seq, d_seq, k=8,
+                              max_new_tokens=SHAPE3B_NEW, eos_token_id=None)
+    rec["rollback"] = {"tokens": s.new_token_ids, "margins": spec_margins(target.outputs, 8, s.accepted_per_iter), "t_blocks": list(t_seq.blocks), "d_blocks": list(d_seq.blocks),
+                       "t_len": t_seq.length, "d_len": d_seq.length, "t_free": list(t_pool.manager._free),
+                       "d_free": list(d_pool.manager._free)}
+    return rec
+
+
+def attention_hd128_fixture(kv):
+    """The verify attention of the 3B target through the reference's
+    PagedSequenceCache.write/_gather and attend(): 16 query / 2 kv heads,
+    head_dim 128, 64 sequences x 5 query rows, bf16, block size 16, contexts
+    (a) as config 2 draws them (lognormal, median 512) and (b) as config 4's
+    decode has them (133..197)."""
+    out, arrays = {}, {}
+    for name, kw in (("lognormal", {}), ("config4", {"median_ctx": 165.0, "sigma": 0.1,
+                                                      "ctx_clip": (133, 197)})):
+        w = workloads.attention_workload(seed=7, num_heads=16, num_kv_heads=2, head_dim=128, **kw)
+        rec, arr = _attention_reference(kv, w)
+        out[name] = rec
+        arrays[f"{name}_attn_out_bf16"] = arr
+    return out, arrays
+
+
+def _attention_reference(kv, w):
+    from kvengine.forward import attend, causal_mask
+
+    nq, hd = w.q.shape[1], w.q.shape[2]
+    nkv = w.k_new.shape[1]
+
+    class A:
+        num_key_value_groups = nq // nkv
+        scaling = w.scale
+
+    pool = kv.PagedKVCache(num_layers=1, num_kv_heads=nkv, head_dim=hd, num_blocks=w.num_blocks,
+                           block_size=w.block_size, dtype=torch.bfloat16, device="cpu")
+    outs, k_sha = [], []
+    for b, ctx in enumerate(w.ctx_lens):
+        s = pool.new_sequence(b)
+        s.blocks = list(w.tables[b])
+        s._refresh_block_ids()
+        hist = ctx - w.q_len
+        if hist:
+            s.reserve(hist)
+            s.write(0, w.k_hist[b].transpose(0, 1)[None], w.v_hist[b].transpose(0, 1)[None], 0)
+            s.commit(hist)
+        s.reserve(w.q_len)
+        rows = slice(b * w.q_len, (b + 1) * w.q_len)
+        k_all, v_all = s.write(0, w.k_new[rows].transpose(0, 1)[None], w.v_new[rows].transpose(0, 1)[None], hist)
+        s.commit(w.q_len)
+        k_sha.append(sha(k_all))
+        q = w.q[rows].transpose(0, 1)[None]
+        mask = causal_mask(w.q_len, ctx, torch.bfloat16, torch.device("cpu"))
+        outs.append(attend(A, q, k_all, v_all, mask, use_sdpa=True)[0])
+    out = torch.cat(outs, 0)
+    return {"ctx_lens": w.ctx_lens, "k_gather_sha": k_sha}, out.view(torch.int16).numpy()
 
 
 def cfg1_fixture(kv):
@@ -295,7 +444,7 @@ def main():
     torch.set_num_threads(os.cpu_count() or 1)
     meta = {"torch": torch.__version__, "transformers": transformers.__version__,
             "generated_by": "tests/golden/make_golden.py (reference kvengine on CPU)"}
-    jobs = ["blocks", "accept", "attention", "tiny", "cfg1"]
+    jobs = ["blocks", "accept", "attention", "attention_hd128", "tiny", "shape3b", "cfg1"]
     if args.only:
         jobs = args.only.split(",")
     for job in jobs:
@@ -309,6 +458,10 @@ def main():
             rec, arr = attention_fixture(kv)
         elif job == "tiny":
             rec, arr = tiny_fixtures(kv)
+        elif job == "attention_hd128":
+            rec, arr = attention_hd128_fixture(kv)
+        elif job == "shape3b":
+            rec, arr = shape3b_fixture(kv), None
         elif job == "cfg1":
             rec, arr = cfg1_fixture(kv), None
         rec = {"meta": meta, "data": rec}

@@ -93,7 +93,7 @@ def test_budgets_eos_block_sizes_and_rollback_tables(cuda_device, tiny_state_dic
     assert s.new_token_ids == rb["tokens"]
     assert (t_seq.blocks, d_seq.blocks, t_seq.length, d_seq.length) == (
         rb["t_blocks"], rb["d_blocks"], rb["t_len"], rb["d_len"])
-    assert pool.manager._free == rb["free_list"]
+    assert pool.manager.free_list == rb["free_list"]
     assert len(t_seq.blocks) == pool.manager.blocks_needed(t_seq.length)
     t_seq.free()
     d_seq.free()
@@ -178,3 +178,57 @@ def test_config1_logits_within_1e3_of_oracle(cuda_device, cfg1_model):
     got = forward_with_own_cache(cfg1_model, torch.tensor([seqv], device=cuda_device), pool.new_sequence("x"),
                                  all_logits=True)[0].cpu()
     assert (got - ref).abs().max().item() <= 1e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_layer_ranges_and_graphs_compose_bit_identically(cuda_device, dtype):
+    """A pass split into stream-launched layers [0, e) and a graph-launched rest
+    [e, n) (kve_forward_layers + kve_forward_layers_graphed, the spec engine's first
+    draft pass) computes exactly what one kve_forward call computes, for e = 0, 1,
+    n/2 and n, with one graph slot reused across every split and pass shape (the
+    executable graph is updated in place or rebuilt): logits and the K/V pool are
+    bit-identical."""
+    from dataclasses import replace
+
+    from kvengine_b200.config import TINY
+    from kvengine_b200.forward import runner_for
+    from kvengine_b200.model import ForwardPlan, SeqSpec
+    from kvengine_b200.weights import init_state_dict
+
+    cfg = replace(TINY, num_layers=6)
+    m = Model(cfg, init_state_dict(cfg, seed=9, bias_std=0.02, norm_jitter=0.1), dtype, cuda_device)
+    pool = PagedKVCache.for_model(m, num_blocks=32, block_size=16)
+    runner = runner_for(m, pool)
+    g = torch.Generator().manual_seed(5)
+    chunks = [torch.randint(0, cfg.vocab_size, (T,), generator=g).to(torch.int32) for T in (37, 5, 1)]
+    stream = torch.cuda.Stream(device=cuda_device)
+
+    def run(graph, eager):
+        pool.manager.reset()            # same blocks, same slots, every run
+        pool.k.zero_()
+        pool.v.zero_()
+        seq = pool.new_sequence("x")
+        outs = []
+        with torch.cuda.stream(stream):
+            for ids in chunks:
+                T = ids.numel()
+                start = seq.length
+                seq.reserve(T)
+                plan = ForwardPlan([SeqSpec(start, T, list(seq.blocks), n_out=T)], pool.block_size)
+                logits = torch.empty(T, cfg.vocab_size, dtype=dtype, device=cuda_device)
+                runner.forward(plan, ids.to(cuda_device), logits, graph=graph, eager_layers=eager)
+                seq.commit(T)
+                outs.append(logits)
+        stream.synchronize()
+        state = ([o.cpu() for o in outs], pool.k.cpu().clone(), pool.v.cpu().clone())
+        seq.free()
+        return state
+
+    ref = run(None, 0)
+    for e in (0, 1, cfg.num_layers // 2, cfg.num_layers):
+        got = run("split", e)
+        for a, b in zip(got[0], ref[0]):
+            assert torch.equal(a, b), e
+        assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2]), e
+    assert runner.graph_fallbacks == []
+    runner.check_status()

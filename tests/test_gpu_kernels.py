@@ -59,7 +59,7 @@ def test_accept_config3_bit_exact(cuda_device, k):
         s.truncate(min(s.length, w.pre_len[b] + n[b] + 1))
     flat = np.array([x for s in seqs for x in s.blocks], dtype=np.int32)
     assert np.array_equal(flat, arr[f"k{k}_tables_flat"])
-    assert np.array_equal(np.array(pool.manager._free, np.int32), arr[f"k{k}_free_list"])
+    assert np.array_equal(np.array(pool.manager.free_list, np.int32), arr[f"k{k}_free_list"])
 
 
 def test_accept_bf16_ties_nan_and_k31(cuda_device):

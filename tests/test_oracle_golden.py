@@ -147,3 +147,71 @@ def test_oracle_cfg1_request0_matches_reference():
     out = oracle_speculative_greedy(m, m, p, pool.new_sequence(), pool.new_sequence(), k=4, max_new_tokens=64)
     assert out["new_token_ids"] == g["spec"][0]["tokens"] == g["greedy"][0] == g["hf_greedy_0"]
     assert out["accepted_per_iter"] == g["spec"][0]["accepted_per_iter"]
+
+
+# ------------------------------------------------ benchmark layer shapes (two layers, bf16)
+@pytest.fixture(scope="module")
+def shape3b_oracles(shape3b_state_dicts):
+    (t_cfg, t_sd), (d_cfg, d_sd) = shape3b_state_dicts["target"], shape3b_state_dicts["draft"]
+    return {"target": OracleModel(t_cfg, t_sd, torch.bfloat16), "small": OracleModel(d_cfg, d_sd, torch.bfloat16),
+            "hostile": OracleModel(t_cfg, t_sd, torch.bfloat16, roll_head=1)}
+
+
+def _pool_for(m, n=256, bs=16):
+    c = m.cfg
+    return OraclePool(c.num_layers, c.num_kv_heads, c.head_dim, n, bs, torch.bfloat16)
+
+
+def test_oracle_shape3b_greedy_matches_reference(shape3b_oracles):
+    """3B-shape target, bf16: greedy tokens and the bit pattern of every step's logits."""
+    g = load_golden("shape3b")
+    tm = shape3b_oracles["target"]
+    for i, p in enumerate(g["prompts"]):
+        log = []
+        out = oracle_greedy_paged(tm, p, _pool_for(tm).new_sequence(), g["new_tokens"], logits_log=log)
+        assert out["new_token_ids"] == g["greedy"][i]
+        assert _sha(torch.stack(log)) == g["greedy_logits_sha"][i]
+
+
+@pytest.mark.parametrize("name", ["self", "small", "hostile"])
+def test_oracle_shape3b_spec_matches_reference(shape3b_oracles, name):
+    g = load_golden("shape3b")
+    tm = shape3b_oracles["target"]
+    dm = shape3b_oracles["target" if name == "self" else name]
+    for k in (1, 2, 4, 8):
+        for i, p in enumerate(g["prompts"]):
+            out = oracle_speculative_greedy(tm, dm, p, _pool_for(tm).new_sequence(), _pool_for(dm).new_sequence(),
+                                            k=k, max_new_tokens=g["new_tokens"])
+            want = g["spec"][name][str(k)][i]
+            assert out["new_token_ids"] == want["tokens"], (name, k, i)
+            assert out["accepted_per_iter"] == want["accepted_per_iter"]
+            assert (out["target_forwards"], out["draft_forwards"]) == (want["target_forwards"],
+                                                                       want["draft_forwards"])
+
+
+def test_oracle_shape3b_rollback_tables_match_reference(shape3b_oracles):
+    g = load_golden("shape3b")
+    rb = g["rollback"]
+    tm, dm = shape3b_oracles["target"], shape3b_oracles["small"]
+    tp, dp = _pool_for(tm, 512, 4), _pool_for(dm, 512, 4)
+    t, d = tp.new_sequence(), dp.new_sequence()
+    out = oracle_speculative_greedy(tm, dm, g["prompts"][1], t, d, k=8, max_new_tokens=g["new_tokens"])
+    assert out["new_token_ids"] == rb["tokens"]
+    assert (t.blocks, d.blocks, t.length, d.length) == (rb["t_blocks"], rb["d_blocks"], rb["t_len"], rb["d_len"])
+    assert tp.alloc.free_list == rb["t_free"] and dp.alloc.free_list == rb["d_free"]
+
+
+@pytest.mark.parametrize("name", ["config4", "lognormal"])
+def test_oracle_attention_hd128_matches_reference(name):
+    """The 3B target's verify attention (16/2 heads, head_dim 128): gather hashes and
+    the bf16 output bit for bit."""
+    g = load_golden("attention_hd128")[name]
+    arr = load_golden_arrays("attention_hd128")
+    kw = {} if name == "lognormal" else {"median_ctx": 165.0, "sigma": 0.1, "ctx_clip": (133, 197)}
+    w = workloads.attention_workload(seed=7, num_heads=16, num_kv_heads=2, head_dim=128, **kw)
+    assert w.ctx_lens == g["ctx_lens"]
+    out, _, _, gathered = oracle_paged_attention(w, return_gathered=True)
+    for b, (kk, _) in enumerate(gathered):
+        assert _sha(kk[None]) == g["k_gather_sha"][b]
+    ref = torch.from_numpy(arr[f"{name}_attn_out_bf16"]).view(torch.bfloat16)
+    assert torch.equal(out, ref.view_as(out))
