@@ -94,6 +94,16 @@ int kve_greedy_accept_noalloc(const void* logits, int dtype, int64_t row_stride,
 int kve_argmax_rows(const void* x, int dtype, int rows, int cols, int64_t row_stride,
                     int32_t* out, cudaStream_t stream);
 
+/* kve_argmax_rows that also writes row i's result to scatter_out[scatter_idx[i]]
+ * (0 <= scatter_idx[i] < scatter_len; an index outside that range is skipped and
+ * KVE_ERR_BOUNDS is recorded in *dev_status, which may be NULL). Replaces the
+ * reference's host-side assembly of the verify feed `unseen + drafts`
+ * (kvengine/speculative.py:155,160-162): each draft lands in its slot of the
+ * verify pass's token ids on the device. */
+int kve_argmax_rows_scatter(const void* x, int dtype, int rows, int cols, int64_t row_stride, int32_t* out,
+                            const int32_t* scatter_idx, int32_t* scatter_out, int64_t scatter_len, int* dev_status,
+                            cudaStream_t stream);
+
 /* KV append: pool[slot_ids[t]] = new[t] for the K and V of one layer.
  * Replaces `pool.k_flat[layer].index_copy_(0, slots, k_src)` and the V twin,
  * kvengine/paged.py:310-311. k_new, v_new: [n_tokens, num_kv_heads, head_dim];
@@ -176,6 +186,12 @@ int kve_gemm_ex(const void* x, const void* w, int dtype, int m, int n, int k, in
  * GEMM. The split-K factor is never forced, so results are bit-identical under
  * every shape; only speed changes. */
 int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_chunks);
+
+/* Tuning hook (no kvengine counterpart): force the tcgen05 GEMM's split-K factor
+ * (1..8; 0 restores the model's choice, a function of (n, k) only) for later
+ * calls in this process. Unlike the other shape hooks this changes the summation
+ * order, hence the low bits of results; it exists for measuring launch shapes. */
+int kve_gemm_force_splits(int splits);
 
 /* Tuning and test hook (no kvengine counterpart): whether later tcgen05 GEMMs
  * without split-K run as CTA pairs (2-CTA MMA on 256-row tiles): 0 = the cost
@@ -272,13 +288,16 @@ int kve_forward(const kve_model_t* model, const kve_batch_t* batch, const kve_sc
                 cudaStream_t stream);
 
 /* kve_forward recorded into a CUDA graph and launched as one graph (no kvengine
- * counterpart; same results, fewer launch costs on the GPU). *graph_slot holds the
- * caller's executable graph: NULL on the first call, then updated in place by later
- * calls of the same launch sequence. The stream must not be the legacy default
- * stream (it cannot be captured). Free the slot with kve_forward_graph_free. */
+ * counterpart; same results, fewer launch costs on the GPU). *graph_slot is an
+ * opaque handle owned by the caller: NULL before the first call, then the library's
+ * record of the executable graph, which later calls update in place when they
+ * record the same kernels (same functions, block, shared-memory and cluster
+ * shapes; new pointers, sizes and grids) and rebuild otherwise. The stream must not
+ * be the legacy default stream (it cannot be captured). Free the handle with
+ * kve_forward_graph_free. */
 int kve_forward_graphed(const kve_model_t* model, const kve_batch_t* batch, const kve_scratch_t* scratch,
                         void** graph_slot, cudaStream_t stream);
-int kve_forward_graph_free(void* graph);
+int kve_forward_graph_free(void* graph_slot);
 
 /* Layers [l0, l1) of a kve_forward pass, as stream launches or recorded into a graph
  * (no kvengine counterpart): l0 == 0 includes the embedding, l1 == num_layers the

@@ -67,6 +67,7 @@ _SIGNATURES = {
     "kve_greedy_accept_noalloc_max_batch": (i32, []),
     "kve_greedy_accept_noalloc": (i32, [vp, i32, i64, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp]),
     "kve_argmax_rows": (i32, [vp, i32, i32, i32, i64, vp, vp]),
+    "kve_argmax_rows_scatter": (i32, [vp, i32, i32, i32, i64, vp, vp, vp, i64, vp, vp]),
     "kve_kv_append": (i32, [vp, vp, i32, vp, i32, i32, i32, vp, vp, i64, vp, vp]),
     "kve_qkv_rope_append": (i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp, vp, i64, vp, vp]),
     "kve_paged_attn_workspace_bytes": (sz, [i32, i32, i32, i32, i32, i32]),
@@ -79,6 +80,7 @@ _SIGNATURES = {
     "kve_gemm": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, i32, vp, sz, vp, vp]),
     "kve_gemm_force_shape": (i32, [i32, i32, i32]),
     "kve_gemm_force_pair": (i32, [i32]),
+    "kve_gemm_force_splits": (i32, [i32]),
     "kve_gemm_force_rows": (i32, [i32]),
     "kve_gemm_plan_info": (i32, [i32, i32, i32, vp]),
     "kve_gemm_ex": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, i32, vp, sz, vp, i32, vp]),

@@ -135,13 +135,25 @@ accept_kernel(const T* __restrict__ logits, int64_t row_stride, const int32_t* _
   if (lane == 0) n_acc[b] = n;
 }
 
+// Row argmax; with `scatter_out`, row i's result is also written to
+// scatter_out[scatter_idx[i]] (the draft loop places each draft token straight
+// into its slot of the verify pass's token ids).
 template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads)
-argmax_kernel(const T* __restrict__ x, int64_t row_stride, int cols, bool vec_ok, int32_t* __restrict__ out) {
+argmax_kernel(const T* __restrict__ x, int64_t row_stride, int cols, bool vec_ok, int32_t* __restrict__ out,
+              const int32_t* __restrict__ scatter_idx, int32_t* __restrict__ scatter_out, int64_t scatter_len,
+              int* __restrict__ status) {
   grid_dep_wait();
   grid_dep_launch();
   int best = row_argmax(x + (size_t)blockIdx.x * row_stride, cols, vec_ok);
-  if (threadIdx.x == 0) out[blockIdx.x] = best;
+  if (threadIdx.x == 0) {
+    out[blockIdx.x] = best;
+    if (scatter_out) {
+      const int j = scatter_idx[blockIdx.x];
+      if (j >= 0 && j < scatter_len) scatter_out[j] = best;
+      else report(status, KVE_ERR_BOUNDS);
+    }
+  }
 }
 
 bool vec_aligned(const void* p, int64_t row_stride, int elem) {
@@ -189,22 +201,44 @@ extern "C" int kve_greedy_accept(const void* logits, int dtype, int64_t row_stri
   return check_launch("kve_greedy_accept");
 }
 
+namespace {
+int argmax_launch(const void* x, int dtype, int rows, int cols, int64_t row_stride, int32_t* out,
+                  const int32_t* scatter_idx, int32_t* scatter_out, int64_t scatter_len, int* status,
+                  cudaStream_t stream) {
+  if (dtype == KVE_F32) {
+    launch_kernel(argmax_kernel<float>, dim3(rows), dim3(kArgmaxThreads), 0, stream,
+        static_cast<const float*>(x), row_stride, cols, vec_aligned(x, row_stride, 4), out, scatter_idx, scatter_out,
+        scatter_len, status);
+  } else if (dtype == KVE_BF16) {
+    launch_kernel(argmax_kernel<__nv_bfloat16>, dim3(rows), dim3(kArgmaxThreads), 0, stream,
+        static_cast<const __nv_bfloat16*>(x), row_stride, cols, vec_aligned(x, row_stride, 2), out, scatter_idx,
+        scatter_out, scatter_len, status);
+  } else {
+    return set_error(KVE_ERR_DTYPE, "kve_argmax_rows: dtype %d", dtype);
+  }
+  return check_launch("kve_argmax_rows");
+}
+}  // namespace
+
 extern "C" int kve_argmax_rows(const void* x, int dtype, int rows, int cols, int64_t row_stride,
                                int32_t* out, cudaStream_t stream) {
   if (rows < 0 || cols < 1 || row_stride < cols)
     return set_error(KVE_ERR_ARG, "kve_argmax_rows: bad sizes");
   if (rows == 0) return KVE_OK;
   if (!x || !out) return set_error(KVE_ERR_ARG, "kve_argmax_rows: null pointer");
-  if (dtype == KVE_F32) {
-    launch_kernel(argmax_kernel<float>, dim3(rows), dim3(kArgmaxThreads), 0, stream,
-        static_cast<const float*>(x), row_stride, cols, vec_aligned(x, row_stride, 4), out);
-  } else if (dtype == KVE_BF16) {
-    launch_kernel(argmax_kernel<__nv_bfloat16>, dim3(rows), dim3(kArgmaxThreads), 0, stream,
-        static_cast<const __nv_bfloat16*>(x), row_stride, cols, vec_aligned(x, row_stride, 2), out);
-  } else {
-    return set_error(KVE_ERR_DTYPE, "kve_argmax_rows: dtype %d", dtype);
-  }
-  return check_launch("kve_argmax_rows");
+  return argmax_launch(x, dtype, rows, cols, row_stride, out, nullptr, nullptr, 0, nullptr, stream);
+}
+
+extern "C" int kve_argmax_rows_scatter(const void* x, int dtype, int rows, int cols, int64_t row_stride,
+                                       int32_t* out, const int32_t* scatter_idx, int32_t* scatter_out,
+                                       int64_t scatter_len, int* dev_status, cudaStream_t stream) {
+  if (rows < 0 || cols < 1 || row_stride < cols || scatter_len < 0)
+    return set_error(KVE_ERR_ARG, "kve_argmax_rows_scatter: bad sizes");
+  if (rows == 0) return KVE_OK;
+  if (!x || !out || !scatter_idx || !scatter_out)
+    return set_error(KVE_ERR_ARG, "kve_argmax_rows_scatter: null pointer");
+  return argmax_launch(x, dtype, rows, cols, row_stride, out, scatter_idx, scatter_out, scatter_len, dev_status,
+                       stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -235,11 +235,23 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 
+// 2^x on the special-function unit (ex2.approx: relative error about 2^-22;
+// 2^-inf = +0). The bf16 kernel keeps its softmax in log2 units: scores are
+// scaled by scale * log2(e), so 2^(s - m) equals e^(scale * (q.k) - m').
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
 // Merge chunk partials in chunk order for the rows of one (sequence x kv-head,
 // query tile). A row at position pos reads chunks 0 .. pos / kChunk; with a
 // single chunk this reproduces acc / l exactly. Partials are read through L2
 // (another CTA of the same launch may have written them).
-template <typename T, int HD, int WARPS>
+// LOG2: the partials' running maxima are in log2 units (the bf16 kernel scores
+// with scale * log2(e) and exponentiates with 2^x); otherwise natural units.
+template <typename T, int HD, int WARPS, bool LOG2>
 __device__ __forceinline__ void merge_partials(const AttnParams& p, int bh, int qtile, int h, int rows,
                                                int first_pos, int qoff, int t0) {
   constexpr int DPL = HD / 32;
@@ -256,7 +268,7 @@ __device__ __forceinline__ void merge_partials(const AttnParams& p, int bh, int 
     for (int dd = 0; dd < DPL; ++dd) acc[dd] = 0.f;
     for (int c = 0; c < live; ++c) {
       const float* pr = base + c * partial_floats(HD) + (size_t)r * (HD + 2);
-      float w = expf(__ldcg(pr + HD) - mx);
+      float w = LOG2 ? ex2f(__ldcg(pr + HD) - mx) : expf(__ldcg(pr + HD) - mx);
       lsum += __ldcg(pr + HD + 1) * w;
 #pragma unroll
       for (int dd = 0; dd < DPL; ++dd) acc[dd] += __ldcg(pr + lane + dd * 32) * w;
@@ -290,15 +302,19 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   constexpr int DT = HD / 8;                        // n8 tiles of the output
   constexpr int CPR = HD * 2 / 16;                  // 16-byte chunks per key row
   constexpr int TCH = 2 * kMmaKeyTile * CPR;        // 16-byte chunks of one tile (K and V)
-  constexpr int SLOTS = kKeySlices * TCH / NTHR;    // chunks per thread per round
-  static_assert(kKeySlices * TCH % NTHR == 0, "round copy must divide evenly");
+  constexpr int TOTAL = kKeySlices * TCH;           // 16-byte chunks of one round
+  constexpr int SLOTS = (TOTAL + NTHR - 1) / NTHR;  // chunks per thread per round
   extern __shared__ __align__(128) uint8_t smem_dyn[];
   // The 128-byte swizzle repeats every 1024 bytes: TMA tiles start 1024-aligned.
   uint8_t* smem_attn = TMA ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023))
                            : smem_dyn;
   const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(smem_attn));
-  // buffers: [round buffer][slice][K|V] tiles, then the chunk's block table, then (TMA) the round barriers
-  uint64_t* round_full = reinterpret_cast<uint64_t*>(smem_attn + kRoundBufs * ROUND + kChunk * sizeof(int));
+  // buffers: [round buffer][slice][K|V] tiles (after the main loop: the slice merge
+  // area), then the chunk's block table, then (TMA) the round barriers
+  constexpr int XS = HD + 8;  // merge rows (floats), padded so the 8 rows g of a warp hit different banks
+  constexpr int MERGE = kKeySlices * RB * 16 * (XS + 2) * 4 + RB * 16 * (kKeySlices + 2) * 4;
+  constexpr int AREA = kRoundBufs * ROUND > MERGE ? kRoundBufs * ROUND : MERGE;
+  uint64_t* round_full = reinterpret_cast<uint64_t*>(smem_attn + AREA + kChunk * sizeof(int));
   if constexpr (TMA) {
     if (threadIdx.x == 0) {
       for (int b = 0; b < kRoundBufs; ++b) mbar_init(smem_u32(&round_full[b]), 1);
@@ -339,7 +355,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   const int32_t* table = p.tables + (size_t)b * p.table_stride;
 
   // The chunk's block-table entries, staged once (kChunk keys / block size).
-  int* tab = reinterpret_cast<int*>(smem_attn + kRoundBufs * ROUND);
+  int* tab = reinterpret_cast<int*>(smem_attn + AREA);
   const int blk_lo = BS > 0 ? key_lo / BS : key_lo / p.bs;
   const int n_blk = (BS > 0 ? (key_hi - 1) / BS : (key_hi - 1) / p.bs) - blk_lo + 1;
   for (int i = threadIdx.x; i < n_blk; i += NTHR) {
@@ -361,6 +377,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
 #pragma unroll
     for (int u = 0; u < SLOTS; ++u) {
       const int i = threadIdx.x + u * NTHR;
+      if (TOTAL % NTHR != 0 && i >= TOTAL) break;
       const int s = i / TCH, rem = i % TCH;
       const bool is_v = rem >= kMmaKeyTile * CPR;
       const int j = is_v ? rem - kMmaKeyTile * CPR : rem;
@@ -458,6 +475,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   const int pos_lo = first_pos + (r_lo < rows ? r_lo / p.group : 0);
   const int pos_hi = first_pos + (r_hi < rows ? r_hi / p.group : 0);
 
+  const float sl2 = p.scale * kLog2e;  // scores in log2 units
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
   float acc[DT][4];
 #pragma unroll
@@ -532,8 +550,8 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
         for (int e = 0; e < 2; ++e) {
           const int key = kt + 8 * j + 2 * tq + e;
           const bool ok = key < key_hi;
-          sc[j][e] = (ok && key <= pos_lo) ? sc[j][e] * p.scale : -INFINITY;
-          sc[j][2 + e] = (ok && key <= pos_hi) ? sc[j][2 + e] * p.scale : -INFINITY;
+          sc[j][e] = (ok && key <= pos_lo) ? sc[j][e] * sl2 : -INFINITY;
+          sc[j][2 + e] = (ok && key <= pos_hi) ? sc[j][2 + e] * sl2 : -INFINITY;
           mx_lo = fmaxf(mx_lo, sc[j][e]);
           mx_hi = fmaxf(mx_hi, sc[j][2 + e]);
         }
@@ -544,16 +562,16 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
       mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
       const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
       // Rows whose tile is fully masked keep their state exactly (factor 1, p = 0).
-      const float f_lo = mx_lo == -INFINITY ? 1.f : expf(m_lo - mn_lo);
-      const float f_hi = mx_hi == -INFINITY ? 1.f : expf(m_hi - mn_hi);
+      const float f_lo = mx_lo == -INFINITY ? 1.f : ex2f(m_lo - mn_lo);
+      const float f_hi = mx_hi == -INFINITY ? 1.f : ex2f(m_hi - mn_hi);
       float s_lo = 0.f, s_hi = 0.f;
       uint32_t pa[NT / 2][4];
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
-        const float p0 = sc[j][0] == -INFINITY ? 0.f : expf(sc[j][0] - mn_lo);
-        const float p1 = sc[j][1] == -INFINITY ? 0.f : expf(sc[j][1] - mn_lo);
-        const float p2 = sc[j][2] == -INFINITY ? 0.f : expf(sc[j][2] - mn_hi);
-        const float p3 = sc[j][3] == -INFINITY ? 0.f : expf(sc[j][3] - mn_hi);
+        const float p0 = sc[j][0] == -INFINITY ? 0.f : ex2f(sc[j][0] - mn_lo);
+        const float p1 = sc[j][1] == -INFINITY ? 0.f : ex2f(sc[j][1] - mn_lo);
+        const float p2 = sc[j][2] == -INFINITY ? 0.f : ex2f(sc[j][2] - mn_hi);
+        const float p3 = sc[j][3] == -INFINITY ? 0.f : ex2f(sc[j][3] - mn_hi);
         s_lo += p0 + p1;
         s_hi += p2 + p3;
         pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16(p0, p1);
@@ -602,21 +620,25 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   if constexpr (!TMA) asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
 
-  // Merge the key slices of each row block in slice order through shared memory
-  // (the round buffers are free now): slices 1.. publish, slice 0 merges. A
-  // slice that saw no key of a row has m = -inf and weight 0.
-  constexpr int XS = HD + 8;  // padded row (floats): the 8 rows g of a warp hit different banks
-  float* xs = reinterpret_cast<float*>(smem_attn);                 // [slice-1][rb][16 rows][XS]
-  float* xml = xs + (size_t)(kKeySlices - 1) * RB * 16 * XS;       // [slice-1][rb][16 rows][m, l]
-  if (ks > 0 && active) {
-    float* a = xs + (size_t)((ks - 1) * RB + rb) * 16 * XS;
+  // Merge the key slices of each row block (the round buffers are free now). Every
+  // slice publishes its unnormalised state (acc, m, l) per row; one thread per row
+  // turns the slice maxima into weights w_s = 2^(m_s - M) (0 for a slice that saw
+  // no key of the row) and the merged sum L = sum_s l_s w_s, in slice order; then
+  // each slice's warp finishes a quarter of the head dims: sum_s acc_s w_s in slice
+  // order, divided by L (or kept unnormalised as this chunk's partial).
+  float* xs = reinterpret_cast<float*>(smem_attn);                  // [slice][rb][16 rows][XS]
+  float* xml = xs + (size_t)kKeySlices * RB * 16 * XS;              // [slice][rb][16 rows][m, l]
+  float* xw = xml + (size_t)kKeySlices * RB * 16 * 2;               // [rb][16 rows][w_0..w_S-1, M, L]
+  constexpr int WS = kKeySlices + 2;
+  if (active) {
+    float* a = xs + (size_t)(ks * RB + rb) * 16 * XS;
 #pragma unroll
     for (int j = 0; j < DT; ++j) {
       *reinterpret_cast<float2*>(a + g * XS + 8 * j + 2 * tq) = make_float2(acc[j][0], acc[j][1]);
       *reinterpret_cast<float2*>(a + (g + 8) * XS + 8 * j + 2 * tq) = make_float2(acc[j][2], acc[j][3]);
     }
     if (tq == 0) {
-      float* ml = xml + (size_t)((ks - 1) * RB + rb) * 16 * 2;
+      float* ml = xml + (size_t)(ks * RB + rb) * 16 * 2;
       ml[g * 2] = m_lo;
       ml[g * 2 + 1] = l_lo;
       ml[(g + 8) * 2] = m_hi;
@@ -624,79 +646,75 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
     }
   }
   __syncthreads();
-  const bool writer = ks == 0 && active;
-  if (writer) {
-    float mm_lo = m_lo, mm_hi = m_hi;
+  if (active && ks == 0 && lane < 16) {
+    float ms[kKeySlices];
+    float mm = -INFINITY;
 #pragma unroll
-    for (int s = 1; s < kKeySlices; ++s) {
-      const float* ml = xml + (size_t)((s - 1) * RB + rb) * 16 * 2;
-      mm_lo = fmaxf(mm_lo, ml[g * 2]);
-      mm_hi = fmaxf(mm_hi, ml[(g + 8) * 2]);
+    for (int s2 = 0; s2 < kKeySlices; ++s2) {
+      ms[s2] = xml[(size_t)(s2 * RB + rb) * 32 + lane * 2];
+      mm = fmaxf(mm, ms[s2]);
     }
-    const float w0_lo = m_lo == -INFINITY ? 0.f : expf(m_lo - mm_lo);
-    const float w0_hi = m_hi == -INFINITY ? 0.f : expf(m_hi - mm_hi);
-    l_lo *= w0_lo;
-    l_hi *= w0_hi;
+    float lsum = 0.f;
+    float* w = xw + (size_t)(rb * 16 + lane) * WS;
 #pragma unroll
-    for (int j = 0; j < DT; ++j) {
-      acc[j][0] *= w0_lo; acc[j][1] *= w0_lo;
-      acc[j][2] *= w0_hi; acc[j][3] *= w0_hi;
+    for (int s2 = 0; s2 < kKeySlices; ++s2) {
+      const float ws = ms[s2] == -INFINITY ? 0.f : ex2f(ms[s2] - mm);
+      lsum += xml[(size_t)(s2 * RB + rb) * 32 + lane * 2 + 1] * ws;
+      w[s2] = ws;
     }
-#pragma unroll
-    for (int s = 1; s < kKeySlices; ++s) {
-      const float* ml = xml + (size_t)((s - 1) * RB + rb) * 16 * 2;
-      const float* a = xs + (size_t)((s - 1) * RB + rb) * 16 * XS;
-      const float ms_lo = ml[g * 2], ms_hi = ml[(g + 8) * 2];
-      const float w_lo = ms_lo == -INFINITY ? 0.f : expf(ms_lo - mm_lo);
-      const float w_hi = ms_hi == -INFINITY ? 0.f : expf(ms_hi - mm_hi);
-      l_lo += ml[g * 2 + 1] * w_lo;
-      l_hi += ml[(g + 8) * 2 + 1] * w_hi;
-#pragma unroll
-      for (int j = 0; j < DT; ++j) {
-        const float2 x_lo = *reinterpret_cast<const float2*>(a + g * XS + 8 * j + 2 * tq);
-        const float2 x_hi = *reinterpret_cast<const float2*>(a + (g + 8) * XS + 8 * j + 2 * tq);
-        acc[j][0] += x_lo.x * w_lo;
-        acc[j][1] += x_lo.y * w_lo;
-        acc[j][2] += x_hi.x * w_hi;
-        acc[j][3] += x_hi.y * w_hi;
-      }
-    }
-    m_lo = mm_lo;
-    m_hi = mm_hi;
+    w[kKeySlices] = mm;
+    w[kKeySlices + 1] = lsum;
   }
+  __syncthreads();
 
-  // Write the normalised output, or this chunk's partial; the last chunk CTA of
-  // this (sequence x kv-head, query tile) to finish then merges all of them.
+  // This warp's quarter of the head dims: QP float pairs per row, 16 rows.
+  constexpr int QP = HD / kKeySlices / 2;
+  constexpr int ITEMS = 16 * QP / 32;  // (row, pair) items per lane
+  const int d_base = ks * (HD / kKeySlices);
   if (p.ws == nullptr) {
-    if (!writer) return;
+    if (!active) return;
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = half ? r_hi : r_lo;
-      if (r >= rows) continue;
-      const float l = half ? l_hi : l_lo;
-      __nv_bfloat16* o = out + ((size_t)(qoff + t0 + r / p.group) * p.nq + h * p.group + r % p.group) * HD;
+    for (int it = 0; it < ITEMS; ++it) {
+      const int item = it * 32 + lane;
+      const int r = item / QP, d = d_base + 2 * (item % QP);
+      const int rr = rb * 16 + r;
+      if (rr >= rows) continue;
+      const float* w = xw + (size_t)(rb * 16 + r) * WS;
+      float o0 = 0.f, o1 = 0.f;
 #pragma unroll
-      for (int j = 0; j < DT; ++j) {
-        const float v0 = acc[j][half * 2] / l, v1 = acc[j][half * 2 + 1] / l;
-        *reinterpret_cast<uint32_t*>(o + 8 * j + 2 * tq) = pack_bf16(v0, v1);
+      for (int s2 = 0; s2 < kKeySlices; ++s2) {
+        const float2 x = *reinterpret_cast<const float2*>(xs + (size_t)((s2 * RB + rb) * 16 + r) * XS + d);
+        o0 += x.x * w[s2];
+        o1 += x.y * w[s2];
       }
+      const float l = w[kKeySlices + 1];
+      __nv_bfloat16* o = out + ((size_t)(qoff + t0 + rr / p.group) * p.nq + h * p.group + rr % p.group) * HD + d;
+      *reinterpret_cast<uint32_t*>(o) = pack_bf16(o0 / l, o1 / l);
     }
   } else {
     float* part = p.ws + ((((size_t)bh * p.n_qtiles + qtile) * p.n_chunks) + c) * partial_floats(HD);
+    if (active) {
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = half ? r_hi : r_lo;
-      if (!writer || r >= rows) continue;
-      float* pr = part + (size_t)r * (HD + 2);
+      for (int it = 0; it < ITEMS; ++it) {
+        const int item = it * 32 + lane;
+        const int r = item / QP, d = d_base + 2 * (item % QP);
+        const int rr = rb * 16 + r;
+        if (rr >= rows) continue;
+        const float* w = xw + (size_t)(rb * 16 + r) * WS;
+        float o0 = 0.f, o1 = 0.f;
 #pragma unroll
-      for (int j = 0; j < DT; ++j) {
-        pr[8 * j + 2 * tq] = acc[j][half * 2];
-        pr[8 * j + 2 * tq + 1] = acc[j][half * 2 + 1];
-      }
-      if (tq == 0) {
-        pr[HD] = half ? m_hi : m_lo;
-        pr[HD + 1] = half ? l_hi : l_lo;
+        for (int s2 = 0; s2 < kKeySlices; ++s2) {
+          const float2 x = *reinterpret_cast<const float2*>(xs + (size_t)((s2 * RB + rb) * 16 + r) * XS + d);
+          o0 += x.x * w[s2];
+          o1 += x.y * w[s2];
+        }
+        float* pr = part + (size_t)rr * (HD + 2);
+        *reinterpret_cast<float2*>(pr + d) = make_float2(o0, o1);
+        if (ks == 0 && (item % QP) == 0) {
+          pr[HD] = w[kKeySlices];
+          pr[HD + 1] = w[kKeySlices + 1];
+        }
       }
     }
     if (!p.counters) return;  // merged by attn_combine_kernel
@@ -713,7 +731,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
     __syncthreads();
     if (s_last) {
       __threadfence();
-      merge_partials<__nv_bfloat16, HD, NTHR / 32>(p, bh, qtile, h, rows, first_pos, qoff, t0);
+      merge_partials<__nv_bfloat16, HD, NTHR / 32, true>(p, bh, qtile, h, rows, first_pos, qoff, t0);
     }
   }
 }
@@ -731,7 +749,8 @@ attn_combine_kernel(AttnParams p) {
   const int t0 = qtile * p.qt;
   if (t0 >= ql) return;
   const int nt = min(p.qt, ql - t0);
-  merge_partials<T, HD, kWarps>(p, bh, qtile, h, nt * p.group, ctx - ql + t0, qoff, t0);
+  merge_partials<T, HD, kWarps, std::is_same<T, __nv_bfloat16>::value>(p, bh, qtile, h, nt * p.group,
+                                                                        ctx - ql + t0, qoff, t0);
 }
 
 template <int HD, int BS, int RB, bool TMA>
@@ -739,9 +758,10 @@ void launch_mma(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& m
   // round buffers (K + V of kKeySlices tiles, twice), then the chunk's block table
   // (<= kChunk entries) and the round barriers; the slice merge reuses the round buffers.
   constexpr size_t kRounds = (size_t)kRoundBufs * kKeySlices * 2 * kMmaKeyTile * (TMA ? HD * 2 : HD * 2 + 16);
-  constexpr size_t kMerge = (size_t)(kKeySlices - 1) * RB * 16 * (HD + 8 + 2) * sizeof(float);
-  static_assert(kMerge <= kRounds, "slice merge must fit in the round buffers");
-  constexpr size_t smem = kRounds + kChunk * sizeof(int) + kRoundBufs * sizeof(uint64_t) + (TMA ? 1024 : 0);
+  constexpr size_t kMerge = (size_t)kKeySlices * RB * 16 * (HD + 8 + 2) * sizeof(float) +
+                            (size_t)RB * 16 * (kKeySlices + 2) * sizeof(float);
+  constexpr size_t kArea = kRounds > kMerge ? kRounds : kMerge;
+  constexpr size_t smem = kArea + kChunk * sizeof(int) + kRoundBufs * sizeof(uint64_t) + (TMA ? 1024 : 0);
   static std::once_flag once;
   std::call_once(once, [] {
     cudaFuncSetAttribute(paged_attn_mma_kernel<HD, BS, RB, TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -755,6 +775,7 @@ void launch_mma_rb(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap
                    cudaStream_t stream) {
   if (p.rb == 1) launch_mma<HD, BS, 1, TMA>(p, mk, mv, grid, stream);
   else if (p.rb == 2) launch_mma<HD, BS, 2, TMA>(p, mk, mv, grid, stream);
+  else if (p.rb == 3) launch_mma<HD, BS, 3, TMA>(p, mk, mv, grid, stream);
   else launch_mma<HD, BS, 4, TMA>(p, mk, mv, grid, stream);
 }
 
@@ -813,7 +834,7 @@ int qtile_tokens(int group) { return group >= kMaxRows ? 1 : kMaxRows / group; }
 // (rows = tokens x group) of the call; a query tile holds 16 * rb / group tokens.
 int row_blocks(int max_q_len, int group) {
   const long long rows = (long long)max_q_len * group;
-  return rows <= 16 ? 1 : rows <= 32 ? 2 : 4;
+  return rows <= 16 ? 1 : rows <= 32 ? 2 : rows <= 48 ? 3 : 4;
 }
 int mma_qtile_tokens(int max_q_len, int group) { return row_blocks(max_q_len, group) * 16 / group; }
 

@@ -4,6 +4,9 @@
 #include "gemm_epilogue.cuh"
 #include "passes.cuh"
 
+#include <cstring>
+#include <vector>
+
 namespace {
 
 inline size_t max3(size_t a, size_t b, size_t c) { return a > b ? (a > c ? a : c) : (b > c ? b : c); }
@@ -109,9 +112,59 @@ extern "C" int kve_forward(const kve_model_t* m, const kve_batch_t* b, const kve
 
 // kve_forward recorded into a CUDA graph and launched as one: the pass's ~170 kernel
 // launches (programmatic dependent launches become programmatic graph edges) reach
-// the GPU without the per-launch work of a stream launch. The executable graph lives
-// in the caller's slot and is updated in place on later calls (the same launch
-// sequence with new pointers and sizes), or rebuilt when the update is refused.
+// the GPU without the per-launch work of a stream launch.
+//
+// The caller's slot holds a GraphSlot: the executable graph plus the signature of
+// the capture it was made from - per node its type and, for kernel nodes, the
+// function, block shape, dynamic shared memory and cluster shape. A later capture
+// with the same signature (same kernels, new pointers, sizes and grids) updates the
+// executable graph in place; any other capture re-instantiates it. Updating in place
+// across a change of kernel function, block shape or cluster shape (the attention
+// kernel's row blocks and the GEMMs' launch shapes depend on the batch) was measured
+// to leave some launches stale on this driver: a pass recorded for a prompt-sized
+// batch and then for a decode-sized one gave wrong results after the update.
+namespace {
+
+struct GraphSlot {
+  cudaGraphExec_t exec = nullptr;
+  std::vector<uint64_t> sig;
+};
+
+// False if some node could not be queried (the caller then re-instantiates).
+bool graph_signature(cudaGraph_t g, std::vector<uint64_t>& sig) {
+  sig.clear();
+  size_t n = 0;
+  if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess) return false;
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (n && cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) return false;
+  size_t edges = 0;
+  if (cudaGraphGetEdges(g, nullptr, nullptr, &edges) != cudaSuccess) return false;
+  sig.reserve(n * 5 + 2);
+  sig.push_back(n);
+  sig.push_back(edges);
+  for (cudaGraphNode_t node : nodes) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(node, &t) != cudaSuccess) return false;
+    sig.push_back((uint64_t)t);
+    if (t != cudaGraphNodeTypeKernel) continue;
+    cudaKernelNodeParams kp;
+    if (cudaGraphKernelNodeGetParams(node, &kp) != cudaSuccess) return false;
+    sig.push_back((uint64_t)(uintptr_t)kp.func);
+    sig.push_back((uint64_t)kp.blockDim.x | (uint64_t)kp.blockDim.y << 21 | (uint64_t)kp.blockDim.z << 42);
+    sig.push_back((uint64_t)kp.sharedMemBytes);
+    cudaKernelNodeAttrValue v;
+    memset(&v, 0, sizeof(v));
+    if (cudaGraphKernelNodeGetAttribute(node, cudaKernelNodeAttributeClusterDimension, &v) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    sig.push_back((uint64_t)v.clusterDim.x | (uint64_t)v.clusterDim.y << 21 | (uint64_t)v.clusterDim.z << 42);
+  }
+  return true;
+}
+
+}  // namespace
+
 extern "C" int kve_forward_layers_graphed(const kve_model_t* m, const kve_batch_t* b, const kve_scratch_t* s,
                                           int l0, int l1, void** graph_slot, cudaStream_t stream) {
   if (!graph_slot) return set_error(KVE_ERR_ARG, "kve_forward_graphed: null graph slot");
@@ -132,27 +185,34 @@ extern "C" int kve_forward_layers_graphed(const kve_model_t* m, const kve_batch_
     cudaGetLastError();
     return rc != KVE_OK ? rc : set_error(KVE_ERR_CUDA, "kve_forward_graphed: end capture: %s", cudaGetErrorString(e));
   }
-  cudaGraphExec_t exec = static_cast<cudaGraphExec_t>(*graph_slot);
-  if (exec) {
-    cudaGraphExecUpdateResultInfo info;
-    if (cudaGraphExecUpdate(exec, graph, &info) != cudaSuccess) {
-      cudaGetLastError();
-      cudaGraphExecDestroy(exec);
-      exec = nullptr;
-      *graph_slot = nullptr;
-    }
+  GraphSlot* slot = static_cast<GraphSlot*>(*graph_slot);
+  if (!slot) {
+    slot = new GraphSlot();
+    *graph_slot = slot;
   }
-  if (!exec) {
-    e = cudaGraphInstantiate(&exec, graph, 0);
+  std::vector<uint64_t> sig;
+  const bool sig_ok = graph_signature(graph, sig);
+  bool updated = false;
+  if (slot->exec && sig_ok && sig == slot->sig) {
+    cudaGraphExecUpdateResultInfo info;
+    updated = cudaGraphExecUpdate(slot->exec, graph, &info) == cudaSuccess;
+    if (!updated) cudaGetLastError();
+  }
+  if (!updated) {
+    if (slot->exec) cudaGraphExecDestroy(slot->exec);
+    slot->exec = nullptr;
+    slot->sig.clear();
+    e = cudaGraphInstantiate(&slot->exec, graph, 0);
     if (e != cudaSuccess) {
+      slot->exec = nullptr;
       cudaGraphDestroy(graph);
       cudaGetLastError();
       return set_error(KVE_ERR_CUDA, "kve_forward_graphed: instantiate: %s", cudaGetErrorString(e));
     }
-    *graph_slot = exec;
+    if (sig_ok) slot->sig.swap(sig);
   }
   cudaGraphDestroy(graph);
-  e = cudaGraphLaunch(exec, stream);
+  e = cudaGraphLaunch(slot->exec, stream);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return set_error(KVE_ERR_CUDA, "kve_forward_graphed: launch: %s", cudaGetErrorString(e));
@@ -166,7 +226,10 @@ extern "C" int kve_forward_graphed(const kve_model_t* m, const kve_batch_t* b, c
   return kve_forward_layers_graphed(m, b, s, 0, m->num_layers, graph_slot, stream);
 }
 
-extern "C" int kve_forward_graph_free(void* graph) {
-  if (graph) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph));
+extern "C" int kve_forward_graph_free(void* graph_slot) {
+  GraphSlot* slot = static_cast<GraphSlot*>(graph_slot);
+  if (!slot) return KVE_OK;
+  if (slot->exec) cudaGraphExecDestroy(slot->exec);
+  delete slot;
   return KVE_OK;
 }

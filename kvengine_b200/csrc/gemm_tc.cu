@@ -1635,6 +1635,8 @@ int choose_splits(int feat_tiles, int k_blocks, bool tma3d) {
 
 // Shape forced through kve_gemm_force_shape (0 = the model's choice).
 std::atomic<int> g_force_t{0}, g_force_mh{0}, g_force_kc{0};
+// Split-K factor forced through kve_gemm_force_splits (0 = the function of (n, k)).
+std::atomic<int> g_force_s{0};
 
 Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
   Plan p{};
@@ -1642,6 +1644,7 @@ Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
   p.k_blocks = (k + BK - 1) / BK;
   p.tma3d = k % BK == 0;
   p.splits = choose_splits(p.feat_tiles, p.k_blocks, p.tma3d);
+  if (const int fs = g_force_s.load()) p.splits = std::min(fs, std::max(1, p.k_blocks / 2));
   TileConfig c = best_config(m, p.feat_tiles, p.k_blocks, p.splits, p.tma3d, row_bytes, false);
   // Split-K stages carry several k-chunks too (the split factor itself is chosen
   // with one-chunk stages): fewer, larger TMA boxes measured 15 % faster for the
@@ -1879,6 +1882,16 @@ extern "C" int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_ch
   g_force_t.store(token_tiles);
   g_force_mh.store(weight_halves);
   g_force_kc.store(k_chunks);
+  g_plan_cache.clear();
+  return KVE_OK;
+}
+
+extern "C" int kve_gemm_force_splits(int splits) {
+  using namespace kve;
+  if (splits < 0 || splits > kMaxSplits)
+    return set_error(KVE_ERR_ARG, "kve_gemm_force_splits: 0 (model) or 1..%d", kMaxSplits);
+  std::lock_guard<std::mutex> g(g_plan_mu);
+  g_force_s.store(splits);
   g_plan_cache.clear();
   return KVE_OK;
 }

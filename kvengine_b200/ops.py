@@ -73,7 +73,11 @@ def greedy_accept(logits: torch.Tensor, drafts: torch.Tensor, workspace: Workspa
     return preds, n_acc, emitted
 
 
-def argmax_rows(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def argmax_rows(x: torch.Tensor, out: torch.Tensor | None = None, scatter_index: torch.Tensor | None = None,
+                scatter_out: torch.Tensor | None = None, status: torch.Tensor | None = None) -> torch.Tensor:
+    """int32 argmax of every row (first index on ties, NaN largest). With
+    `scatter_index` / `scatter_out` (contiguous int32), row i's result is also
+    written to scatter_out[scatter_index[i]]."""
     lib = L.load()
     L.require_cuda(x)
     rows, cols = x.shape
@@ -81,8 +85,18 @@ def argmax_rows(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
         raise ValueError("argmax_rows needs unit column stride")
     if out is None:
         out = torch.empty(rows, dtype=torch.int32, device=x.device)
-    L.check(lib.kve_argmax_rows(x.data_ptr(), L.dtype_code(x.dtype), rows, cols, x.stride(0),
-                                out.data_ptr(), L.stream_handle(x.device)))
+    if scatter_out is None:
+        L.check(lib.kve_argmax_rows(x.data_ptr(), L.dtype_code(x.dtype), rows, cols, x.stride(0),
+                                    out.data_ptr(), L.stream_handle(x.device)))
+        return out
+    for t in (scatter_index, scatter_out):
+        if t.dtype != torch.int32 or not t.is_contiguous() or not t.is_cuda:
+            raise ValueError("argmax_rows: scatter_index and scatter_out must be contiguous int32 CUDA tensors")
+    if scatter_index.numel() != rows:
+        raise ValueError("argmax_rows: one scatter index per row")
+    L.check(lib.kve_argmax_rows_scatter(x.data_ptr(), L.dtype_code(x.dtype), rows, cols, x.stride(0),
+                                        out.data_ptr(), scatter_index.data_ptr(), scatter_out.data_ptr(),
+                                        scatter_out.numel(), L.ptr(status), L.stream_handle(x.device)))
     return out
 
 

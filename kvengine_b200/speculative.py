@@ -172,17 +172,29 @@ class SpecEngine:
             r.u_t = len(r.tokens) - r.t_seq.length
             r.d_seq.reserve(r.u_d + k - 1)
         bs_d, bs_t = self.d_pool.block_size, self.t_pool.block_size
-        # --- upload 1: the first draft pass's plan and ids, so the GPU starts while
-        # the host builds the other plans (the later uploads queue behind that pass).
+        # --- upload 1: the first draft pass's plan and ids, and the verify pass's token
+        # ids with a slot per draft (the draft argmax kernels write the drafts there),
+        # so the GPU starts while the host builds the other plans (the later uploads
+        # queue behind that pass).
         plan0 = ForwardPlan([SeqSpec(r.d_seq.length, r.u_d, r.d_seq.blocks, 1) for r in reqs], bs_d)
         d_ids = [t for r in reqs for t in r.tokens[len(r.tokens) - r.u_d:]]
-        (plan0_dev, d_ids_dev) = self._upload(0, [plan0.host, np.asarray(d_ids, np.int32)])
+        v_ids, dst = [], np.empty((k, S), dtype=np.int32)
+        for i, r in enumerate(reqs):
+            base = len(v_ids) + r.u_t
+            v_ids.extend(r.tokens[len(r.tokens) - r.u_t:])
+            v_ids.extend([0] * k)
+            dst[:, i] = base + np.arange(k)
+        (plan0_dev, d_ids_dev, v_ids_dev, dst_dev) = self._upload(
+            0, [plan0.host, np.asarray(d_ids, np.int32), np.asarray(v_ids, np.int32), dst.reshape(-1)])
+        dst_dev = dst_dev.view(k, S)
+        status = self.tr.status
         # --- draft: k passes, argmax feeding the next pass on the device
         # Pass 0: the first draft layers as stream launches (the GPU is idle until they
         # arrive), the rest recorded into a graph while those run.
         self.dr.forward(plan0, d_ids_dev, self.dlog[:S], plan_dev=plan0_dev,
                         graph="draft0" if self.graphs else None, eager_layers=self.eager0)
-        ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S])
+        ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S], scatter_index=dst_dev[0], scatter_out=v_ids_dev,
+                        status=status)
         # The target reservations follow the draft ones with no allocator call in
         # between, as in the reference's order, while the first draft pass runs.
         for r in reqs:
@@ -195,27 +207,20 @@ class SpecEngine:
             plans.append(ForwardPlan([SeqSpec(r.d_seq.length + r.u_d, 1, r.d_seq.blocks, 1) for r in reqs], bs_d))
             (plan1_dev,) = self._upload(1, [plans[1].host])
             self.dr.forward(plans[1], self.drafts[0, :S], self.dlog[:S], plan_dev=plan1_dev, graph=gd)
-            ops.argmax_rows(self.dlog[:S], out=self.drafts[1, :S])
+            ops.argmax_rows(self.dlog[:S], out=self.drafts[1, :S], scatter_index=dst_dev[1], scatter_out=v_ids_dev,
+                            status=status)
         for j in range(2, k):
             plans.append(ForwardPlan([SeqSpec(r.d_seq.length + r.u_d + j - 1, 1, r.d_seq.blocks, 1)
                                       for r in reqs], bs_d))
         vplan = ForwardPlan([SeqSpec(r.t_seq.length, r.u_t + k, r.t_seq.blocks, k + 1) for r in reqs], bs_t)
-        v_ids, dst = [], np.empty((k, S), dtype=np.int64)
-        for i, r in enumerate(reqs):
-            base = len(v_ids) + r.u_t
-            v_ids.extend(r.tokens[len(r.tokens) - r.u_t:])
-            v_ids.extend([0] * k)
-            dst[:, i] = base + np.arange(k)
-        views = self._upload(2, [p.host for p in plans[2:]] + [vplan.host, np.asarray(v_ids, np.int32),
-                                                                dst.reshape(-1).astype(np.int32)])
-        v_ids_dev, dst_dev = views[-2], views[-1].long()
-        vplan_dev = views[-3]
+        views = self._upload(2, [p.host for p in plans[2:]] + [vplan.host])
+        vplan_dev = views[-1]
         for j in range(2, k):
             self.dr.forward(plans[j], self.drafts[j - 1, :S], self.dlog[:S], plan_dev=views[j - 2], graph=gd)
-            ops.argmax_rows(self.dlog[:S], out=self.drafts[j, :S])
+            ops.argmax_rows(self.dlog[:S], out=self.drafts[j, :S], scatter_index=dst_dev[j],
+                            scatter_out=v_ids_dev, status=status)
         # --- verify: one target pass over every request's u+k rows
         drafts = self.drafts[:, :S]
-        v_ids_dev.index_copy_(0, dst_dev, drafts.reshape(-1))
         tlog = self.tlog[: S * (k + 1)]
         if self.verify_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

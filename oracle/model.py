@@ -37,6 +37,11 @@ class OracleModel:
             cfg.rope_theta ** (torch.arange(0, hd, 2, dtype=torch.int64).to(dtype=torch.float) / hd)
         )
 
+    def as_fp32(self) -> "OracleModel":
+        """The same weights (already rounded to this model's dtype) evaluated in
+        fp32: the exact answer that a bf16 evaluation approximates."""
+        return OracleModel(self.cfg, self.sd, torch.float32, self.roll_head)
+
     def rmsnorm(self, x, w):
         xf = x.to(torch.float32)
         var = xf.pow(2).mean(-1, keepdim=True)

@@ -113,6 +113,30 @@ def test_argmax_rows(cuda_device):
     assert torch.equal(ops.argmax_rows(x.to(cuda_device)).cpu().long(), x.argmax(-1))
 
 
+def test_argmax_rows_scatter_places_drafts_in_the_verify_feed(cuda_device):
+    """The draft loop's argmax writes each row's token both to the drafts buffer and
+    to its slot of the verify pass's token ids (kvengine speculative.py:160-162:
+    unseen tokens followed by the drafts); an index outside the feed is skipped and
+    reported as KVE_ERR_BOUNDS."""
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(6, 151936, generator=g).to(torch.bfloat16)
+    x[2, 7] = x[2, 9] = 50.0                                     # tie: the lower index wins
+    feed = torch.full((40,), -5, dtype=torch.int32)
+    idx = torch.tensor([3, 11, 12, 20, 39, 0], dtype=torch.int32)
+    status = ops.status_tensor(cuda_device)
+    feed_d = feed.to(cuda_device)
+    got = ops.argmax_rows(x.to(cuda_device), scatter_index=idx.to(cuda_device), scatter_out=feed_d,
+                          status=status).cpu()
+    want = torch.argmax(x.float(), -1).to(torch.int32)
+    assert torch.equal(got, want) and int(got[2]) == 7
+    feed[idx.long()] = want
+    assert torch.equal(feed_d.cpu(), feed)
+    assert int(status.item()) == 0
+    bad = torch.tensor([0, 1, 2, 3, 40, 5], dtype=torch.int32, device=cuda_device)
+    ops.argmax_rows(x.to(cuda_device), scatter_index=bad, scatter_out=feed_d, status=status)
+    assert int(status.item()) == -7  # KVE_ERR_BOUNDS; the other rows were still written
+
+
 # ------------------------------------------------------------------ append / gather / rope
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_kv_append_matches_index_copy(cuda_device, dtype):
