@@ -208,6 +208,9 @@ def run_gpu(args):
     v_ms = statistics.mean(a.elapsed_time(b) for a, b, _ in steady) if steady else float("nan")
     wb = target.weights.weight_bytes()
     alg_b, alg_f = verify_algorithmic([p for _, _, p in steady], QWEN2_3B, wb)
+    ctx_sum = statistics.mean(float(p.host[p.offsets["ctx_lens"][0]: p.offsets["ctx_lens"][0] + p.offsets["ctx_lens"][1]]
+                                    .sum()) for _, _, p in steady) if steady else float(VERIFY_KERNEL_DRAM_CTX)
+    traffic = verify_pass_traffic(QWEN2_3B.num_layers, ctx_sum)
     pk = peaks()
     t_hbm = alg_b / (pk["hbm_gbs"] * 1e9)
     t_tc = alg_f / (pk["bf16_tflops_sustained"] * 1e12)
@@ -224,8 +227,8 @@ def run_gpu(args):
         "kernel": "verify step: kve_forward of the 3B target over B*(k+1)=320 rows (36 layers + lm_head)",
         "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
         "frac": round(achieved / peak, 4), "peak_src": pk["src"] + (" sustained" if bound == "tensor" else ""),
-        "traffic": VERIFY_PASS_DRAM_BYTES, "traffic_src": "ncu dram__bytes_read.sum + dram__bytes_write.sum summed "
-        "over the kernels of one steady verify pass (bench.py --profile-iteration, --cache-control none)",
+        "traffic": traffic, "traffic_src": "per-kernel ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+        "each (profiles/verify_pass_dram_config4.md) x launches per 36-layer pass; attention scaled by context",
         "verify_ms": round(v_ms, 4), "verify_passes_timed": len(steady),
         "alg_bytes_per_launch": round(alg_b), "alg_flops_per_launch": round(alg_f),
         "hbm_gbs_achieved": round(alg_b / (v_ms / 1e3) / 1e9, 1),
@@ -458,10 +461,26 @@ def _time_launches(fns, iters: int) -> float:
 
 L2_BYTES = 126 * 2**20
 
-# DRAM bytes (read + write) of one steady verify pass of the config-4 workload, summed
-# over its kernels from an ncu launch list of `bench.py --profile-iteration` with
-# dram__bytes_read.sum and dram__bytes_write.sum (measured, not modelled).
-VERIFY_PASS_DRAM_BYTES = 7_270_500_000
+# DRAM bytes (read + write) per launch of each kernel of a steady verify pass, from
+# single-kernel ncu captures (dram__bytes_read.sum + dram__bytes_write.sum, one launch
+# each, --cache-control none) of `bench.py --profile-verify-small`: the config-4 batch
+# (64 requests, k = 4, block size 16) on two-layer models with the benchmark's layer
+# shapes, whose per-layer kernels have the 36-layer pass's grids and shapes. Summary and
+# commands: profiles/verify_pass_dram_config4.md. The attention kernel's traffic is its
+# K/V reads; it is scaled by the timed plans' context sum over the captured case's
+# (64 sequences at context 136).
+VERIFY_KERNEL_DRAM = {
+    "embed": 1_047_808, "rmsnorm": 31_744, "qkv_rope_append_gemm": 10_690_000, "attention": 9_312_512,
+    "o_proj": 8_610_000, "gate_up_swiglu": 107_810_000, "down": 52_750_000, "lm_head": 721_610_000,
+}
+VERIFY_KERNEL_DRAM_CTX = 64 * 136
+
+
+def verify_pass_traffic(n_layers: int, ctx_sum: float) -> int:
+    k = VERIFY_KERNEL_DRAM
+    per_layer = (k["qkv_rope_append_gemm"] + k["o_proj"] + k["gate_up_swiglu"] + k["down"] + 2 * k["rmsnorm"]
+                 + k["attention"] * ctx_sum / VERIFY_KERNEL_DRAM_CTX)
+    return int(n_layers * per_layer + k["embed"] + k["rmsnorm"] + k["lm_head"])
 
 
 def run_micro(args):
@@ -604,6 +623,48 @@ def run_profile_iteration(args):
     print(json.dumps({"profiled": "one steady-state spec iteration", "requests": N_REQ, "k": K_SPEC}))
 
 
+def run_profile_verify_small(args):
+    """A small case of the verify pass for per-kernel DRAM counter captures: the two-layer
+    models with the benchmark's layer shapes (3B-shape target, 0.5B-shape draft, bf16,
+    full vocabulary; about 1.2 GB on the device), the benchmark's batch (64 requests x 128
+    prompt ids, k = 4, block size 16); after the prefill-fused first iteration and 3
+    steady ones, exactly one steady verify pass runs between cudaProfilerStart/Stop.
+    Every per-layer kernel of the 36-layer pass appears here with the same grid and
+    shape, so its per-launch traffic scales to the full pass by the layer count."""
+    from kvengine_b200 import Model, PagedKVCache, SpecEngine
+    from kvengine_b200.config import QWEN2_0_5B_L2, QWEN2_3B_L2
+    from kvengine_b200.speculative import _Request
+    from kvengine_b200.workloads import random_prompts
+
+    dev = torch.device("cuda", 0)
+    draft = Model.random_init(QWEN2_0_5B_L2, seed=1, dtype=torch.bfloat16, device=dev, init_device=dev)
+    target = Model.random_init(QWEN2_3B_L2, seed=2, dtype=torch.bfloat16, device=dev, init_device=dev)
+    prompts = random_prompts(N_REQ, PROMPT, seed=4).tolist()
+    nb = N_REQ * (-(-(PROMPT + NEW + 2 * K_SPEC + 2) // BLOCK)) + 64
+    t_pool = PagedKVCache.for_model(target, num_blocks=nb, block_size=BLOCK)
+    d_pool = PagedKVCache.for_model(draft, num_blocks=nb, block_size=BLOCK)
+    eng = SpecEngine(target, draft, t_pool, d_pool, K_SPEC)
+    reqs = [_Request(p, t_pool.new_sequence(f"t{i}"), d_pool.new_sequence(f"d{i}"), NEW)
+            for i, p in enumerate(prompts)]
+    for _ in range(4):
+        eng.step(reqs, set())
+    torch.cuda.synchronize()
+    orig = eng.tr.forward
+
+    def profiled(*a, **kw):
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        orig(*a, **kw)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+
+    eng.tr.forward = profiled
+    eng.step(reqs, set())
+    torch.cuda.synchronize()
+    print(json.dumps({"profiled": "one steady verify pass, two-layer 3B-shape target", "requests": N_REQ,
+                      "k": K_SPEC}))
+
+
 def run_serve(args):
     """Config 5: continuous-batching spec decode over a lognormal request mix
     (prompt mean 128, output mean 64, sigma 0.7, uniform tokens), requests sharded
@@ -688,6 +749,8 @@ def main():
     ap.add_argument("--micro", default=None, help="comma list of accept,attention,attention_decode,gemm microbenchmarks")
     ap.add_argument("--gemm-case", default=None, help="restrict --micro gemm to these shapes (comma list)")
     ap.add_argument("--profile-iteration", action="store_true")
+    ap.add_argument("--profile-verify-small", action="store_true",
+                    help="one steady verify pass of two-layer benchmark-shape models (for counter captures)")
     ap.add_argument("--serve", type=int, default=0, help="config 5: continuous batching over this many requests")
     ap.add_argument("--serve-batch", type=int, default=128, help="running requests per GPU (--serve)")
     ap.add_argument("--serve-blocks", type=int, default=8192, help="KV blocks per pool (--serve)")
@@ -702,6 +765,8 @@ def main():
         run_micro(args)
     elif args.profile_iteration:
         run_profile_iteration(args)
+    elif args.profile_verify_small:
+        run_profile_verify_small(args)
     elif args.serve:
         run_serve(args)
     elif args.impl == "reference":
