@@ -582,6 +582,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   uint4 res_first[E::NPASS];
   if (epi && a.splits == 1 && first_c0 < a.mt)
     E::load_res(a, tok0 + first_c0, min(kRows, a.mt - first_c0), col0, etid, res_first);
+  if constexpr (BMT == BM) {
+    // Split-K: the first chunk of tokens this CTA owns in the first round.
+    constexpr int kSumGroupsP = 2 * kEpiGroups * (kRows * E::W * E::ES) <= kStageBytes ? kEpiGroups : 1;
+    if (epi && a.splits > 1 && egrp < kSumGroupsP) {
+      const int ch0 = min(a.rch, a.mt);
+      const uint32_t rk = cluster_rank();
+      const int lo = (int)((long long)rk * ch0 / a.splits), hi = (int)((long long)(rk + 1) * ch0 / a.splits);
+      const int t0 = egrp * kRows;
+      if (t0 < hi - lo) E::load_res(a, tok0 + lo + t0, min(kRows, hi - lo - t0), col0, etid, res_first);
+    }
+  }
   bool have = false;
   if (epi) {
     have = !aborted && mbar_wait(smem_u32(tmem_full), 0, a.status);
@@ -641,18 +652,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         epi_bar_all();
-        if (egrp == 0 && etid == 0) {
-          const uint32_t mine = (uint32_t)(my_hi - my_lo);
-          mbar_expect_tx(smem_u32(recv_bar), (uint32_t)(S - 1) * mine * BM * 4);
-          for (int u = 0; u < S; ++u) {
-            if (u == (int)rank) continue;
+        // Thread u of the first warpgroup sends peer u its slice (one bulk copy each,
+        // issued in parallel: one thread issuing them in turn spent ~0.3 us per copy);
+        // thread `rank` arms this CTA's receive barrier for the S - 1 incoming slices.
+        if (egrp == 0 && etid < S) {
+          const int u = etid;
+          if (u == (int)rank) {
+            mbar_expect_tx(smem_u32(recv_bar), (uint32_t)(S - 1) * (uint32_t)(my_hi - my_lo) * BM * 4);
+          } else {
             const int lo = (int)((long long)u * ch / S), hi = (int)((long long)(u + 1) * ch / S);
-            if (hi <= lo) continue;
-            bulk_copy_to_peer(map_to(smem_u32(recv + (size_t)rank * slm * BM), (uint32_t)u),
-                              smem_u32(pout + (size_t)lo * BM), (uint32_t)(hi - lo) * BM * 4,
-                              map_to(smem_u32(recv_bar), (uint32_t)u));
+            if (hi > lo)
+              bulk_copy_to_peer(map_to(smem_u32(recv + (size_t)rank * slm * BM), (uint32_t)u),
+                                smem_u32(pout + (size_t)lo * BM), (uint32_t)(hi - lo) * BM * 4,
+                                map_to(smem_u32(recv_bar), (uint32_t)u));
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
-          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
         mbar_wait(smem_u32(recv_bar), (uint32_t)(round & 1), a.status);
         // Sum the S partials of each owned token in rank order (own slice from
@@ -670,7 +684,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
           const int n = min(kRows, mine - t0);
           uint8_t* buf = stg + (egrp * 2 + (it & 1)) * kStgBufC;
           uint4 res[E::NPASS];
-          E::load_res(a, tok0 + r0 + my_lo + t0, n, col0, etid, res);
+          if (round == 0 && it == 0) {
+#pragma unroll
+            for (int i = 0; i < E::NPASS; ++i) res[i] = res_first[i];
+          } else {
+            E::load_res(a, tok0 + r0 + my_lo + t0, n, col0, etid, res);
+          }
           for (int j0 = 0; j0 < n; j0 += 4) {
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -686,7 +705,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
           epi_bar(egrp);
           E::copy_out(a, buf, tok0 + r0 + my_lo + t0, n, col0, etid, res);
         }
-        if (egrp == 0 && etid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        if (egrp == 0 && etid < S && etid != (int)rank) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         epi_bar_all();
       }
     }
