@@ -88,9 +88,15 @@ class SeqSpec:
 
 @dataclass
 class ForwardPlan:
-    seqs: list[SeqSpec]
+    """The ragged batch of one model pass, as the int32 arrays the forward kernels
+    read (packed into `host` in one buffer, so one copy uploads it): per token its
+    position and pool slot, per sequence its query length, row offset, context
+    length and block-table row, and the rows whose logits are wanted."""
+
+    seqs: list[SeqSpec] | None
     block_size: int
     host: np.ndarray = field(init=False)
+    n_seqs: int = field(init=False)
     n_tokens: int = field(init=False)
     n_out: int = field(init=False)
     max_q_len: int = field(init=False)
@@ -99,22 +105,46 @@ class ForwardPlan:
     offsets: dict = field(init=False)
 
     def __post_init__(self):
+        if self.seqs is None:  # filled in by from_arrays
+            return
         seqs = self.seqs
         S = len(seqs)
-        bs = self.block_size
-        q = np.array([s.q_len for s in seqs], dtype=np.int64)
-        start = np.array([s.start for s in seqs], dtype=np.int64)
-        n_out = np.array([s.n_out for s in seqs], dtype=np.int64)
         nb = [len(s.blocks) for s in seqs]
-        nblk = np.array(nb, dtype=np.int64)
+        width = max(1, max(nb) if S else 1)
+        tables = np.zeros((S, width), dtype=np.int64)
+        if S:
+            nblk = np.array(nb, dtype=np.int64)
+            tables[np.arange(width) < nblk[:, None]] = list(chain.from_iterable(s.blocks for s in seqs))
+        else:
+            nblk = np.zeros(0, dtype=np.int64)
+        self._build(np.array([s.start for s in seqs], dtype=np.int64),
+                    np.array([s.q_len for s in seqs], dtype=np.int64),
+                    np.array([s.n_out for s in seqs], dtype=np.int64), tables, nblk)
+
+    @classmethod
+    def from_arrays(cls, start: np.ndarray, q_len: np.ndarray, n_out: np.ndarray, tables: np.ndarray,
+                    n_blocks: np.ndarray, block_size: int) -> "ForwardPlan":
+        """The same plan from per-sequence arrays: start positions, query lengths and
+        output-row counts [S], the zero-padded block tables [S, width] and each row's
+        block count [S] (a caller that keeps these arrays builds several plans over
+        one table without going back to the per-sequence lists)."""
+        plan = cls(None, block_size)
+        plan._build(np.asarray(start, dtype=np.int64), np.asarray(q_len, dtype=np.int64),
+                    np.asarray(n_out, dtype=np.int64), tables, np.asarray(n_blocks, dtype=np.int64))
+        return plan
+
+    def _build(self, start, q, n_out, tables, nblk):
+        S = q.shape[0]
+        bs = self.block_size
         M = int(q.sum())
+        self.n_seqs = S
         self.n_tokens = M
         self.max_q_len = int(q.max()) if S else 0
         ctx = start + q
         self.max_ctx = int(ctx.max()) if S else 0
         if S and bool((nblk * bs < ctx).any()):
             raise ValueError("block table does not cover the sequence (reserve first)")
-        width = self.width = max(1, max(nb) if S else 1)
+        self.width = tables.shape[1]
         q_off = np.zeros(S + 1, dtype=np.int64)
         np.cumsum(q, out=q_off[1:])
         if M == S and bool((q == 1).all()):      # one row per sequence (decode passes)
@@ -122,10 +152,6 @@ class ForwardPlan:
         else:
             seq_of_tok = np.repeat(np.arange(S), q)
             pos = (np.arange(M) - q_off[:-1][seq_of_tok]) + start[seq_of_tok]
-        # [S, width] block table, zero-padded
-        tables = np.zeros((S, width), dtype=np.int64)
-        if S:
-            tables[np.arange(width) < nblk[:, None]] = list(chain.from_iterable(s.blocks for s in seqs))
         slots = tables[seq_of_tok, pos // bs] * bs + pos % bs
         # logits rows: the last n_out rows of every sequence
         n_tot = int(n_out.sum())
@@ -135,15 +161,29 @@ class ForwardPlan:
             out_rows = (np.repeat(q_off[1:] - n_out, n_out)
                         + (np.arange(n_tot) - np.repeat(np.cumsum(n_out) - n_out, n_out)))
         self.n_out = n_tot
-        parts = {"positions": pos, "slots": slots, "q_lens": q, "q_offsets": q_off, "ctx_lens": ctx,
-                 "out_rows": out_rows, "tables": tables.reshape(-1)}
+        parts = (("positions", pos), ("slots", slots), ("q_lens", q), ("q_offsets", q_off), ("ctx_lens", ctx),
+                 ("out_rows", out_rows), ("tables", tables.reshape(-1)))
+        host = np.empty(sum(arr.shape[0] for _, arr in parts), dtype=np.int32)
         self.offsets = {}
-        chunks, off = [], 0
-        for name, arr in parts.items():
-            self.offsets[name] = (off, arr.shape[0])
-            chunks.append(arr)
-            off += arr.shape[0]
-        self.host = np.concatenate(chunks).astype(np.int32)
+        off = 0
+        for name, arr in parts:
+            n = arr.shape[0]
+            self.offsets[name] = (off, n)
+            host[off:off + n] = arr
+            off += n
+        self.host = host
+
+
+def block_tables(seqs, min_width: int = 1) -> tuple[np.ndarray, np.ndarray]:
+    """Zero-padded [len(seqs), width] int64 table of the sequences' block lists and
+    the block count of each row."""
+    nb = np.fromiter((len(s.blocks) for s in seqs), dtype=np.int64, count=len(seqs))
+    width = max(min_width, int(nb.max()) if len(seqs) else 1)
+    tables = np.zeros((len(seqs), width), dtype=np.int64)
+    if len(seqs):
+        tables[np.arange(width) < nb[:, None]] = np.fromiter(chain.from_iterable(s.blocks for s in seqs),
+                                                             dtype=np.int64, count=int(nb.sum()))
+    return tables, nb
 
 
 class Runner:
@@ -246,7 +286,7 @@ class Runner:
 
         logits_ptr = logits.data_ptr() if logits is not None else None
         ldt = L.dtype_code(logits.dtype) if logits is not None else self.dt
-        return L.BatchT(plan.n_tokens, len(plan.seqs), plan.max_q_len, plan.max_ctx, ids.data_ptr(),
+        return L.BatchT(plan.n_tokens, plan.n_seqs, plan.max_q_len, plan.max_ctx, ids.data_ptr(),
                         p("positions"), p("slots"), p("q_lens"), p("q_offsets"), p("ctx_lens"), p("tables"),
                         plan.width, plan.n_out if logits is not None else 0, p("out_rows"), logits_ptr, ldt)
 
@@ -259,7 +299,7 @@ class Runner:
         recording the rest, so the GPU starts at once."""
         if plan.n_tokens == 0:
             return
-        self.ensure(plan.n_tokens, plan.n_out, len(plan.seqs), plan.max_q_len, plan.max_ctx)
+        self.ensure(plan.n_tokens, plan.n_out, plan.n_seqs, plan.max_q_len, plan.max_ctx)
         if plan_dev is None:
             plan_dev = self.upload(plan)
         batch = self.batch_struct(plan, plan_dev, ids, logits)

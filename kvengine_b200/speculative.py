@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import time
 from dataclasses import dataclass, field
+from itertools import chain
 
 import numpy as np
 import torch
@@ -29,7 +30,7 @@ import torch
 from . import ops
 from .decode import AUTO_EOS, _resolve_eos, _sync
 from .forward import runner_for
-from .model import ForwardPlan, SeqSpec, as_model
+from .model import ForwardPlan, as_model, block_tables
 
 
 @dataclass
@@ -84,6 +85,27 @@ class _Request:
         self.max_new = max_new
         self.done = max_new <= 0
         self.u_d = self.u_t = 0
+
+
+def verify_feed(token_lists: list[list[int]], u_t: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """The verify pass's token ids and where the drafts go in them.
+
+    Request i feeds its last u_t[i] tokens (the ones the target has not seen)
+    followed by its k drafts, as kvengine/speculative.py:160-162 builds
+    `unseen + drafts`. Returns the int32 ids with zeros in the draft slots and
+    dst [k, S] int32: draft j of request i goes to ids[dst[j, i]]."""
+    S = len(token_lists)
+    u_t = np.asarray(u_t, dtype=np.int64)
+    v_len = u_t + k
+    v_off = np.zeros(S + 1, dtype=np.int64)
+    np.cumsum(v_len, out=v_off[1:])
+    seq_of = np.repeat(np.arange(S), v_len)
+    unseen = (np.arange(int(v_off[-1])) - v_off[:-1][seq_of]) < u_t[seq_of]
+    v_ids = np.zeros(int(v_off[-1]), dtype=np.int32)
+    v_ids[unseen] = np.fromiter(chain.from_iterable(t[len(t) - u:] for t, u in zip(token_lists, u_t.tolist())),
+                                dtype=np.int32, count=int(u_t.sum()))
+    dst = ((v_off[:-1] + u_t)[None, :] + np.arange(k)[:, None]).astype(np.int32)
+    return v_ids, dst
 
 
 class SpecEngine:
@@ -167,25 +189,30 @@ class SpecEngine:
         k, S = self.k, len(reqs)
         self._ensure(S)
         # --- block reservation, in the reference's order: draft feeds, then the verify feed.
+        lens = []
         for r in reqs:
-            r.u_d = len(r.tokens) - r.d_seq.length
-            r.u_t = len(r.tokens) - r.t_seq.length
+            n = len(r.tokens)
+            dl, tl = r.d_seq.length, r.t_seq.length
+            r.u_d, r.u_t = n - dl, n - tl
+            lens.append((dl, tl, n))
             r.d_seq.reserve(r.u_d + k - 1)
+        d_len, t_len, n_tok = np.array(lens, dtype=np.int64).T
+        u_d, u_t = n_tok - d_len, n_tok - t_len
         bs_d, bs_t = self.d_pool.block_size, self.t_pool.block_size
+        ones = np.ones(S, dtype=np.int64)
+        # One draft block table serves all k draft passes of the step (every slot they
+        # write was reserved above).
+        t_d, nb_d = block_tables([r.d_seq for r in reqs])
+        plan0 = ForwardPlan.from_arrays(d_len, u_d, ones, t_d, nb_d, bs_d)
         # --- upload 1: the first draft pass's plan and ids, and the verify pass's token
         # ids with a slot per draft (the draft argmax kernels write the drafts there),
         # so the GPU starts while the host builds the other plans (the later uploads
         # queue behind that pass).
-        plan0 = ForwardPlan([SeqSpec(r.d_seq.length, r.u_d, r.d_seq.blocks, 1) for r in reqs], bs_d)
-        d_ids = [t for r in reqs for t in r.tokens[len(r.tokens) - r.u_d:]]
-        v_ids, dst = [], np.empty((k, S), dtype=np.int32)
-        for i, r in enumerate(reqs):
-            base = len(v_ids) + r.u_t
-            v_ids.extend(r.tokens[len(r.tokens) - r.u_t:])
-            v_ids.extend([0] * k)
-            dst[:, i] = base + np.arange(k)
-        (plan0_dev, d_ids_dev, v_ids_dev, dst_dev) = self._upload(
-            0, [plan0.host, np.asarray(d_ids, np.int32), np.asarray(v_ids, np.int32), dst.reshape(-1)])
+        d_ids = np.fromiter(chain.from_iterable(r.tokens[len(r.tokens) - r.u_d:] for r in reqs), dtype=np.int32,
+                            count=int(u_d.sum()))
+        v_len = u_t + k
+        v_ids, dst = verify_feed([r.tokens for r in reqs], u_t, k)
+        (plan0_dev, d_ids_dev, v_ids_dev, dst_dev) = self._upload(0, [plan0.host, d_ids, v_ids, dst.reshape(-1)])
         dst_dev = dst_dev.view(k, S)
         status = self.tr.status
         # --- draft: k passes, argmax feeding the next pass on the device
@@ -204,15 +231,15 @@ class SpecEngine:
         # Pass 1 goes first, with its own upload, so that it is recorded and launched
         # while the GPU still runs pass 0; the other plans are built while pass 1 runs.
         if k > 1:
-            plans.append(ForwardPlan([SeqSpec(r.d_seq.length + r.u_d, 1, r.d_seq.blocks, 1) for r in reqs], bs_d))
+            plans.append(ForwardPlan.from_arrays(d_len + u_d, ones, ones, t_d, nb_d, bs_d))
             (plan1_dev,) = self._upload(1, [plans[1].host])
             self.dr.forward(plans[1], self.drafts[0, :S], self.dlog[:S], plan_dev=plan1_dev, graph=gd)
             ops.argmax_rows(self.dlog[:S], out=self.drafts[1, :S], scatter_index=dst_dev[1], scatter_out=v_ids_dev,
                             status=status)
         for j in range(2, k):
-            plans.append(ForwardPlan([SeqSpec(r.d_seq.length + r.u_d + j - 1, 1, r.d_seq.blocks, 1)
-                                      for r in reqs], bs_d))
-        vplan = ForwardPlan([SeqSpec(r.t_seq.length, r.u_t + k, r.t_seq.blocks, k + 1) for r in reqs], bs_t)
+            plans.append(ForwardPlan.from_arrays(d_len + u_d + j - 1, ones, ones, t_d, nb_d, bs_d))
+        t_t, nb_t = block_tables([r.t_seq for r in reqs])
+        vplan = ForwardPlan.from_arrays(t_len, v_len, np.full(S, k + 1, dtype=np.int64), t_t, nb_t, bs_t)
         views = self._upload(2, [p.host for p in plans[2:]] + [vplan.host])
         vplan_dev = views[-1]
         for j in range(2, k):
