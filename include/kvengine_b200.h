@@ -309,6 +309,37 @@ int kve_forward_layers(const kve_model_t* model, const kve_batch_t* batch, const
 int kve_forward_layers_graphed(const kve_model_t* model, const kve_batch_t* batch, const kve_scratch_t* scratch,
                                int l0, int l1, void** graph_slot, cudaStream_t stream);
 
+/* The next speculative step's first draft pass, planned on the device from this
+ * step's acceptance result (no kvengine counterpart as a kernel: it moves to the
+ * device the host bookkeeping between two iterations of kvengine/speculative.py,
+ * the rollback to the accepted prefix at :199-214 and the next
+ * `feed(draft, unseen)` at :147-158), so that the pass can be queued before the
+ * accept readback.
+ * Inputs per sequence s of this step: start_lens[s] = T0, its token count at the
+ * start of the step; last_tokens[s] = its token at position T0 - 1 (rows == 2
+ * only); n_blocks[s] and tables [n_seqs, width] its draft block count and block
+ * table (width >= max block count + 2); n_accepted [n_seqs] and emitted
+ * [n_seqs, k+1] as kve_greedy_accept writes them; dump_block: a pool block no
+ * sequence holds (a free block: later owners write it after this pass).
+ * rows == 1: one row per sequence, (position T0 + n, bonus emitted[s][n]); exact
+ * when n < k; a sequence with n == k gets position T0 + k - 1 (its first
+ * uncommitted draft position) and the caller must discard the pass.
+ * rows == 2: two rows per sequence, exact for every n: (T0 + n - 1, the token
+ * there) and (T0 + n, bonus); for n < k the first row rewrites a committed
+ * position with the same token and context, i.e. the same K/V bits.
+ * A row at a position past the sequence's n_blocks blocks reads and writes
+ * dump_block (table entries from n_blocks on are set to it); the caller must then
+ * discard the pass.
+ * Writes plan_out in the kve_batch_t layout, packed as positions [M] | slots [M] |
+ * q_lens [S] | q_offsets [S+1] | ctx_lens [S] | out_rows [S] | tables [S * width]
+ * (M = rows * S, logits row = the last row of each sequence), ids_out [M] (the
+ * rows' tokens) and verify_ids_out[s * (k+1)] (the bonus: row 0 of the next
+ * verify feed, whose other k rows the draft argmax kernels fill). */
+int kve_spec_next_draft_plan(const int32_t* start_lens, const int32_t* last_tokens, const int32_t* n_blocks,
+                             const int32_t* tables, int n_seqs, int width, int block_size, int k, int rows,
+                             int dump_block, const int32_t* n_accepted, const int32_t* emitted, int32_t* plan_out,
+                             int32_t* ids_out, int32_t* verify_ids_out, int* dev_status, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -93,6 +93,7 @@ _SIGNATURES = {
     "kve_forward_layers": (i32, [C.POINTER(ModelT), C.POINTER(BatchT), C.POINTER(ScratchT), i32, i32, vp]),
     "kve_forward_layers_graphed": (i32, [C.POINTER(ModelT), C.POINTER(BatchT), C.POINTER(ScratchT), i32, i32,
                                          C.POINTER(C.c_void_p), vp]),
+    "kve_spec_next_draft_plan": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -120,6 +120,12 @@ class BlockManager:
     def blocks_needed(self, n_tokens: int) -> int:
         return -(-n_tokens // self.block_size)
 
+    def unused_block(self) -> int | None:
+        """A never-cached free block (the last one `allocate` would hand out), without
+        allocating it, or None: scratch space for device work that must touch no
+        sequence's blocks (whoever allocates it later writes it after that work)."""
+        return self._stack[0] if self._stack else None
+
     @property
     def free_list(self) -> list[int]:
         """The never-cached free blocks, next to be handed out LAST (a copy)."""

@@ -19,7 +19,7 @@ INCLUDE = os.path.join(ROOT, "include")
 OBJDIR = os.path.join(ROOT, "_build")
 LIB = os.path.join(PKG, "libkvengine_b200.so")
 SOURCES = ["capi.cu", "accept.cu", "kv.cu", "attention.cu", "gemm.cu", "gemm_simt.cu", "gemm_tc.cu",
-           "forward.cu"]
+           "forward.cu", "step.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
                 f"-I{INCLUDE}"]

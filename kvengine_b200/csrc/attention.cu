@@ -203,11 +203,17 @@ paged_attn_kernel(AttnParams p) {
 // keys at fixed absolute positions, so results do not depend on the batch.
 constexpr int kMmaKeyTile = 32;
 // Key tile t of a chunk (32 keys at key_lo + 32 t) belongs to key slice
-// t % kKeySlices. The slices of a row block (16 query rows) run in separate warps
+// t % SL (SL = key_slices(head_dim)). The slices of a row block (16 query rows) run in separate warps
 // at the same time and their softmax states merge in slice order at the end, so
 // a row's arithmetic is the same whatever the number of row blocks in its CTA.
-constexpr int kKeySlices = 4;
-constexpr int kRoundBufs = 2;  // rounds (kKeySlices tiles each) staged in shared memory
+// Slices per row block: 8 for head_dim 64 (a round then covers 256 keys, so a
+// decode context of a few hundred keys takes one round), 4 for head_dim 128 (its
+// accumulators take twice the registers). A model has one head_dim, so all of
+// its passes slice alike. Row blocks per CTA are capped so the CTA stays at 16
+// warps.
+constexpr int key_slices(int hd) { return hd == 64 ? 8 : 4; }
+constexpr int max_row_blocks(int hd) { return hd == 64 ? 2 : 4; }
+constexpr int kRoundBufs = 2;  // rounds (one tile per slice each) staged in shared memory
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -285,7 +291,7 @@ __device__ __forceinline__ void merge_partials(const AttnParams& p, int bh, int 
 // chunk load from outside the tensor (zero fill) and the tail of the last
 // partial block is zeroed in shared memory. Otherwise 16-byte cp.async per thread.
 template <int HD, int BS, int RB, bool TMA>
-__global__ void __launch_bounds__(RB * kKeySlices * 32, 1)
+__global__ void __launch_bounds__(RB * key_slices(HD) * 32, 1)
 paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                       AttnParams p) {
   // With hist_static the wait moves down to the first load of a key written in
@@ -293,16 +299,17 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   bool waited = !p.hist_static;
   if (waited) grid_dep_wait();
   grid_dep_launch();
-  constexpr int NTHR = RB * kKeySlices * 32;
+  constexpr int SL = key_slices(HD);
+  constexpr int NTHR = RB * SL * 32;
   constexpr int ROW = HD * 2 + 16;                  // padded smem row (bytes, cp.async layout)
   constexpr int TILE = TMA ? kMmaKeyTile * HD * 2 : kMmaKeyTile * ROW;  // one K or V tile
-  constexpr int ROUND = kKeySlices * 2 * TILE;      // K and V of one round (kKeySlices tiles)
+  constexpr int ROUND = SL * 2 * TILE;      // K and V of one round (SL tiles)
   constexpr int KSTEPS = HD / 16;                   // k16 steps over the head dim
   constexpr int NT = kMmaKeyTile / 8;               // n8 tiles of keys per tile
   constexpr int DT = HD / 8;                        // n8 tiles of the output
   constexpr int CPR = HD * 2 / 16;                  // 16-byte chunks per key row
   constexpr int TCH = 2 * kMmaKeyTile * CPR;        // 16-byte chunks of one tile (K and V)
-  constexpr int TOTAL = kKeySlices * TCH;           // 16-byte chunks of one round
+  constexpr int TOTAL = SL * TCH;           // 16-byte chunks of one round
   constexpr int SLOTS = (TOTAL + NTHR - 1) / NTHR;  // chunks per thread per round
   extern __shared__ __align__(128) uint8_t smem_dyn[];
   // The 128-byte swizzle repeats every 1024 bytes: TMA tiles start 1024-aligned.
@@ -312,7 +319,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   // buffers: [round buffer][slice][K|V] tiles (after the main loop: the slice merge
   // area), then the chunk's block table, then (TMA) the round barriers
   constexpr int XS = HD + 8;  // merge rows (floats), padded so the 8 rows g of a warp hit different banks
-  constexpr int MERGE = kKeySlices * RB * 16 * (XS + 2) * 4 + RB * 16 * (kKeySlices + 2) * 4;
+  constexpr int MERGE = SL * RB * 16 * (XS + 2) * 4 + RB * 16 * (SL + 2) * 4;
   constexpr int AREA = kRoundBufs * ROUND > MERGE ? kRoundBufs * ROUND : MERGE;
   uint64_t* round_full = reinterpret_cast<uint64_t*>(smem_attn + AREA + kChunk * sizeof(int));
   if constexpr (TMA) {
@@ -344,7 +351,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   }
   const int key_hi = min(min(ctx, key_lo + kChunk), last_pos + 1);
   const int n_tiles = (key_hi - key_lo + kMmaKeyTile - 1) / kMmaKeyTile;
-  const int n_rounds = (n_tiles + kKeySlices - 1) / kKeySlices;
+  const int n_rounds = (n_tiles + SL - 1) / SL;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rb = warp % RB, ks = warp / RB;  // row block, key slice
@@ -368,7 +375,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   }
   __syncthreads();
 
-  // Round r holds tiles r*kKeySlices .. +kKeySlices-1 (tile s of the round at
+  // Round r holds tiles r*SL .. +SL-1 (tile s of the round at
   // slot s); every thread copies the same slots of every round.
   const size_t head_off = (size_t)h * HD;
   const size_t row_stride = (size_t)p.nkv * HD;  // elements between consecutive tokens
@@ -382,7 +389,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
       const bool is_v = rem >= kMmaKeyTile * CPR;
       const int j = is_v ? rem - kMmaKeyTile * CPR : rem;
       const int kk = j / CPR, ch = j % CPR;
-      const int tile = r * kKeySlices + s;
+      const int tile = r * SL + s;
       const int key = key_lo + tile * kMmaKeyTile + kk;
       const __nv_bfloat16* src = pk;
       uint32_t bytes = 0;
@@ -405,18 +412,22 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
     }
   };
 
-  // TMA round: thread 0 asks for every 16-key block of the round's tiles.
+  // TMA: thread 0 asks for the 16-key blocks of round r's tiles in slots [s0, s1);
+  // with `arm` it first arms the round's barrier for every tile of the round, so a
+  // round may be requested in two parts (history tiles before the dependency wait).
   const int oob_row = (int)(p.num_blocks * 16);  // first row past the pool: loads there fill zeros
-  auto tma_round = [&](int r) {
+  auto tma_tiles = [&](int r, int s0, int s1, bool arm) {
     if constexpr (TMA) {
       if (threadIdx.x != 0) return;
       const uint32_t fb = smem_u32(&round_full[r % kRoundBufs]);
       const uint32_t rbase = sbase + (uint32_t)((r % kRoundBufs) * ROUND);
-      int tiles = 0;
-      for (int s = 0; s < kKeySlices; ++s) tiles += r * kKeySlices + s < n_tiles;
-      mbar_expect_tx(fb, (uint32_t)(tiles * 2 * TILE));  // K and V of every tile of the round
-      for (int s = 0; s < kKeySlices; ++s) {
-        const int tile = r * kKeySlices + s;
+      if (arm) {
+        int tiles = 0;
+        for (int s = 0; s < SL; ++s) tiles += r * SL + s < n_tiles;
+        mbar_expect_tx(fb, (uint32_t)(tiles * 2 * TILE));  // K and V of every tile of the round
+      }
+      for (int s = s0; s < s1; ++s) {
+        const int tile = r * SL + s;
         if (tile >= n_tiles) break;
 #pragma unroll
         for (int jb = 0; jb < 2; ++jb) {
@@ -436,21 +447,46 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
       }
     }
   };
+  auto tma_round = [&](int r) { tma_tiles(r, 0, SL, true); };
 
-  // Prologue: kRoundBufs rounds in flight (one commit group per round, empty
-  // groups past the end). Rounds of history keys may load before the wait.
+  // Prologue: kRoundBufs rounds in flight. Keys written before this pass (history)
+  // may load before the dependency wait: TMA requests every history tile of those
+  // rounds first and the rest after the wait; cp.async (one commit group per round,
+  // empty groups past the end) goes by whole rounds.
   const int hist_end = ctx - ql;  // keys below this were written before this pass
+  if constexpr (TMA) {
+    int issued[kRoundBufs];
 #pragma unroll
-  for (int r = 0; r < kRoundBufs; ++r) {
-    if (r < n_rounds) {
-      if (!waited && key_lo + (r + 1) * kKeySlices * kMmaKeyTile > hist_end) {
-        grid_dep_wait();
-        waited = true;
+    for (int r = 0; r < kRoundBufs; ++r) {
+      issued[r] = 0;
+      if (r >= n_rounds) continue;
+      int s1 = SL;
+      if (!waited) {  // slots whose 32 keys all lie below hist_end
+        const int hist_tiles = hist_end > key_lo ? (hist_end - key_lo) / kMmaKeyTile : 0;
+        s1 = min(max(hist_tiles - r * SL, 0), SL);
       }
-      if constexpr (TMA) tma_round(r);
-      else load_round(r);
+      tma_tiles(r, 0, s1, true);
+      issued[r] = s1;
     }
-    if constexpr (!TMA) asm volatile("cp.async.commit_group;" ::: "memory");
+    if (!waited) {
+      grid_dep_wait();
+      waited = true;
+    }
+#pragma unroll
+    for (int r = 0; r < kRoundBufs; ++r)
+      if (r < n_rounds && issued[r] < SL) tma_tiles(r, issued[r], SL, false);
+  } else {
+#pragma unroll
+    for (int r = 0; r < kRoundBufs; ++r) {
+      if (r < n_rounds) {
+        if (!waited && key_lo + (r + 1) * SL * kMmaKeyTile > hist_end) {
+          grid_dep_wait();
+          waited = true;
+        }
+        load_round(r);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
   }
   if (!waited) grid_dep_wait();  // before q and the remaining rounds
 
@@ -502,10 +538,10 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
       // Zero the V rows of the last partial block past the chunk's keys (pool contents there are
       // not this sequence's keys; P is 0 for them but 0 * NaN would not be).
       const int t_last = (key_hi - 1 - key_lo) / kMmaKeyTile;
-      if (t_last / kKeySlices == r) {
+      if (t_last / SL == r) {
         const int first = key_hi - (key_lo + t_last * kMmaKeyTile);
         if (first < kMmaKeyTile) {
-          uint8_t* vt = smem_attn + (r % kRoundBufs) * ROUND + (t_last % kKeySlices) * 2 * TILE + TILE;
+          uint8_t* vt = smem_attn + (r % kRoundBufs) * ROUND + (t_last % SL) * 2 * TILE + TILE;
           const int per_half = (kMmaKeyTile - first) * 8;  // 16-byte pieces of one 64-dim half
           for (int i = threadIdx.x; i < per_half * (HD / 64); i += NTHR) {
             const int half = i / per_half, rem = i % per_half;
@@ -519,7 +555,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
       asm volatile("cp.async.wait_group %0;" ::"n"(kRoundBufs - 1) : "memory");
       __syncthreads();
     }
-    const int tile = r * kKeySlices + ks;
+    const int tile = r * SL + ks;
     if (active && tile < n_tiles) {
       const uint32_t kbase = sbase + (uint32_t)((r % kRoundBufs) * ROUND + ks * 2 * TILE);
       const uint32_t vbase = kbase + TILE;
@@ -627,9 +663,9 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   // each slice's warp finishes a quarter of the head dims: sum_s acc_s w_s in slice
   // order, divided by L (or kept unnormalised as this chunk's partial).
   float* xs = reinterpret_cast<float*>(smem_attn);                  // [slice][rb][16 rows][XS]
-  float* xml = xs + (size_t)kKeySlices * RB * 16 * XS;              // [slice][rb][16 rows][m, l]
-  float* xw = xml + (size_t)kKeySlices * RB * 16 * 2;               // [rb][16 rows][w_0..w_S-1, M, L]
-  constexpr int WS = kKeySlices + 2;
+  float* xml = xs + (size_t)SL * RB * 16 * XS;              // [slice][rb][16 rows][m, l]
+  float* xw = xml + (size_t)SL * RB * 16 * 2;               // [rb][16 rows][w_0..w_S-1, M, L]
+  constexpr int WS = SL + 2;
   if (active) {
     float* a = xs + (size_t)(ks * RB + rb) * 16 * XS;
 #pragma unroll
@@ -647,30 +683,30 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
   }
   __syncthreads();
   if (active && ks == 0 && lane < 16) {
-    float ms[kKeySlices];
+    float ms[SL];
     float mm = -INFINITY;
 #pragma unroll
-    for (int s2 = 0; s2 < kKeySlices; ++s2) {
+    for (int s2 = 0; s2 < SL; ++s2) {
       ms[s2] = xml[(size_t)(s2 * RB + rb) * 32 + lane * 2];
       mm = fmaxf(mm, ms[s2]);
     }
     float lsum = 0.f;
     float* w = xw + (size_t)(rb * 16 + lane) * WS;
 #pragma unroll
-    for (int s2 = 0; s2 < kKeySlices; ++s2) {
+    for (int s2 = 0; s2 < SL; ++s2) {
       const float ws = ms[s2] == -INFINITY ? 0.f : ex2f(ms[s2] - mm);
       lsum += xml[(size_t)(s2 * RB + rb) * 32 + lane * 2 + 1] * ws;
       w[s2] = ws;
     }
-    w[kKeySlices] = mm;
-    w[kKeySlices + 1] = lsum;
+    w[SL] = mm;
+    w[SL + 1] = lsum;
   }
   __syncthreads();
 
   // This warp's quarter of the head dims: QP float pairs per row, 16 rows.
-  constexpr int QP = HD / kKeySlices / 2;
+  constexpr int QP = HD / SL / 2;
   constexpr int ITEMS = 16 * QP / 32;  // (row, pair) items per lane
-  const int d_base = ks * (HD / kKeySlices);
+  const int d_base = ks * (HD / SL);
   if (p.ws == nullptr) {
     if (!active) return;
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
@@ -683,12 +719,12 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
       const float* w = xw + (size_t)(rb * 16 + r) * WS;
       float o0 = 0.f, o1 = 0.f;
 #pragma unroll
-      for (int s2 = 0; s2 < kKeySlices; ++s2) {
+      for (int s2 = 0; s2 < SL; ++s2) {
         const float2 x = *reinterpret_cast<const float2*>(xs + (size_t)((s2 * RB + rb) * 16 + r) * XS + d);
         o0 += x.x * w[s2];
         o1 += x.y * w[s2];
       }
-      const float l = w[kKeySlices + 1];
+      const float l = w[SL + 1];
       __nv_bfloat16* o = out + ((size_t)(qoff + t0 + rr / p.group) * p.nq + h * p.group + rr % p.group) * HD + d;
       *reinterpret_cast<uint32_t*>(o) = pack_bf16(o0 / l, o1 / l);
     }
@@ -704,7 +740,7 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
         const float* w = xw + (size_t)(rb * 16 + r) * WS;
         float o0 = 0.f, o1 = 0.f;
 #pragma unroll
-        for (int s2 = 0; s2 < kKeySlices; ++s2) {
+        for (int s2 = 0; s2 < SL; ++s2) {
           const float2 x = *reinterpret_cast<const float2*>(xs + (size_t)((s2 * RB + rb) * 16 + r) * XS + d);
           o0 += x.x * w[s2];
           o1 += x.y * w[s2];
@@ -712,8 +748,8 @@ paged_attn_mma_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_co
         float* pr = part + (size_t)rr * (HD + 2);
         *reinterpret_cast<float2*>(pr + d) = make_float2(o0, o1);
         if (ks == 0 && (item % QP) == 0) {
-          pr[HD] = w[kKeySlices];
-          pr[HD + 1] = w[kKeySlices + 1];
+          pr[HD] = w[SL];
+          pr[HD + 1] = w[SL + 1];
         }
       }
     }
@@ -755,11 +791,12 @@ attn_combine_kernel(AttnParams p) {
 
 template <int HD, int BS, int RB, bool TMA>
 void launch_mma(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid, cudaStream_t stream) {
-  // round buffers (K + V of kKeySlices tiles, twice), then the chunk's block table
+  // round buffers (K + V of SL tiles, twice), then the chunk's block table
   // (<= kChunk entries) and the round barriers; the slice merge reuses the round buffers.
-  constexpr size_t kRounds = (size_t)kRoundBufs * kKeySlices * 2 * kMmaKeyTile * (TMA ? HD * 2 : HD * 2 + 16);
-  constexpr size_t kMerge = (size_t)kKeySlices * RB * 16 * (HD + 8 + 2) * sizeof(float) +
-                            (size_t)RB * 16 * (kKeySlices + 2) * sizeof(float);
+  constexpr int SL = key_slices(HD);
+  constexpr size_t kRounds = (size_t)kRoundBufs * SL * 2 * kMmaKeyTile * (TMA ? HD * 2 : HD * 2 + 16);
+  constexpr size_t kMerge = (size_t)SL * RB * 16 * (HD + 8 + 2) * sizeof(float) +
+                            (size_t)RB * 16 * (SL + 2) * sizeof(float);
   constexpr size_t kArea = kRounds > kMerge ? kRounds : kMerge;
   constexpr size_t smem = kArea + kChunk * sizeof(int) + kRoundBufs * sizeof(uint64_t) + (TMA ? 1024 : 0);
   static std::once_flag once;
@@ -767,13 +804,14 @@ void launch_mma(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& m
     cudaFuncSetAttribute(paged_attn_mma_kernel<HD, BS, RB, TMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
   });
-  launch_kernel(paged_attn_mma_kernel<HD, BS, RB, TMA>, grid, dim3(RB * kKeySlices * 32), smem, stream, mk, mv, p);
+  launch_kernel(paged_attn_mma_kernel<HD, BS, RB, TMA>, grid, dim3(RB * SL * 32), smem, stream, mk, mv, p);
 }
 
 template <int HD, int BS, bool TMA>
 void launch_mma_rb(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, dim3 grid,
                    cudaStream_t stream) {
   if (p.rb == 1) launch_mma<HD, BS, 1, TMA>(p, mk, mv, grid, stream);
+  else if constexpr (max_row_blocks(HD) == 2) launch_mma<HD, BS, 2, TMA>(p, mk, mv, grid, stream);
   else if (p.rb == 2) launch_mma<HD, BS, 2, TMA>(p, mk, mv, grid, stream);
   else if (p.rb == 3) launch_mma<HD, BS, 3, TMA>(p, mk, mv, grid, stream);
   else launch_mma<HD, BS, 4, TMA>(p, mk, mv, grid, stream);
@@ -831,12 +869,14 @@ int launch(AttnParams& p, int batch, cudaStream_t stream) {
 int qtile_tokens(int group) { return group >= kMaxRows ? 1 : kMaxRows / group; }
 
 // bf16 kernel: row blocks of 16 query rows per CTA, from the largest query tile
-// (rows = tokens x group) of the call; a query tile holds 16 * rb / group tokens.
-int row_blocks(int max_q_len, int group) {
+// (rows = tokens x group) of the call, at most max_row_blocks(head_dim); a query
+// tile holds 16 * rb / group tokens.
+int row_blocks(int max_q_len, int group, int hd) {
   const long long rows = (long long)max_q_len * group;
-  return rows <= 16 ? 1 : rows <= 32 ? 2 : rows <= 48 ? 3 : 4;
+  const int rb = rows <= 16 ? 1 : rows <= 32 ? 2 : rows <= 48 ? 3 : 4;
+  return rb < max_row_blocks(hd) ? rb : max_row_blocks(hd);
 }
-int mma_qtile_tokens(int max_q_len, int group) { return row_blocks(max_q_len, group) * 16 / group; }
+int mma_qtile_tokens(int max_q_len, int group, int hd) { return row_blocks(max_q_len, group, hd) * 16 / group; }
 
 // Split-mode workspace: kCounterSlots int32 chunk counters at offset 0 (always the
 // same addresses, so no call's partials ever land on them), then the fp32
@@ -859,7 +899,8 @@ extern "C" size_t kve_paged_attn_workspace_bytes(int batch, int max_q_len, int m
   int group = num_heads / num_kv_heads;
   if (group < 1 || group > kMaxRows) return 0;
   // The bf16 kernel's query tiles are never larger than the fp32 kernel's: size for them.
-  int qt = mma_qtile_tokens(max_q_len, group);
+  int qt = mma_qtile_tokens(max_q_len, group, head_dim);
+  if (qt < 1) qt = 1;
   size_t n_qtiles = (max_q_len + qt - 1) / qt;
   size_t n_chunks = (max_ctx + kChunk - 1) / kChunk;
   return kCounterBytes + partials_bytes(batch, num_kv_heads, n_qtiles, n_chunks, head_dim);
@@ -879,6 +920,9 @@ int kve::paged_attn_run(const void* q, int dtype, const void* pool_k, const void
     return set_error(KVE_ERR_SHAPE, "kve_paged_verify_attn: head_dim %d (supported: 64, 128)", head_dim);
   int group = num_heads / num_kv_heads;
   if (group > kMaxRows) return set_error(KVE_ERR_SHAPE, "kve_paged_verify_attn: group %d > %d", group, kMaxRows);
+  if (dtype == KVE_BF16 && group > 16 * max_row_blocks(head_dim))
+    return set_error(KVE_ERR_SHAPE, "kve_paged_verify_attn: bf16 group %d > %d at head_dim %d", group,
+                     16 * max_row_blocks(head_dim), head_dim);
   if (!q || !pool_k || !pool_v || !block_tables || !ctx_lens || !q_lens || !q_offsets || !out)
     return set_error(KVE_ERR_ARG, "kve_paged_verify_attn: null pointer");
   if ((uintptr_t)pool_k % 16 || (uintptr_t)pool_v % 16)
@@ -887,8 +931,8 @@ int kve::paged_attn_run(const void* q, int dtype, const void* pool_k, const void
   p.q = q; p.pool_k = pool_k; p.pool_v = pool_v; p.tables = block_tables; p.table_stride = table_stride;
   p.ctx_lens = ctx_lens; p.q_lens = q_lens; p.q_offsets = q_offsets;
   p.nq = num_heads; p.nkv = num_kv_heads; p.group = group;
-  p.rb = row_blocks(max_q_len, group);
-  p.qt = dtype == KVE_BF16 ? mma_qtile_tokens(max_q_len, group) : qtile_tokens(group);
+  p.rb = row_blocks(max_q_len, group, head_dim);
+  p.qt = dtype == KVE_BF16 ? mma_qtile_tokens(max_q_len, group, head_dim) : qtile_tokens(group);
   p.bs = block_size; p.num_blocks = num_blocks; p.scale = scale; p.out = out; p.status = dev_status;
   p.hist_static = hist_static ? 1 : 0;
   p.n_qtiles = (max_q_len + p.qt - 1) / p.qt;

@@ -133,6 +133,25 @@ class ForwardPlan:
                     np.asarray(n_out, dtype=np.int64), tables, np.asarray(n_blocks, dtype=np.int64))
         return plan
 
+    @classmethod
+    def device_built(cls, n_seqs: int, rows: int, width: int, max_ctx: int, block_size: int) -> "ForwardPlan":
+        """The shape of a plan whose arrays a kernel writes on the device (no host
+        copy): `rows` rows per sequence, the last one's logits wanted, tables of
+        `width` blocks, contexts up to `max_ctx`. Same packed layout as _build."""
+        plan = cls(None, block_size)
+        S, M = n_seqs, rows * n_seqs
+        plan.host = None
+        plan.n_seqs, plan.n_tokens, plan.n_out = S, M, S
+        plan.max_q_len, plan.max_ctx, plan.width = rows, max_ctx, width
+        plan.offsets = {}
+        off = 0
+        for name, n in (("positions", M), ("slots", M), ("q_lens", S), ("q_offsets", S + 1), ("ctx_lens", S),
+                        ("out_rows", S), ("tables", S * width)):
+            plan.offsets[name] = (off, n)
+            off += n
+        plan.size = off
+        return plan
+
     def _build(self, start, q, n_out, tables, nblk):
         S = q.shape[0]
         bs = self.block_size

@@ -205,3 +205,31 @@ def gemm(x, w, epilogue: int = L.EPI_STORE, bias=None, residual=None, out=None, 
                             out.data_ptr(), L.dtype_code(out_dtype), L.ptr(ws), 0 if ws is None else ws.numel(),
                             L.ptr(status), algo, L.stream_handle(x.device)))
     return out
+
+
+def spec_next_draft_plan(start_lens: torch.Tensor, last_tokens: torch.Tensor, n_blocks: torch.Tensor,
+                         tables: torch.Tensor, block_size: int, k: int, rows: int, dump_block: int,
+                         n_accepted: torch.Tensor, emitted: torch.Tensor, plan_out: torch.Tensor,
+                         ids_out: torch.Tensor, verify_ids_out: torch.Tensor, status: torch.Tensor | None = None):
+    """The next step's first draft pass planned on the device (kve_spec_next_draft_plan).
+    start_lens, last_tokens, n_blocks [S], tables [S, width], n_accepted [S],
+    emitted [S, k+1] (contiguous int32); writes plan_out (the packed ForwardPlan
+    layout of `ForwardPlan.device_built(S, rows, width, ...)`), ids_out [rows * S]
+    and verify_ids_out[s * (k+1)]."""
+    lib = L.load()
+    S = start_lens.numel()
+    tensors = (start_lens, last_tokens, n_blocks, tables, n_accepted, emitted, plan_out, ids_out, verify_ids_out)
+    L.require_cuda(*tensors)
+    for t in tensors:
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError("spec_next_draft_plan takes contiguous int32 tensors")
+    width = tables.numel() // max(S, 1)
+    if tables.numel() != S * width or n_blocks.numel() != S or n_accepted.numel() < S or \
+            emitted.numel() < S * (k + 1) or ids_out.numel() < rows * S or verify_ids_out.numel() < S * (k + 1) or \
+            plan_out.numel() < 2 * rows * S + 4 * S + 1 + S * width:
+        raise ValueError("spec_next_draft_plan: buffer sizes do not match")
+    L.check(lib.kve_spec_next_draft_plan(start_lens.data_ptr(), last_tokens.data_ptr(), n_blocks.data_ptr(),
+                                         tables.data_ptr(), S, width, block_size, k, rows, dump_block,
+                                         n_accepted.data_ptr(), emitted.data_ptr(), plan_out.data_ptr(),
+                                         ids_out.data_ptr(), verify_ids_out.data_ptr(), L.ptr(status),
+                                         L.stream_handle(start_lens.device)))

@@ -112,7 +112,7 @@ class SpecEngine:
     """Batched draft/verify/accept loop over one target and one draft model."""
 
     def __init__(self, target, draft, target_pool, draft_pool, k: int, graphs: bool = True,
-                 eager_layers: int | None = None):
+                 eager_layers: int | None = None, speculate: bool = True):
         assert k >= 1, "k must be at least 1"
         self.target = as_model(target)
         self.draft = as_model(draft)
@@ -142,6 +142,18 @@ class SpecEngine:
         # `eager_layers` overrides it: 0 records the whole pass, num_layers launches it all.
         n_layers = self.draft.cfg.num_layers
         self.eager0 = max(1, n_layers // 4) if eager_layers is None else min(max(int(eager_layers), 0), n_layers)
+        # Speculative planning of the next step's first draft pass: after the accept
+        # kernel the engine queues a device-side plan (kve_spec_next_draft_plan) and that
+        # pass, so the GPU runs it while the host reads the accept result back and does
+        # its bookkeeping. One row per sequence (exact unless a sequence accepted all k
+        # drafts) while the previous step saw no full acceptance, two rows (exact for
+        # every outcome) otherwise. The next step uses the pass if its request list is
+        # the one planned for and every request's draft feed matches; else it is
+        # discarded (its K/V writes land only past each draft's committed prefix).
+        self.speculate = speculate
+        self._spec = None
+        self._saw_full_accept = False
+        self.spec_stats = {"planned": 0, "used": 0, "discarded": 0}
 
     def _ensure(self, S: int):
         if S <= self._cap:
@@ -157,6 +169,14 @@ class SpecEngine:
         self.accepted = torch.empty(S * (k + 2), dtype=torch.int32, device=dev)
         self.accepted_host = torch.empty(S * (k + 2), dtype=torch.int32, pin_memory=True)
         self.accepted_ready = torch.cuda.Event()
+        # speculated first draft pass: its token ids (up to 2 rows per sequence), the
+        # next verify feed (bonus + k drafts per sequence) and where draft j goes in it
+        self.spec_ids = torch.empty(2 * S, dtype=torch.int32, device=dev)
+        self.spec_vids = torch.zeros(S * (k + 1), dtype=torch.int32, device=dev)
+        self.spec_dst = (torch.arange(S, dtype=torch.int32)[None, :] * (k + 1) + 1
+                         + torch.arange(k, dtype=torch.int32)[:, None]).to(dev).contiguous()
+        self.spec_plans = [torch.empty(0, dtype=torch.int32, device=dev) for _ in range(2)]
+        self._spec_flip = 0
 
     def _upload(self, slot: int, arrays: list[np.ndarray]) -> list[torch.Tensor]:
         """Copy int32 host arrays to the device in one transfer through pinned
@@ -188,6 +208,7 @@ class SpecEngine:
     def _step(self, reqs: list[_Request], eos: set[int]) -> None:
         k, S = self.k, len(reqs)
         self._ensure(S)
+        spec, self._spec = self._spec, None
         # --- block reservation, in the reference's order: draft feeds, then the verify feed.
         lens = []
         for r in reqs:
@@ -203,25 +224,38 @@ class SpecEngine:
         # One draft block table serves all k draft passes of the step (every slot they
         # write was reserved above).
         t_d, nb_d = block_tables([r.d_seq for r in reqs])
-        plan0 = ForwardPlan.from_arrays(d_len, u_d, ones, t_d, nb_d, bs_d)
-        # --- upload 1: the first draft pass's plan and ids, and the verify pass's token
-        # ids with a slot per draft (the draft argmax kernels write the drafts there),
-        # so the GPU starts while the host builds the other plans (the later uploads
-        # queue behind that pass).
-        d_ids = np.fromiter(chain.from_iterable(r.tokens[len(r.tokens) - r.u_d:] for r in reqs), dtype=np.int32,
-                            count=int(u_d.sum()))
-        v_len = u_t + k
-        v_ids, dst = verify_feed([r.tokens for r in reqs], u_t, k)
-        (plan0_dev, d_ids_dev, v_ids_dev, dst_dev) = self._upload(0, [plan0.host, d_ids, v_ids, dst.reshape(-1)])
-        dst_dev = dst_dev.view(k, S)
+        # The first draft pass was queued by the previous step (planned on the device)
+        # when it fed what this step's feed is: the same requests, every target feed the
+        # bonus alone and every draft feed covered by the planned rows.
+        use_spec = spec is not None and len(spec["reqs"]) == S and all(a is b for a, b in zip(spec["reqs"], reqs)) \
+            and bool((u_t == 1).all()) and bool((u_d <= spec["rows"]).all()) and bool((n_tok - 1 < spec["cover"]).all())
+        if spec is not None:
+            self.spec_stats["used" if use_spec else "discarded"] += 1
         status = self.tr.status
-        # --- draft: k passes, argmax feeding the next pass on the device
-        # Pass 0: the first draft layers as stream launches (the GPU is idle until they
-        # arrive), the rest recorded into a graph while those run.
-        self.dr.forward(plan0, d_ids_dev, self.dlog[:S], plan_dev=plan0_dev,
-                        graph="draft0" if self.graphs else None, eager_layers=self.eager0)
-        ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S], scatter_index=dst_dev[0], scatter_out=v_ids_dev,
-                        status=status)
+        if use_spec:
+            plan0 = spec["plan"]
+            v_ids_dev = self.spec_vids[: S * (k + 1)]
+            dst_dev = self.spec_dst[:, :S]
+        else:
+            plan0 = ForwardPlan.from_arrays(d_len, u_d, ones, t_d, nb_d, bs_d)
+            # --- upload 1: the first draft pass's plan and ids, and the verify pass's token
+            # ids with a slot per draft (the draft argmax kernels write the drafts there),
+            # so the GPU starts while the host builds the other plans (the later uploads
+            # queue behind that pass).
+            d_ids = np.fromiter(chain.from_iterable(r.tokens[len(r.tokens) - r.u_d:] for r in reqs),
+                                dtype=np.int32, count=int(u_d.sum()))
+            v_ids, dst = verify_feed([r.tokens for r in reqs], u_t, k)
+            (plan0_dev, d_ids_dev, v_ids_dev, dst_dev) = self._upload(0, [plan0.host, d_ids, v_ids,
+                                                                           dst.reshape(-1)])
+            dst_dev = dst_dev.view(k, S)
+            # --- draft: k passes, argmax feeding the next pass on the device
+            # Pass 0: the first draft layers as stream launches (the GPU is idle until they
+            # arrive), the rest recorded into a graph while those run.
+            self.dr.forward(plan0, d_ids_dev, self.dlog[:S], plan_dev=plan0_dev,
+                            graph="draft0" if self.graphs else None, eager_layers=self.eager0)
+            ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S], scatter_index=dst_dev[0], scatter_out=v_ids_dev,
+                            status=status)
+        v_len = u_t + k
         # The target reservations follow the draft ones with no allocator call in
         # between, as in the reference's order, while the first draft pass runs.
         for r in reqs:
@@ -240,8 +274,17 @@ class SpecEngine:
             plans.append(ForwardPlan.from_arrays(d_len + u_d + j - 1, ones, ones, t_d, nb_d, bs_d))
         t_t, nb_t = block_tables([r.t_seq for r in reqs])
         vplan = ForwardPlan.from_arrays(t_len, v_len, np.full(S, k + 1, dtype=np.int64), t_t, nb_t, bs_t)
-        views = self._upload(2, [p.host for p in plans[2:]] + [vplan.host])
-        vplan_dev = views[-1]
+        # What the device needs to plan the next step's first draft pass: each request's
+        # token count and last token at the start of this step, and its draft blocks (the
+        # table two entries wider: a planned row may land up to two positions past them).
+        last_tok = np.fromiter((r.tokens[-1] for r in reqs), dtype=np.int32, count=S)
+        t_d2 = np.zeros((S, t_d.shape[1] + 2), dtype=np.int32)
+        t_d2[:, : t_d.shape[1]] = t_d
+        views = self._upload(2, [p.host for p in plans[2:]] + [vplan.host, n_tok.astype(np.int32), last_tok,
+                                                               nb_d.astype(np.int32), t_d2.reshape(-1)])
+        nv = len(plans) - 2 if k > 1 else 0
+        vplan_dev = views[nv]
+        spec_src = views[nv + 1:]
         for j in range(2, k):
             self.dr.forward(plans[j], self.drafts[j - 1, :S], self.dlog[:S], plan_dev=views[j - 2], graph=gd)
             ops.argmax_rows(self.dlog[:S], out=self.drafts[j, :S], scatter_index=dst_dev[j],
@@ -264,10 +307,13 @@ class SpecEngine:
         back_t = self.accepted_host[:ne + S]
         back_t.copy_(self.accepted[:ne + S], non_blocking=True)
         self.accepted_ready.record()
+        if self.speculate:
+            self._queue_next_draft_pass(reqs, n_tok, nb_d, t_d2.shape[1], spec_src, ne)
         self.accepted_ready.synchronize()
         back = back_t.numpy()
         n_host = back[ne:].tolist()
         em_host = back[:ne].reshape(S, k + 1).tolist()
+        self._saw_full_accept = k in n_host
         self.stats["d2h_bytes"] += back.nbytes
         self.stats["iterations"] += 1
         self.stats["verify_rows"] += vplan.n_tokens
@@ -295,6 +341,40 @@ class SpecEngine:
                 r.done = True
             elif len(res.new_token_ids) >= r.max_new:
                 r.done = True
+
+    def _queue_next_draft_pass(self, reqs, n_tok, nb_d, width, spec_src, ne) -> None:
+        """Plan the next step's first draft pass on the device from this step's accept
+        result and queue it (with its argmax) behind the accept readback. Skipped when
+        a request is expected to finish (the next step's request list would differ)
+        or the draft pool has no unused block for rows past a sequence's blocks."""
+        k, S = self.k, len(reqs)
+        rows = 2 if self._saw_full_accept else 1
+        # A request expected to finish this step (it emits its previous step's accepted
+        # count + 1 tokens, 1 on its first step) would change the next request list.
+        if any(len(r.res.new_token_ids) + 1 + (r.res.accepted_per_iter[-1] if r.res.accepted_per_iter else 0)
+               >= r.max_new for r in reqs):
+            return
+        dump = self.d_pool.manager.unused_block()
+        if dump is None:
+            return
+        bs = self.d_pool.block_size
+        desc = ForwardPlan.device_built(S, rows, width, int(n_tok.max()) + k + 1, bs)
+        self._spec_flip ^= 1
+        buf = self.spec_plans[self._spec_flip]
+        if buf.numel() < desc.size:
+            buf = self.spec_plans[self._spec_flip] = torch.empty(int(desc.size * 1.5) + 256, dtype=torch.int32,
+                                                                 device=self.device)
+        start, last, nblk, tables = spec_src
+        ops.spec_next_draft_plan(start, last, nblk, tables, bs, k, rows, dump, self.accepted[ne:ne + S],
+                                 self.accepted[:ne], buf, self.spec_ids, self.spec_vids[: S * (k + 1)],
+                                 status=self.tr.status)
+        self.dr.forward(desc, self.spec_ids[: rows * S], self.dlog[:S], plan_dev=buf,
+                        graph="draft_spec" if self.graphs else None)
+        ops.argmax_rows(self.dlog[:S], out=self.drafts[0, :S], scatter_index=self.spec_dst[0, :S],
+                        scatter_out=self.spec_vids[: S * (k + 1)], status=self.tr.status)
+        # the next step's last row must lie in the blocks this plan used
+        self._spec = {"reqs": list(reqs), "rows": rows, "plan": desc, "cover": nb_d * bs}
+        self.spec_stats["planned"] += 1
 
     def check(self) -> None:
         self.tr.check_status()

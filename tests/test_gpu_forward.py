@@ -232,3 +232,97 @@ def test_layer_ranges_and_graphs_compose_bit_identically(cuda_device, dtype):
         assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2]), e
     assert runner.graph_fallbacks == []
     runner.check_status()
+
+
+def test_spec_next_draft_plan_matches_host_plan(cuda_device):
+    """kve_spec_next_draft_plan writes, on the device, the plan the host builds for
+    the next step's first draft pass (ForwardPlan.from_arrays over the same tables):
+    one row (position T0 + n, bonus token) or two rows (T0 + n - 1 with the token
+    there, then the bonus) per sequence, for every accepted count n in 0..k; rows
+    past a sequence's blocks read and write the dump block."""
+    import numpy as np
+
+    from kvengine_b200 import ops
+    from kvengine_b200.model import ForwardPlan
+
+    rng = np.random.default_rng(5)
+    S, k, bs, dump = 13, 4, 16, 4095
+    start = rng.integers(1, 300, S)
+    start[:3] = [16 - k + 1, 32 - k, 48 - k - 1]          # rows landing at a block boundary
+    nb = (start + k - 2) // bs + 1                         # the draft's reservation: up to T0 + k - 2
+    width = int(nb.max()) + 2
+    ids = rng.permutation(4000)[: int(nb.sum())]
+    tables = np.zeros((S, width), dtype=np.int64)
+    tables[np.arange(width) < nb[:, None]] = ids
+    n_acc = np.concatenate([[k - 1, k, k - 1, 0, k], rng.integers(0, k + 1, S - 5)])
+    emitted = np.full((S, k + 1), -1, dtype=np.int64)
+    for s in range(S):
+        emitted[s, : n_acc[s] + 1] = rng.integers(0, 151936, n_acc[s] + 1)
+    last = rng.integers(0, 151936, S)
+
+    def dev(a):
+        return torch.tensor(np.ascontiguousarray(a), dtype=torch.int32, device=cuda_device).reshape(-1)
+
+    full = np.where(np.arange(width) < nb[:, None], tables, dump)   # the table the plan uses
+    for rows in (1, 2):
+        desc = ForwardPlan.device_built(S, rows, width, int(start.max()) + k + 1, bs)
+        plan = torch.full((desc.size + 8,), -99, dtype=torch.int32, device=cuda_device)
+        out_ids = torch.full((2 * S,), -99, dtype=torch.int32, device=cuda_device)
+        vids = torch.full((S * (k + 1),), -99, dtype=torch.int32, device=cuda_device)
+        status = ops.status_tensor(cuda_device)
+        ops.spec_next_draft_plan(dev(start), dev(last), dev(nb), dev(tables), bs, k, rows, dump, dev(n_acc),
+                                 dev(emitted), plan, out_ids, vids, status=status)
+        ops.check_status(status)
+        if rows == 1:
+            first = start + np.minimum(n_acc, k - 1)
+            want_ids = emitted[np.arange(S), n_acc]
+        else:
+            first = start + n_acc - 1
+            prev = np.where(n_acc > 0, emitted[np.arange(S), np.maximum(n_acc - 1, 0)], last)
+            want_ids = np.stack([prev, emitted[np.arange(S), n_acc]], 1).reshape(-1)
+        host = ForwardPlan.from_arrays(first, np.full(S, rows), np.ones(S, dtype=np.int64), full,
+                                       np.full(S, width), bs)
+        assert host.offsets == desc.offsets and host.n_tokens == desc.n_tokens and host.width == desc.width
+        assert plan[: desc.size].cpu().numpy().tolist() == host.host.tolist(), rows
+        assert plan[desc.size:].cpu().tolist() == [-99] * 8
+        assert out_ids[: rows * S].cpu().numpy().tolist() == want_ids.tolist()
+        v = vids.view(S, k + 1).cpu().numpy()
+        assert v[:, 0].tolist() == emitted[np.arange(S), n_acc].tolist()
+        assert (v[:, 1:] == -99).all()
+        # rows past a sequence's blocks (set up at the block boundaries above) hit the dump block
+        pos_last = first + rows - 1
+        slots = plan[desc.offsets["slots"][0]: desc.offsets["slots"][0] + rows * S].cpu().numpy()
+        hit = pos_last >= nb * bs
+        assert hit[0] and (rows == 1 or hit[1])
+        assert ((slots.reshape(S, rows)[:, -1] // bs == dump) == hit).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_speculated_first_draft_pass_changes_no_token(cuda_device, tiny_state_dicts, dtype):
+    """The first draft pass of each step queued before the accept readback (planned
+    on the device) gives exactly the tokens, acceptances and final free lists of the
+    host-planned pass: with a hostile draft (one-row plans, used) and a self draft
+    (two-row plans after the first full acceptance), ragged prompts and budgets
+    (the request list shrinks, so some queued passes are discarded)."""
+    from kvengine_b200 import SpecEngine
+
+    cfg, m, hostile = _models(tiny_state_dicts, "tiny", dtype, cuda_device)
+    g = torch.Generator().manual_seed(17)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (5, 23, 40, 9, 17, 31)]
+    ragged = [20, 13, 26, 31, 8, 24]
+    for draft, k, budgets in ((hostile, 4, ragged), (hostile, 1, ragged), (m, 3, ragged), (m, 3, [40] * 6),
+                              (m, 4, [33] * 6)):
+        outs = []
+        for spec in (False, True):
+            tp = PagedKVCache.for_model(m, num_blocks=256, block_size=16)
+            dp = PagedKVCache.for_model(m, num_blocks=256, block_size=16)
+            eng = SpecEngine(m, draft, tp, dp, k, speculate=spec)
+            res, _ = speculative_greedy_batch(m, draft, prompts, tp, dp, k=k, max_new_tokens=budgets,
+                                              eos_token_id=None, engine=eng)
+            eng.check()
+            outs.append(([r.new_token_ids for r in res], [r.accepted_per_iter for r in res],
+                         list(tp.manager._stack), list(dp.manager._stack)))
+            if spec and (draft is hostile or budgets != ragged):
+                assert eng.spec_stats["used"] > 0, (k, eng.spec_stats)
+            assert tp.manager.num_allocated == 0 and dp.manager.num_allocated == 0
+        assert outs[0] == outs[1], (k, draft is m)

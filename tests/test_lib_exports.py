@@ -42,8 +42,10 @@ def test_workspace_queries_without_gpu():
     # split-K partials live in the cluster's shared memory: no GEMM workspace
     assert lib.kve_gemm_workspace_bytes(320, 2560, 2048, L.KVE_BF16) == 0
     # contexts past one 512-key chunk split across CTAs: 64 KiB of chunk counters + fp32 partials
-    # (64 rows x (hd + 2) floats per sequence, kv head, query tile and chunk)
-    assert lib.kve_paged_attn_workspace_bytes(64, 5, 4096, 14, 2, 64) == 65536 + 64 * 2 * 1 * 8 * 64 * 66 * 4
+    # (64 rows x (hd + 2) floats per sequence, kv head, query tile and chunk); at head_dim 64 a
+    # query tile holds two 16-row blocks, 4 of the 5 tokens of a 7-head group: 2 query tiles
+    assert lib.kve_paged_attn_workspace_bytes(64, 5, 4096, 14, 2, 64) == 65536 + 64 * 2 * 2 * 8 * 64 * 66 * 4
+    assert lib.kve_paged_attn_workspace_bytes(64, 5, 4096, 16, 2, 128) == 65536 + 64 * 2 * 1 * 8 * 64 * 130 * 4
     assert lib.kve_paged_attn_workspace_bytes(64, 5, 512, 14, 2, 64) == 0
 
 

@@ -48,3 +48,23 @@ def test_verify_feed_layout():
             want.extend([0] * k)
         assert ids.tolist() == want
         assert dst.shape == (k, len(toks)) and dst.T.tolist() == slots
+
+
+def test_device_built_plan_layout_equals_host_layout():
+    """The packed layout a device-side planner writes (ForwardPlan.device_built) is
+    the one the host builder gives a pass of `rows` rows per sequence with the last
+    row's logits wanted: same offsets, sizes and shape fields."""
+    rng = random.Random(11)
+    for rows in (1, 2):
+        for _ in range(20):
+            S, bs = rng.randint(1, 70), rng.choice([1, 3, 16])
+            start = np.array([rng.randint(rows, 400) for _ in range(S)]) - (rows - 1)
+            nb = (start + rows + bs - 1) // bs + np.array([rng.randint(0, 2) for _ in range(S)])
+            width = int(nb.max())
+            tables = np.zeros((S, width), dtype=np.int64)
+            tables[np.arange(width) < nb[:, None]] = [rng.randrange(9000) for _ in range(int(nb.sum()))]
+            host = ForwardPlan.from_arrays(start, np.full(S, rows), np.ones(S, dtype=np.int64), tables, nb, bs)
+            dev = ForwardPlan.device_built(S, rows, width, host.max_ctx, bs)
+            assert dev.offsets == host.offsets and dev.size == host.host.shape[0]
+            assert (dev.n_seqs, dev.n_tokens, dev.n_out, dev.max_q_len, dev.max_ctx, dev.width) == \
+                (host.n_seqs, host.n_tokens, host.n_out, host.max_q_len, host.max_ctx, host.width)
