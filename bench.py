@@ -176,6 +176,7 @@ def run_gpu(args):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = lib.kve_launch_count()
     stats0 = dict(eng.stats)
+    spec0 = dict(eng.spec_stats)
     collected = []
     ev0.record()
     tokens = 0
@@ -201,6 +202,7 @@ def run_gpu(args):
     accepted = sum(r.res.tokens_accepted for reqs in collected for r in reqs)
     drafted = sum(r.res.tokens_drafted for reqs in collected for r in reqs)
     iters = eng.stats["iterations"] - stats0["iterations"]
+    spec_first = {key: eng.spec_stats[key] - spec0[key] for key in spec0}
 
     # ------------------------------------------------------------ roofline
     steady = [(a, b, p) for a, b, p in verify_ev if p.max_q_len == K_SPEC + 1]
@@ -295,6 +297,7 @@ def run_gpu(args):
                        "l2": "inputs larger than L2 (6.2 GB target + 1.0 GB draft weights streamed per pass)"},
             "acceptance_rate": round(accepted / drafted, 4) if drafted else None,
             "iterations_per_step": iters / args.steps,
+            "first_draft_pass_planned_on_device": spec_first,
             "e2e": e2e,
             "gpu_launches": int(launches),
             "roofline": roofline,
