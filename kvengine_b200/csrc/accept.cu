@@ -103,7 +103,7 @@ __device__ __forceinline__ int row_argmax(const T* x, int cols, bool vec_ok) {
 
 template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads)
-accept_kernel(const T* __restrict__ logits, int64_t row_stride, const int32_t* __restrict__ drafts,
+accept_kernel(const T* logits, int64_t row_stride, const int32_t* drafts,
               int64_t dsb, int64_t dsj, int k, int vocab, bool vec_ok, int32_t* __restrict__ preds, int32_t* __restrict__ n_acc,
               int32_t* __restrict__ emitted, int32_t* __restrict__ counters) {
   grid_dep_wait();
@@ -140,8 +140,8 @@ accept_kernel(const T* __restrict__ logits, int64_t row_stride, const int32_t* _
 // into its slot of the verify pass's token ids).
 template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads)
-argmax_kernel(const T* __restrict__ x, int64_t row_stride, int cols, bool vec_ok, int32_t* __restrict__ out,
-              const int32_t* __restrict__ scatter_idx, int32_t* __restrict__ scatter_out, int64_t scatter_len,
+argmax_kernel(const T* x, int64_t row_stride, int cols, bool vec_ok, int32_t* __restrict__ out,
+              const int32_t* scatter_idx, int32_t* __restrict__ scatter_out, int64_t scatter_len,
               int* __restrict__ status) {
   grid_dep_wait();
   grid_dep_launch();

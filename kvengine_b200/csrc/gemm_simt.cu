@@ -18,7 +18,7 @@ constexpr int kThreads = 256;
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-gemm_simt_kernel(const T* __restrict__ x, const T* __restrict__ w, int m, int n, int k, EpiArgs e) {
+gemm_simt_kernel(const T* x, const T* __restrict__ w, int m, int n, int k, EpiArgs e) {
   grid_dep_wait();
   grid_dep_launch();
   __shared__ float xs[BK][BM + 4];

@@ -11,8 +11,8 @@ namespace {
 
 // ---------------------------------------------------------------- append
 // One 16-byte chunk per thread; chunks [0, n*cpr) are K rows, [n*cpr, 2*n*cpr) V rows.
-__global__ void kv_append_kernel(const uint4* __restrict__ k_new, const uint4* __restrict__ v_new,
-                                 const int64_t* __restrict__ slots, int n_tokens, int chunks_per_row,
+__global__ void kv_append_kernel(const uint4* k_new, const uint4* v_new, const int64_t* slots, int n_tokens,
+                                 int chunks_per_row,
                                  uint4* __restrict__ pool_k, uint4* __restrict__ pool_v,
                                  int64_t num_slots, int* status) {
   grid_dep_wait();
@@ -39,9 +39,8 @@ __global__ void kv_append_kernel(const uint4* __restrict__ k_new, const uint4* _
 // qkv GEMM epilogue.
 
 template <typename T>
-__global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int nq, int nkv, int hd,
-                                       const int32_t* __restrict__ positions,
-                                       const int32_t* __restrict__ slots,
+__global__ void qkv_rope_append_kernel(const T* qkv, int nq, int nkv, int hd, const int32_t* positions,
+                                       const int32_t* slots,
                                        const float* __restrict__ rope_cos,
                                        const float* __restrict__ rope_sin, int rope_len,
                                        T* __restrict__ q_out, T* __restrict__ pool_k,
@@ -88,7 +87,7 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, int nq, int nk
 
 // ------------------------------------------------------------- gather
 template <typename T>
-__global__ void gather_kv_kernel(const T* __restrict__ pool, const int32_t* __restrict__ table, int length,
+__global__ void gather_kv_kernel(const T* pool, const int32_t* table, int length,
                                  int nkv, int hd, int bs, int64_t num_blocks, T* __restrict__ out,
                                  int* status) {
   grid_dep_wait();
@@ -108,8 +107,8 @@ __global__ void gather_kv_kernel(const T* __restrict__ pool, const int32_t* __re
 
 // -------------------------------------------------------------- embed
 template <typename T>
-__global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restrict__ table, int hidden,
-                             int vocab, T* __restrict__ out, int* status) {
+__global__ void embed_kernel(const int32_t* ids, const T* __restrict__ table, int hidden, int vocab,
+                             T* __restrict__ out, int* status) {
   grid_dep_wait();
   grid_dep_launch();
   int t = blockIdx.x;
@@ -129,8 +128,10 @@ constexpr int kNormThreads = 256;
 
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads)
-rmsnorm_kernel(const T* __restrict__ x, const float* __restrict__ w, int hidden, float eps,
-               const int32_t* __restrict__ row_index, T* __restrict__ out, int w_static) {
+rmsnorm_kernel(const T* x, const float* __restrict__ w, int hidden, float eps, const int32_t* row_index,
+               T* __restrict__ out, int w_static) {
+  // x and row_index are written by earlier kernels: no __restrict__ on them, so no
+  // load through them can be scheduled above the dependency wait.
   // Thread t owns elements t, t + 256, ...: the first kNormRegs of them stay in
   // registers between the sum of squares and the scaling (one read of x), and the
   // weights for them are read before the dependency wait when they are constant.

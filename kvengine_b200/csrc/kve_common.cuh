@@ -92,6 +92,10 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 // their writes are visible); only inputs declared constant, such as model
 // weights in kve_forward, are read before it. grid_dep_launch() follows it.
 // Both are no-ops for a plain launch.
+// The wait is an inline-asm memory barrier, which the compiler honours only for
+// memory it cannot prove private: a load through a `const T* __restrict__` kernel
+// parameter may be scheduled above it. Inputs that an earlier kernel writes are
+// therefore never declared __restrict__ (constant weights may be).
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

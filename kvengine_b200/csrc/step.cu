@@ -32,10 +32,10 @@ namespace {
 
 // One thread per (sequence, table entry) in a grid-stride loop; entry 0 of a
 // sequence also writes the per-sequence arrays.
-__global__ void spec_next_draft_plan_kernel(const int32_t* __restrict__ start_len, const int32_t* __restrict__ last_tok,
-                                            const int32_t* __restrict__ n_blocks, const int32_t* __restrict__ tables_in,
+__global__ void spec_next_draft_plan_kernel(const int32_t* start_len, const int32_t* last_tok, const int32_t* n_blocks,
+                                            const int32_t* tables_in,
                                             int n_seqs, int width, int bs, int k, int rows, int dump_block,
-                                            const int32_t* __restrict__ n_acc, const int32_t* __restrict__ emitted,
+                                            const int32_t* n_acc, const int32_t* emitted,
                                             int32_t* __restrict__ plan, int32_t* __restrict__ ids,
                                             int32_t* __restrict__ verify_ids, int* status) {
   grid_dep_wait();
