@@ -305,10 +305,16 @@ struct Epi {
           const uint4 pv = *reinterpret_cast<const uint4*>(srow + cp);
           T* y = reinterpret_cast<T*>(&val);
           const T* o = reinterpret_cast<const T*>(&pv);
+          // One branch-free form of both halves: the first half is x1 c - x2 s
+          // (rope_first), the second x2 c + x1 s (rope_second); with `self` the
+          // element and `other` its partner that is round(self c) + round(+-other s),
+          // the same roundings in the same order, without a divergent branch.
+          const float sgn = lo ? -1.f : 1.f;
 #pragma unroll
           for (int e = 0; e < VE; ++e) {
             const float self = (float)y[e], other = (float)o[e];
-            y[e] = cvt(lo ? rope_first<T>(self, other, cv[e], sv[e]) : rope_second<T>(other, self, cv[e], sv[e]));
+            const float cb = Elem<T>::round(cv[e]), sb = Elem<T>::round(sv[e]);
+            y[e] = cvt(__fadd_rn(Elem<T>::round(__fmul_rn(self, cb)), Elem<T>::round(__fmul_rn(sgn * other, sb))));
           }
         }
         T* dst;
