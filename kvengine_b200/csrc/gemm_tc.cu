@@ -376,10 +376,211 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t
                : "memory");
 }
 
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ uint32_t map_to(uint32_t local, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
   return r;
+}
+
+// Split-K over the cluster, general form: each CTA writes its fp32 partial,
+// grouped by the CTA that owns each token (contiguous slices of the round), and
+// sends every peer its group with one bulk shared-memory copy; the owner then sums
+// the S partials of its tokens in rank order from its own shared memory.
+template <int MODE, bool BF, int MH, int BMT>
+__device__ __forceinline__ void splitk_exchange(const TcArgs& a, uint8_t* smem, uint32_t t_lane, bool have, bool epi,
+                                                int egrp, int f_local, int etid, int tok0, int col0, float bias_f,
+                                                const uint4 (&res_first)[Epi<MODE, BF, BMT>::NPASS],
+                                                uint64_t* recv_bar) {
+  using E = Epi<MODE, BF, BMT>;
+  const int S = a.splits;
+  uint8_t* stg = smem + a.stg_off;
+    const uint32_t rank = cluster_rank();
+    const int slm = (a.rch + S - 1) / S;               // max tokens per slice
+    float* pout = reinterpret_cast<float*>(smem);      // [rch][128] this CTA's partial, token-major
+    float* recv = pout + (size_t)a.rch * BM;           // [S][slm][128] received slices, by sender
+    int round = 0;
+    for (int r0 = 0; r0 < a.mt; r0 += a.rch, ++round) {
+      const int ch = min(a.rch, a.mt - r0);
+      // Peers write into this CTA's drained stage buffers: wait until every CTA of
+      // the cluster has finished its main loop (and, in later rounds, its reads).
+      cluster_sync();
+      const int my_lo = (int)((long long)rank * ch / S), my_hi = (int)((long long)(rank + 1) * ch / S);
+      if (epi) {
+        // Both warpgroups drain alternate 32-token chunks; owner u's tokens
+        // [lo_u, hi_u) are contiguous rows of pout.
+        float* prow = pout + f_local;
+        for (int c = egrp * kRows; c < ch; c += kEpiGroups * kRows) {
+          const int n = min(kRows, ch - c);
+          float v[32];
+          tmem_load_cols(t_lane + r0 + c, n, have, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < n) prow[(c + j) * BM] = v[j];
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        epi_bar_all();
+        // Thread u of the first warpgroup sends peer u its slice (one bulk copy each,
+        // issued in parallel: one thread issuing them in turn spent ~0.3 us per copy);
+        // thread `rank` arms this CTA's receive barrier for the S - 1 incoming slices.
+        if (egrp == 0 && etid < S) {
+          const int u = etid;
+          if (u == (int)rank) {
+            mbar_expect_tx(smem_u32(recv_bar), (uint32_t)(S - 1) * (uint32_t)(my_hi - my_lo) * BM * 4);
+          } else {
+            const int lo = (int)((long long)u * ch / S), hi = (int)((long long)(u + 1) * ch / S);
+            if (hi > lo)
+              bulk_copy_to_peer(map_to(smem_u32(recv + (size_t)rank * slm * BM), (uint32_t)u),
+                                smem_u32(pout + (size_t)lo * BM), (uint32_t)(hi - lo) * BM * 4,
+                                map_to(smem_u32(recv_bar), (uint32_t)u));
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        }
+        mbar_wait(smem_u32(recv_bar), (uint32_t)(round & 1), a.status);
+        // Sum the S partials of each owned token in rank order (own slice from
+        // pout), 32-token chunks alternating between the warpgroups when both
+        // groups' double-buffered staging fits (16-bit outputs).
+        constexpr int kStgBufC = kRows * E::W * E::ES;
+        constexpr int kSumGroups = 2 * kEpiGroups * kStgBufC <= kStageBytes ? kEpiGroups : 1;
+        const float* src[kMaxSplits];
+#pragma unroll
+        for (int u = 0; u < kMaxSplits; ++u)
+          src[u] = (u == (int)rank ? pout + (size_t)my_lo * BM : recv + (size_t)u * slm * BM) + f_local;
+        const int mine = my_hi - my_lo;
+        int it = 0;
+        for (int t0 = egrp * kRows; egrp < kSumGroups && t0 < mine; t0 += kSumGroups * kRows, ++it) {
+          const int n = min(kRows, mine - t0);
+          uint8_t* buf = stg + (egrp * 2 + (it & 1)) * kStgBufC;
+          uint4 res[E::NPASS];
+          if (round == 0 && it == 0) {
+#pragma unroll
+            for (int i = 0; i < E::NPASS; ++i) res[i] = res_first[i];
+          } else {
+            E::load_res(a, tok0 + r0 + my_lo + t0, n, col0, etid, res);
+          }
+          for (int j0 = 0; j0 < n; j0 += 4) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int u = 0; u < kMaxSplits; ++u) {
+              if (u < S) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  if (j0 + q < n) acc[q] += src[u][(t0 + j0 + q) * BM];
+              }
+            }
+            E::template stage<4>(buf, j0, n, f_local, acc, bias_f);
+          }
+          epi_bar(egrp);
+          E::copy_out(a, buf, tok0 + r0 + my_lo + t0, n, col0, etid, res);
+        }
+        if (egrp == 0 && etid < S && etid != (int)rank) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        epi_bar_all();
+      }
+    }
+  }
+
+// Split-K over the cluster for 16-bit RESIDUAL / STORE tiles whose partials fit
+// the drained stage area in one round: every CTA drains its fp32 partial to its
+// own shared memory and, after a cluster barrier, the owner of each token reads
+// the S partials of that token straight from the peers' shared memory (16-byte
+// distributed loads, all issued before the sums) and sums them in rank order -
+// the same additions, in the same order, as splitk_exchange, without the bulk
+// copies, receive buffers and staging. A third barrier keeps every partial alive
+// until its readers are done.
+__device__ __forceinline__ void splitk_direct(const TcArgs& a, uint8_t* smem, uint32_t t_lane, bool have, bool epi,
+                                              int egrp, int f_local, int tok0, int col0) {
+  using T = __nv_bfloat16;
+  constexpr int B = 4;  // tokens per thread per batch
+  const int S = a.splits;
+  const uint32_t rank = cluster_rank();
+  float* pout = reinterpret_cast<float*>(smem);  // [mt][128] this CTA's partial, token-major
+  const int my_lo = (int)((long long)rank * a.mt / S), my_hi = (int)((long long)(rank + 1) * a.mt / S);
+  const int tid = (int)threadIdx.x - 64;  // epilogue thread 0 .. 255
+  const int fq = tid & 31;                 // features 4 fq .. 4 fq + 3 of the tile
+  const int tsub = tid >> 5;               // token offset within a pass of 8
+  const T* res_base = static_cast<const T*>(a.e.residual) + col0 + 4 * fq;
+  T* out_base = static_cast<T*>(a.e.out) + col0 + 4 * fq;
+  const bool residual = a.e.mode == KVE_EPI_RESIDUAL;
+  // The first batch's residual rows load while the partials drain and the cluster syncs.
+  uint2 res[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    res[b] = make_uint2(0u, 0u);
+    const int t = my_lo + tsub + 8 * b;
+    if (epi && residual && t < my_hi && tok0 + t < a.m)
+      res[b] = *reinterpret_cast<const uint2*>(res_base + (size_t)(tok0 + t) * a.e.ld_out);
+  }
+  // Peers read this CTA's stage buffers: wait until every CTA has finished its main loop.
+  cluster_sync();
+  if (epi) {
+    float* prow = pout + f_local;
+    for (int c = egrp * kRows; c < a.mt; c += kEpiGroups * kRows) {
+      const int n = min(kRows, a.mt - c);
+      float v[32];
+      tmem_load_cols(t_lane + c, n, have, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < n) prow[(c + j) * BM] = v[j];
+    }
+  }
+  cluster_sync();  // every partial is in its CTA's shared memory
+  if (epi) {
+    uint32_t peer[kMaxSplits];
+#pragma unroll
+    for (int u = 0; u < kMaxSplits; ++u) peer[u] = u < S ? map_to(smem_u32(pout + 4 * fq), (uint32_t)u) : 0u;
+    for (int t_b = my_lo + tsub; t_b < my_hi; t_b += 8 * B) {
+      float4 acc[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        acc[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int t = t_b + 8 * b;
+        if (t_b != my_lo + tsub && residual && t < my_hi && tok0 + t < a.m)
+          res[b] = *reinterpret_cast<const uint2*>(res_base + (size_t)(tok0 + t) * a.e.ld_out);
+      }
+      float4 part[kMaxSplits][B];
+#pragma unroll
+      for (int u = 0; u < kMaxSplits; ++u)
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const int t = t_b + 8 * b;
+          part[u][b] = u < S && t < my_hi ? ld_cluster_f4(peer[u] + (uint32_t)(t * BM * 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int u = 0; u < kMaxSplits; ++u)
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+          if (u < S) {
+            acc[b].x += part[u][b].x;
+            acc[b].y += part[u][b].y;
+            acc[b].z += part[u][b].z;
+            acc[b].w += part[u][b].w;
+          }
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int t = t_b + 8 * b;
+        if (t >= my_hi || tok0 + t >= a.m) continue;
+        const float sv[4] = {acc[b].x, acc[b].y, acc[b].z, acc[b].w};
+        const T* rv = reinterpret_cast<const T*>(&res[b]);
+        uint2 outv;
+        T* ov = reinterpret_cast<T*>(&outv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const T y = __float2bfloat16_rn(sv[j]);
+          ov[j] = residual ? __float2bfloat16_rn(__fadd_rn(__bfloat162float(rv[j]), __bfloat162float(y))) : y;
+        }
+        *reinterpret_cast<uint2*>(out_base + (size_t)(tok0 + t) * a.e.ld_out) = outv;
+      }
+    }
+  }
+  cluster_sync();  // no CTA leaves (or reuses its partial) while a peer may still read it
 }
 
 // Rows of weights per CTA: MH halves of 128 (one MMA M-tile each) sharing the
@@ -628,93 +829,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
         E::copy_out(a, buf, tok0 + c0, n, col0, etid, res);
       }
     }
-  } else if constexpr (BMT == BM) {
-    // Split-K over the cluster: each CTA writes its fp32 partial, grouped by the
-    // CTA that owns each token (contiguous slices of the round), and sends every
-    // peer its group with one bulk shared-memory copy; the owner then sums the
-    // S partials of its tokens in rank order from its own shared memory.
-    const uint32_t rank = cluster_rank();
-    const int slm = (a.rch + S - 1) / S;               // max tokens per slice
-    float* pout = reinterpret_cast<float*>(smem);      // [rch][128] this CTA's partial, token-major
-    float* recv = pout + (size_t)a.rch * BM;           // [S][slm][128] received slices, by sender
-    int round = 0;
-    for (int r0 = 0; r0 < a.mt; r0 += a.rch, ++round) {
-      const int ch = min(a.rch, a.mt - r0);
-      // Peers write into this CTA's drained stage buffers: wait until every CTA of
-      // the cluster has finished its main loop (and, in later rounds, its reads).
-      cluster_sync();
-      const int my_lo = (int)((long long)rank * ch / S), my_hi = (int)((long long)(rank + 1) * ch / S);
-      if (epi) {
-        // Both warpgroups drain alternate 32-token chunks; owner u's tokens
-        // [lo_u, hi_u) are contiguous rows of pout.
-        float* prow = pout + f_local;
-        for (int c = egrp * kRows; c < ch; c += kEpiGroups * kRows) {
-          const int n = min(kRows, ch - c);
-          float v[32];
-          tmem_load_cols(t_lane + r0 + c, n, have, v);
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < n) prow[(c + j) * BM] = v[j];
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        epi_bar_all();
-        // Thread u of the first warpgroup sends peer u its slice (one bulk copy each,
-        // issued in parallel: one thread issuing them in turn spent ~0.3 us per copy);
-        // thread `rank` arms this CTA's receive barrier for the S - 1 incoming slices.
-        if (egrp == 0 && etid < S) {
-          const int u = etid;
-          if (u == (int)rank) {
-            mbar_expect_tx(smem_u32(recv_bar), (uint32_t)(S - 1) * (uint32_t)(my_hi - my_lo) * BM * 4);
-          } else {
-            const int lo = (int)((long long)u * ch / S), hi = (int)((long long)(u + 1) * ch / S);
-            if (hi > lo)
-              bulk_copy_to_peer(map_to(smem_u32(recv + (size_t)rank * slm * BM), (uint32_t)u),
-                                smem_u32(pout + (size_t)lo * BM), (uint32_t)(hi - lo) * BM * 4,
-                                map_to(smem_u32(recv_bar), (uint32_t)u));
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-          }
-        }
-        mbar_wait(smem_u32(recv_bar), (uint32_t)(round & 1), a.status);
-        // Sum the S partials of each owned token in rank order (own slice from
-        // pout), 32-token chunks alternating between the warpgroups when both
-        // groups' double-buffered staging fits (16-bit outputs).
-        constexpr int kStgBufC = kRows * E::W * E::ES;
-        constexpr int kSumGroups = 2 * kEpiGroups * kStgBufC <= kStageBytes ? kEpiGroups : 1;
-        const float* src[kMaxSplits];
-#pragma unroll
-        for (int u = 0; u < kMaxSplits; ++u)
-          src[u] = (u == (int)rank ? pout + (size_t)my_lo * BM : recv + (size_t)u * slm * BM) + f_local;
-        const int mine = my_hi - my_lo;
-        int it = 0;
-        for (int t0 = egrp * kRows; egrp < kSumGroups && t0 < mine; t0 += kSumGroups * kRows, ++it) {
-          const int n = min(kRows, mine - t0);
-          uint8_t* buf = stg + (egrp * 2 + (it & 1)) * kStgBufC;
-          uint4 res[E::NPASS];
-          if (round == 0 && it == 0) {
-#pragma unroll
-            for (int i = 0; i < E::NPASS; ++i) res[i] = res_first[i];
-          } else {
-            E::load_res(a, tok0 + r0 + my_lo + t0, n, col0, etid, res);
-          }
-          for (int j0 = 0; j0 < n; j0 += 4) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int u = 0; u < kMaxSplits; ++u) {
-              if (u < S) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-                  if (j0 + q < n) acc[q] += src[u][(t0 + j0 + q) * BM];
-              }
-            }
-            E::template stage<4>(buf, j0, n, f_local, acc, bias_f);
-          }
-          epi_bar(egrp);
-          E::copy_out(a, buf, tok0 + r0 + my_lo + t0, n, col0, etid, res);
-        }
-        if (egrp == 0 && etid < S && etid != (int)rank) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-        epi_bar_all();
-      }
+  } else if constexpr (BMT == BM && MH == 1 && BF &&
+                       (MODE == KVE_EPI_RESIDUAL || MODE == KVE_EPI_STORE)) {
+    if ((size_t)a.mt * BM * 4 <= (size_t)a.stages * a.stage_bytes && a.out_vec_ok && col0 + BM <= a.e.ld_out) {
+      splitk_direct(a, smem, t_lane, have, epi, egrp, f_local, tok0, col0);
+    } else {
+      splitk_exchange<MODE, BF, MH, BMT>(a, smem, t_lane, have, epi, egrp, f_local, etid, tok0, col0, bias_f,
+                                         res_first, recv_bar);
     }
+  } else if constexpr (BMT == BM) {
+    splitk_exchange<MODE, BF, MH, BMT>(a, smem, t_lane, have, epi, egrp, f_local, etid, tok0, col0, bias_f,
+                                       res_first, recv_bar);
   }
 
   if (epi) {
