@@ -46,14 +46,18 @@ template <> struct Vec<__nv_bfloat16> {
   }
 };
 
+// Argmax of x[lo, hi) of one row (x is the row's start, indices are absolute;
+// with vec_ok, lo is a multiple of the vector width). The result, valid in
+// thread 0, goes to best_v / best_i.
 template <typename T>
-__device__ __forceinline__ int row_argmax(const T* x, int cols, bool vec_ok) {
-  float best_v = -INFINITY;
-  int best_i = 0x7fffffff;
+__device__ __forceinline__ void range_argmax(const T* x, int lo, int hi, bool vec_ok, float& best_v, int& best_i) {
+  best_v = -INFINITY;
+  best_i = 0x7fffffff;
   constexpr int N = Vec<T>::N;
-  int nvec = vec_ok ? cols / N : 0;
+  const int v0 = vec_ok ? lo / N : 0;
+  const int nvec = vec_ok ? hi / N : 0;  // vectors [v0, nvec), then elements [max(lo, nvec * N), hi)
   constexpr int U = 4;
-  int v = threadIdx.x;
+  int v = v0 + threadIdx.x;
   for (; v + (U - 1) * kArgmaxThreads < nvec; v += U * kArgmaxThreads) {
     float buf[U][N];
 #pragma unroll
@@ -73,7 +77,7 @@ __device__ __forceinline__ int row_argmax(const T* x, int cols, bool vec_ok) {
     for (int j = 0; j < N; ++j)
       if (better(buf[j], v * N + j, best_v, best_i)) { best_v = buf[j]; best_i = v * N + j; }
   }
-  for (int i = nvec * N + threadIdx.x; i < cols; i += kArgmaxThreads) {
+  for (int i = max(lo, nvec * N) + threadIdx.x; i < hi; i += kArgmaxThreads) {
     float f = Elem<T>::to_f(x[i]);
     if (better(f, i, best_v, best_i)) { best_v = f; best_i = i; }
   }
@@ -98,7 +102,14 @@ __device__ __forceinline__ int row_argmax(const T* x, int cols, bool vec_ok) {
       if (better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
     }
   }
-  return best_i;  // valid in thread 0
+}
+
+template <typename T>
+__device__ __forceinline__ int row_argmax(const T* x, int cols, bool vec_ok) {
+  float v;
+  int i;
+  range_argmax(x, 0, cols, vec_ok, v, i);
+  return i;  // valid in thread 0
 }
 
 template <typename T>
@@ -156,6 +167,55 @@ argmax_kernel(const T* x, int64_t row_stride, int cols, bool vec_ok, int32_t* __
   }
 }
 
+// Row argmax split over a cluster of `parts` CTAs (consecutive CTAs form one
+// row's cluster): CTA p scans columns [p * chunk, (p + 1) * chunk) and rank 0
+// combines the parts' (value, index) pairs through distributed shared memory.
+// `better` is a total order, so the result is the one argmax_kernel gives; with
+// few rows (the draft's 64) a single CTA per row leaves most SMs idle and each
+// scans 300 KB at one SM's load rate.
+template <typename T>
+__global__ void __launch_bounds__(kArgmaxThreads)
+argmax_split_kernel(const T* x, int64_t row_stride, int cols, bool vec_ok, int parts, int chunk,
+                    int32_t* __restrict__ out, const int32_t* scatter_idx, int32_t* __restrict__ scatter_out,
+                    int64_t scatter_len, int* __restrict__ status) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int row = blockIdx.x / parts, part = blockIdx.x % parts;
+  const int lo = min(part * chunk, cols), hi = min(lo + chunk, cols);
+  float v;
+  int i;
+  range_argmax(x + (size_t)row * row_stride, lo, hi, vec_ok, v, i);
+  __shared__ float s_v;
+  __shared__ int s_i;
+  if (threadIdx.x == 0) {
+    s_v = v;
+    s_i = i;
+  }
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (part == 0 && threadIdx.x == 0) {
+    const uint32_t av = static_cast<uint32_t>(__cvta_generic_to_shared(&s_v));
+    const uint32_t ai = static_cast<uint32_t>(__cvta_generic_to_shared(&s_i));
+    for (int p = 1; p < parts; ++p) {
+      uint32_t rv, ri;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rv) : "r"(av), "r"(p));
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ri) : "r"(ai), "r"(p));
+      float pv;
+      int pi;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(rv) : "memory");
+      asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(pi) : "r"(ri) : "memory");
+      if (better(pv, pi, v, i)) { v = pv; i = pi; }
+    }
+    out[row] = i;
+    if (scatter_out) {
+      const int j = scatter_idx[row];
+      if (j >= 0 && j < scatter_len) scatter_out[j] = i;
+      else report(status, KVE_ERR_BOUNDS);
+    }
+  }
+  // The parts stay resident until rank 0 has read them.
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 bool vec_aligned(const void* p, int64_t row_stride, int elem) {
   return ((uintptr_t)p % 16 == 0) && ((row_stride * elem) % 16 == 0);
 }
@@ -202,9 +262,47 @@ extern "C" int kve_greedy_accept(const void* logits, int dtype, int64_t row_stri
 }
 
 namespace {
+// Parts per row for argmax_split_kernel (cluster size, at most the portable 8):
+// enough CTAs to cover the SMs a few times over, none for wide batches or short rows.
+int argmax_parts(int rows, int cols) {
+  if (cols < 8 * 4096) return 1;
+  const int want = (4 * 148 + rows - 1) / rows;
+  return want >= 8 ? 8 : want >= 4 ? 4 : want >= 2 ? 2 : 1;
+}
+
+template <typename T>
+int argmax_split_launch(const T* x, int rows, int cols, int64_t row_stride, bool vec_ok, int parts, int32_t* out,
+                        const int32_t* scatter_idx, int32_t* scatter_out, int64_t scatter_len, int* status,
+                        cudaStream_t stream) {
+  constexpr int N = Vec<T>::N;
+  const int chunk = ((cols + parts - 1) / parts + N - 1) / N * N;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = parts;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cudaError_t err = launch_kernel_ex(argmax_split_kernel<T>, dim3(rows * parts), dim3(kArgmaxThreads), 0, stream,
+                                     &attr, 1, x, row_stride, cols, vec_ok, parts, chunk, out, scatter_idx,
+                                     scatter_out, scatter_len, status);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    count_launch();
+    return set_error(KVE_ERR_CUDA, "kve_argmax_rows(split): launch failed: %s", cudaGetErrorString(err));
+  }
+  return check_launch("kve_argmax_rows");
+}
+
 int argmax_launch(const void* x, int dtype, int rows, int cols, int64_t row_stride, int32_t* out,
                   const int32_t* scatter_idx, int32_t* scatter_out, int64_t scatter_len, int* status,
                   cudaStream_t stream) {
+  const int parts = argmax_parts(rows, cols);
+  if (parts > 1 && dtype == KVE_F32)
+    return argmax_split_launch(static_cast<const float*>(x), rows, cols, row_stride, vec_aligned(x, row_stride, 4),
+                               parts, out, scatter_idx, scatter_out, scatter_len, status, stream);
+  if (parts > 1 && dtype == KVE_BF16)
+    return argmax_split_launch(static_cast<const __nv_bfloat16*>(x), rows, cols, row_stride,
+                               vec_aligned(x, row_stride, 2), parts, out, scatter_idx, scatter_out, scatter_len,
+                               status, stream);
   if (dtype == KVE_F32) {
     launch_kernel(argmax_kernel<float>, dim3(rows), dim3(kArgmaxThreads), 0, stream,
         static_cast<const float*>(x), row_stride, cols, vec_aligned(x, row_stride, 4), out, scatter_idx, scatter_out,

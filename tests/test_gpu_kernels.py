@@ -113,6 +113,23 @@ def test_argmax_rows(cuda_device):
     assert torch.equal(ops.argmax_rows(x.to(cuda_device)).cpu().long(), x.argmax(-1))
 
 
+def test_argmax_rows_split_over_parts(cuda_device):
+    """Few long rows split each row over a cluster of CTAs (8 parts of 18,992 columns
+    here): a tie across a part boundary resolves to the lower index, the first NaN is
+    the maximum, an all -inf row gives 0 - every row equal to torch.argmax."""
+    g = torch.Generator().manual_seed(9)
+    for dt in (torch.float32, torch.bfloat16):
+        x = torch.randn(8, 151936, generator=g).to(dt)
+        x[0, 18991] = x[0, 18992] = 100.0                 # the two sides of the first part boundary
+        x[1, 18992 * 3 + 5] = x[1, 18992 * 7 + 1] = 100.0
+        x[2, 100000] = x[2, 150000] = float("nan")
+        x[3, :] = float("-inf")
+        x[4, 151935] = 100.0                              # the last column
+        got = ops.argmax_rows(x.to(cuda_device)).cpu().long()
+        assert torch.equal(got, torch.argmax(x.float(), -1)), (dt, got)
+        assert got[:5].tolist() == [18991, 18992 * 3 + 5, 100000, 0, 151935]
+
+
 def test_argmax_rows_scatter_places_drafts_in_the_verify_feed(cuda_device):
     """The draft loop's argmax writes each row's token both to the drafts buffer and
     to its slot of the verify pass's token ids (kvengine speculative.py:160-162:
