@@ -112,8 +112,10 @@ __device__ __forceinline__ int row_argmax(const T* x, int cols, bool vec_ok) {
   return i;  // valid in thread 0
 }
 
+// Three CTAs per SM (at most 40 registers a thread): a verify batch's rows
+// (64 x 5 = 320) then run in one wave on 148 SMs instead of 296 + 24.
 template <typename T>
-__global__ void __launch_bounds__(kArgmaxThreads)
+__global__ void __launch_bounds__(kArgmaxThreads, 3)
 accept_kernel(const T* logits, int64_t row_stride, const int32_t* drafts,
               int64_t dsb, int64_t dsj, int k, int vocab, bool vec_ok, int32_t* __restrict__ preds, int32_t* __restrict__ n_acc,
               int32_t* __restrict__ emitted, int32_t* __restrict__ counters) {
@@ -263,10 +265,10 @@ extern "C" int kve_greedy_accept(const void* logits, int dtype, int64_t row_stri
 
 namespace {
 // Parts per row for argmax_split_kernel (cluster size, at most the portable 8):
-// enough CTAs to cover the SMs a few times over, none for wide batches or short rows.
+// as many CTAs as fit the SMs in one wave, none for wide batches or short rows.
 int argmax_parts(int rows, int cols) {
   if (cols < 8 * 4096) return 1;
-  const int want = (4 * 148 + rows - 1) / rows;
+  const int want = 2 * 148 / rows;  // one wave at two 512-thread CTAs per SM
   return want >= 8 ? 8 : want >= 4 ? 4 : want >= 2 ? 2 : 1;
 }
 
