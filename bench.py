@@ -574,7 +574,9 @@ def run_micro(args):
                  # the prompt pass fused into the first verify (64 requests x 132 rows)
                  ("prefill_qkv", 8448, 2560, 2048, L.EPI_BIAS), ("prefill_o_proj", 8448, 2048, 2048, L.EPI_RESIDUAL),
                  ("prefill_gate_up", 8448, 22016, 2048, L.EPI_SILU_MUL),
-                 ("prefill_down", 8448, 2048, 11008, L.EPI_RESIDUAL))
+                 ("prefill_down", 8448, 2048, 11008, L.EPI_RESIDUAL),
+                 # the draft's prompt pass (64 requests x 128 rows)
+                 ("prefill_draft_down", 8192, 896, 4864, L.EPI_RESIDUAL))
         for name, m, n, k, epi in cases:
             if args.gemm_case and name not in args.gemm_case.split(","):
                 continue

@@ -206,6 +206,14 @@ int kve_gemm_force_pair(int mode);
  * bit-identical either way. */
 int kve_gemm_force_rows(int rows);
 
+/* Tuning and test hook (no kvengine counterpart): whether later tcgen05 GEMMs
+ * with split-K compute all of a tile's k-ranges in one CTA (one TMEM accumulator
+ * per range, summed in the epilogue) instead of over a cluster of CTAs that
+ * exchange their partials: 0 = for prompt-sized batches (m >= 2048, the
+ * default), 1 = never, 2 = wherever the shape allows. The ranges and the order
+ * of their sum are the same either way, so results are bit-identical. */
+int kve_gemm_force_local_split(int mode);
+
 /* The tcgen05 GEMM's launch plan for an [m, k] x [n, k]^T product with a bf16
  * output (no kvengine counterpart): out[0..12] = split-K factor, token tiles,
  * token groups per tile, tokens per group, weight halves, k-chunks per stage,

@@ -68,6 +68,7 @@ struct TcArgs {
   int feat_ctas;         // tiles along features (128 x MH weight rows each)
   int acc_bufs;          // TMEM accumulators per CTA (2: the epilogue overlaps the next tile)
   int stg_bytes;         // output staging after the stage ring (CTAs that walk several tiles), else 0
+  int lsplit;            // 1: one CTA computes all `splits` k-ranges into its own TMEM accumulators
   EpiArgs e;
   int* status;
 };
@@ -591,10 +592,14 @@ __device__ __forceinline__ void splitk_direct(const TcArgs& a, uint8_t* smem, ui
 // slab fits, so all of a CTA's weights can be requested before the dependency
 // wait. The accumulator's 64 rows sit in TMEM lanes 0-15 of each 32-lane
 // quarter: epilogue threads 0-15 of each warp own a row, 16-31 write nothing.
-template <int MODE, bool BF, int NG, int MH, int BMT = BM>
+//
+// LSP (a.lsplit): split-K inside the CTA - it computes all a.splits k-ranges of
+// its tile, range r into its own TMEM accumulator, and sums them in the epilogue.
+template <int MODE, bool BF, int NG, int MH, int BMT = BM, bool LSP = false>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, TcArgs a) {
   static_assert(BMT == BM || (BMT == 64 && MH == 1), "64-row tiles carry one weight half");
+  static_assert(!LSP || (BMT == BM && MH == 1 && NG == 1), "in-CTA split-K tiles are one 128-row half, one group");
   using E = Epi<MODE, BF, BMT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Stage buffers need 1024-byte alignment for the 128-byte swizzle atoms.
@@ -612,12 +617,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * a.mt;
   const int feat0 = blockIdx.y * BMT * MH;
-  const int split = blockIdx.z;
-  const int kb0 = (int)((long long)split * a.k_blocks / a.splits);
-  const int kb1 = (int)((long long)(split + 1) * a.k_blocks / a.splits);
-  const int n_stages_work = (kb1 - kb0 + a.kc - 1) / a.kc;  // pipeline stages of kc k-blocks
+  // Split-K: k-range r is k-blocks [range_lo(r), range_lo(r + 1)). Over a cluster
+  // (CS CTAs) this CTA computes range blockIdx.z; with lsplit it computes all LS
+  // ranges itself, range r into its own TMEM accumulator, and sums them in the
+  // epilogue exactly as the cluster's owner sums its peers' partials.
+  const int LS = LSP ? a.splits : 1;
+  const int CS = LSP ? 1 : a.splits;
+  // (r * k_blocks fits 32 bits: k_blocks = k / 64 < 2^25 and r <= kMaxSplits.)
+  auto range_lo = [&](int r) { return r * a.k_blocks / a.splits; };
+  const int r_first = LSP ? 0 : (int)blockIdx.z;
+  const int kb0 = range_lo(r_first), kb1 = range_lo(r_first + 1);
+  // Pipeline stages of kc k-blocks, a range's last one possibly partial.
+  int n_stages_work = (kb1 - kb0 + a.kc - 1) / a.kc;
+  if constexpr (LSP)
+    for (int r = 1; r < LS; ++r) n_stages_work += (range_lo(r + 1) - range_lo(r) + a.kc - 1) / a.kc;
   uint32_t tmem_cols = 32;
-  while ((int)tmem_cols < MH * a.mt) tmem_cols <<= 1;
+  while ((int)tmem_cols < MH * a.mt * LS) tmem_cols <<= 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -658,15 +673,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       else tma_load_2d(smem_u32(d), &map_x, chunk * BK, tok0 + g * a.n_g, fb);
     }
   };
+  // Walk to the next stage: `chunk` is its first k-block, in range r = [rlo, rhi).
+  auto next_stage = [&](int& r, int& chunk, int& rlo, int& rhi) {
+    chunk += a.kc;
+    if (LSP && chunk >= rhi) {
+      ++r;
+      rlo = chunk = rhi;
+      rhi = range_lo(r + 1);
+    }
+  };
   const int pre = a.w_static ? min(n_stages_work, a.stages) : 0;
   if (warp == 0 && lane == 0) {
     prefetch_map(&map_w);
     prefetch_map(&map_x);
     uint8_t* sa = smem;
+    int r = r_first, chunk = kb0, rlo = kb0, rhi = kb1;
     for (int it = 0; it < pre; ++it, sa += a.stage_bytes) {
       const uint32_t fb = smem_u32(&full[it]);
       mbar_add_tx(fb, a.w_bytes);
-      load_w(sa, kb0 + it * a.kc, fb);
+      load_w(sa, chunk, fb);
+      next_stage(r, chunk, rlo, rhi);
     }
   }
   // Everything else touches global memory only after the previous kernel has
@@ -684,7 +710,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       int issued = 0, s = 0;
       uint32_t ph = 0;
       uint8_t* sa = smem;
-      int chunk = kb0;
+      int r = r_first, chunk = kb0, rlo = kb0, rhi = kb1;
       for (int it = 0; it < n_iter; ++it) {
         if (it >= a.stages && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, a.status)) break;
         const uint32_t fb = smem_u32(&full[s]);
@@ -696,7 +722,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
         }
         load_x(sa + a.w_bytes, chunk, fb);
         ++issued;
-        chunk += a.kc;
+        next_stage(r, chunk, rlo, rhi);
         if (++s == a.stages) {
           s = 0;
           ph ^= 1u;
@@ -732,25 +758,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       int s = 0;
       uint32_t ph = 0;
       uint64_t soff = 0;
-      int chunk = kb0;
+      int r = r_first, chunk = kb0, rlo = kb0, rhi = kb1;
       for (int it = 0; it < n_iter; ++it) {
         if (!mbar_wait(smem_u32(&full[s]), ph, a.status)) break;
         fence_after();
-        const int nch = min(a.kc, kb1 - chunk);  // a partial last stage multiplies only real chunks
+        const int nch = min(a.kc, rhi - chunk);  // a range's partial last stage multiplies only its own chunks
+        const uint32_t acc_base = tmem_base + (LSP ? (uint32_t)(r * a.mt) : 0u);
         for (int j = 0; j < nch; ++j) {
           const uint64_t ad = a0 + soff + j * a_chunk, bd = b0 + soff + j * b_chunk;
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-            const uint32_t acc = (it > 0 || j > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t acc = (chunk > rlo || j > 0 || kk > 0) ? 1u : 0u;
 #pragma unroll
             for (int h = 0; h < MH; ++h)
 #pragma unroll
               for (int g = 0; g < NG; ++g)
-                umma_bf16(tmem_base + h * a.mt + g * a.n_g, ad + h * half_step + kk * kstep,
+                umma_bf16(acc_base + h * a.mt + g * a.n_g, ad + h * half_step + kk * kstep,
                           bd + g * grp_step + kk * kstep, idesc, acc);
           }
         }
-        chunk += a.kc;
+        next_stage(r, chunk, rlo, rhi);
         umma_commit(smem_u32(&empty[s]));
         if (++s == a.stages) {
           s = 0;
@@ -787,12 +814,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   // The first chunk's per-row inputs load while the main loop runs.
   const int first_c0 = MH == 1 ? egrp * kRows : 0;
   uint4 res_first[E::NPASS];
-  if (epi && a.splits == 1 && first_c0 < a.mt)
+  if (epi && CS == 1 && first_c0 < a.mt)
     E::load_res(a, tok0 + first_c0, min(kRows, a.mt - first_c0), col0, etid, res_first);
   if constexpr (BMT == BM) {
     // Split-K: the first chunk of tokens this CTA owns in the first round.
     constexpr int kSumGroupsP = 2 * kEpiGroups * (kRows * E::W * E::ES) <= kStageBytes ? kEpiGroups : 1;
-    if (epi && a.splits > 1 && egrp < kSumGroupsP) {
+    if (epi && CS > 1 && egrp < kSumGroupsP) {
       const int ch0 = min(a.rch, a.mt);
       const uint32_t rk = cluster_rank();
       const int lo = (int)((long long)rk * ch0 / a.splits), hi = (int)((long long)(rk + 1) * ch0 / a.splits);
@@ -805,10 +832,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     have = !aborted && mbar_wait(smem_u32(tmem_full), 0, a.status);
     fence_after();
   }
-  const int S = a.splits;
   uint8_t* stg = smem + a.stg_off;
   constexpr int kStgBuf = kRows * BM * 4;  // one staging buffer (fp32 worst case)
-  if (S == 1) {
+  if (CS == 1) {
     if (epi) {
       int it = 0;
       constexpr int kChunkStride = (MH == 1 ? kEpiGroups : 1) * kRows;
@@ -823,7 +849,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
           E::load_res(a, tok0 + c0, n, col0, etid, res);
         }
         float v[32];
-        tmem_load_cols(t_lane + c0, n, have, v);
+        if constexpr (!LSP) {
+          tmem_load_cols(t_lane + c0, n, have, v);
+        } else {
+          // The LS partials summed from zero in range order: the additions of the
+          // cluster split-K reductions (splitk_exchange, splitk_direct).
+          // 16 columns per load keeps the second operand to 16 registers.
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          for (int u = 0; u < LS; ++u) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (h == 1 && n <= 16) break;
+              float p[16];
+              if (have) {
+                tmem_ld16(t_lane + (uint32_t)(u * a.mt) + c0 + 16 * h, p);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) p[i] = 0.f;
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[16 * h + i] += p[i];
+            }
+          }
+        }
         E::template stage<32>(buf, 0, live ? n : 0, f_local, v, bias_f);
         epi_bar(egrp);
         E::copy_out(a, buf, tok0 + c0, n, col0, etid, res);
@@ -1482,6 +1531,7 @@ struct Plan {
   int acc_bufs, stg_bytes;
   bool pair;          // CTA pairs with the 2-CTA MMA (gemm_tc_pair_kernel)
   int bmt;            // weight rows per MMA tile: 128, or 64 (rows64)
+  bool lsplit;        // split-K ranges summed inside one CTA (no cluster exchange)
 };
 
 typedef void (*GemmKernel)(CUtensorMap, CUtensorMap, TcArgs);
@@ -1490,6 +1540,27 @@ template <int MODE, bool BF, int NG, int MH, bool P>
 GemmKernel kernel_of() {
   if constexpr (P) return gemm_tc_persistent_kernel<MODE, BF, NG, MH>;
   else return gemm_tc_kernel<MODE, BF, NG, MH>;
+}
+
+// The in-CTA split-K kernel (one 128-row half, one token group).
+GemmKernel lsplit_kernel_for(int mode, int out_dtype) {
+  const bool bf = out_dtype == KVE_BF16;
+  switch (mode) {
+    case KVE_EPI_STORE:
+      return bf ? gemm_tc_kernel<KVE_EPI_STORE, true, 1, 1, BM, true> : gemm_tc_kernel<KVE_EPI_STORE, false, 1, 1, BM, true>;
+    case KVE_EPI_BIAS:
+      return bf ? gemm_tc_kernel<KVE_EPI_BIAS, true, 1, 1, BM, true> : gemm_tc_kernel<KVE_EPI_BIAS, false, 1, 1, BM, true>;
+    case KVE_EPI_RESIDUAL:
+      return bf ? gemm_tc_kernel<KVE_EPI_RESIDUAL, true, 1, 1, BM, true>
+                : gemm_tc_kernel<KVE_EPI_RESIDUAL, false, 1, 1, BM, true>;
+    case KVE_EPI_SILU_MUL:
+      return bf ? gemm_tc_kernel<KVE_EPI_SILU_MUL, true, 1, 1, BM, true>
+                : gemm_tc_kernel<KVE_EPI_SILU_MUL, false, 1, 1, BM, true>;
+    case kEpiQkvRope:
+      return bf ? gemm_tc_kernel<kEpiQkvRope, true, 1, 1, BM, true> : nullptr;
+    default:
+      return nullptr;
+  }
 }
 
 template <int NG, int MH, bool P>
@@ -1563,6 +1634,8 @@ void configure_kernel() {
             if (shape == 0 && !persist) {
               GemmKernel rk = rows64_kernel_for(mode, dt);
               if (rk) cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
+              GemmKernel lk = lsplit_kernel_for(mode, dt);
+              if (lk) cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
             }
           }
   });
@@ -1787,6 +1860,47 @@ int choose_splits(int feat_tiles, int k_blocks, bool tma3d) {
 std::atomic<int> g_force_t{0}, g_force_mh{0}, g_force_kc{0};
 // Split-K factor forced through kve_gemm_force_splits (0 = the function of (n, k)).
 std::atomic<int> g_force_s{0};
+// In-CTA split-K through kve_gemm_force_local_split: 0 = the rule, 1 = never, 2 = where valid.
+std::atomic<int> g_force_local{0};
+
+// In-CTA split-K for prompt-sized batches. The split factor S is a function of
+// (n, k) only, so a prompt-sized batch splits K like a decode batch does; over a
+// cluster that costs an exchange of fp32 partials about as long as the main loop
+// (three rounds of 128 x 384 partials per tile for the 3B down projection). With
+// many tiles to spread over the SMs, one CTA can instead compute all S ranges of
+// its tile, range r into its own TMEM accumulator (S x mt <= 512 columns), and sum
+// them in the epilogue in the same order from the same zero start: the same bits
+// as the cluster reduction, without the exchange.
+void try_local_split(Plan& p, int m) {
+  const int force = g_force_local.load();
+  if (force == 1 || p.splits < 2 || !p.tma3d) return;
+  if (force != 2 && m < kLargeM) return;
+  int mt = 512 / p.splits / 16 * 16;  // tokens per tile: S accumulators fill at most the 512 TMEM columns
+  if (mt > kMaxNG) mt = kMaxNG;
+  if (mt < 16) return;
+  const int per = round16(m < mt ? (m < 16 ? 16 : m) : mt);
+  const int kc = chunks_for(1, per, 1, true, kAvail);
+  const uint32_t w_bytes = (uint32_t)(BM * BK * 2 * kc);
+  const uint32_t stage_bytes = w_bytes + (uint32_t)(per * BK * 2 * kc);
+  const int stages = (int)std::min<size_t>(kMaxStages, kAvail / stage_bytes);
+  // Two stages, and the drained ring must hold the epilogue's four output staging buffers.
+  if (stages < 2 || (size_t)stages * stage_bytes < 4 * (size_t)kRows * BM * 4) return;
+  p.lsplit = true;
+  p.mt = p.n_g = per;
+  p.ng = 1;
+  p.mh = 1;
+  p.pair = false;
+  p.token_tiles = (m + per - 1) / per;
+  p.kc = kc;
+  p.w_bytes = w_bytes;
+  p.stage_bytes = stage_bytes;
+  p.stages = stages;
+  p.stg_bytes = 0;
+  p.acc_bufs = 1;
+  p.rch = per;
+  p.stg_off = 0;
+  p.grid_x = p.token_tiles * p.feat_tiles;
+}
 
 Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
   Plan p{};
@@ -1883,6 +1997,7 @@ Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
       }
     }
   }
+  try_local_split(p, m);
   return p;
 }
 
@@ -1965,7 +2080,7 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   const int row_bytes = (e.mode == KVE_EPI_SILU_MUL ? BM / 2 : BM) * (e.out_dtype == KVE_BF16 ? 2 : 4);
   Plan p = make_plan(m, n, k, row_bytes);
   try_rows64(p, m, n, k, e.mode, e.out_dtype, e.hd);
-  if (p.stages < 2 || (p.splits > 1 && p.rch == 0))
+  if (p.stages < 2 || (p.splits > 1 && !p.lsplit && p.rch == 0))
     return set_error(KVE_ERR_SHAPE, "kve_gemm(tcgen05): tile does not fit shared memory");
   TcArgs a{};
   a.m = m; a.n = n; a.k = k; a.mt = p.mt; a.ng = p.ng; a.n_g = p.n_g; a.k_blocks = p.k_blocks;
@@ -1976,11 +2091,13 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   a.token_tiles = p.token_tiles;
   a.feat_ctas = p.bmt == 64 ? (n + 63) / 64 : p.pair ? (p.feat_tiles + 1) / 2 : (p.feat_tiles + p.mh - 1) / p.mh;
   a.acc_bufs = p.acc_bufs; a.stg_bytes = p.stg_bytes;
+  a.lsplit = p.lsplit ? 1 : 0;
   const int es = e.out_dtype == KVE_BF16 ? 2 : 4;
   a.out_vec_ok = ((uintptr_t)e.out % 16 == 0) && ((size_t)e.ld_out * es % 16 == 0) &&
                  (e.mode != KVE_EPI_RESIDUAL || (uintptr_t)e.residual % 16 == 0);
   const bool persist = p.stg_bytes > 0;
   GemmKernel kern = p.bmt == 64 ? rows64_kernel_for(e.mode, e.out_dtype)
+                  : p.lsplit ? lsplit_kernel_for(e.mode, e.out_dtype)
                   : p.pair ? pair_kernel_for(e.mode, e.out_dtype, p.ng) : kernel_for(e.mode, e.out_dtype, p.ng, p.mh, persist);
   if (!kern) return set_error(KVE_ERR_DTYPE, "kve_gemm(tcgen05): epilogue %d needs bf16 output", e.mode);
   CUtensorMap mw, mx;
@@ -1993,11 +2110,12 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   attr.id = cudaLaunchAttributeClusterDimension;
   attr.val.clusterDim.x = p.pair ? 2 : 1;  // a CTA pair, or the split-K CTAs of one tile
   attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = p.splits;
-  const dim3 grid = persist ? dim3(p.grid_x, 1, 1) : dim3(p.token_tiles, a.feat_ctas, p.splits);
+  const int cl_splits = p.lsplit ? 1 : p.splits;  // CTAs of a cluster splitting K
+  attr.val.clusterDim.z = cl_splits;
+  const dim3 grid = persist ? dim3(p.grid_x, 1, 1) : dim3(p.token_tiles, a.feat_ctas, cl_splits);
   cudaError_t err = launch_kernel_ex(kern, grid, dim3(kThreads),
                                      (size_t)p.stages * p.stage_bytes + p.stg_bytes + 1024 + 512, stream, &attr,
-                                     (p.splits > 1 || p.pair) ? 1 : 0, mw, mx, a);
+                                     (cl_splits > 1 || p.pair) ? 1 : 0, mw, mx, a);
   if (err != cudaSuccess) {
     cudaGetLastError();
     count_launch();
@@ -2046,6 +2164,16 @@ extern "C" int kve_gemm_force_splits(int splits) {
   return KVE_OK;
 }
 
+extern "C" int kve_gemm_force_local_split(int mode) {
+  using namespace kve;
+  if (mode < 0 || mode > 2)
+    return set_error(KVE_ERR_ARG, "kve_gemm_force_local_split: mode 0 (rule), 1 (never) or 2 (where valid)");
+  std::lock_guard<std::mutex> g(g_plan_mu);
+  g_force_local.store(mode);
+  g_plan_cache.clear();
+  return KVE_OK;
+}
+
 extern "C" int kve_gemm_force_rows(int rows) {
   using namespace kve;
   if (!(rows == 0 || rows == 64 || rows == 128))
@@ -2070,7 +2198,8 @@ extern "C" int kve_gemm_plan_info(int m, int n, int k, int* out) {
   try_rows64(p, m, n, k, KVE_EPI_STORE, KVE_BF16, 0);
   const int feat_ctas = p.bmt == 64 ? (n + 63) / 64 : p.pair ? (p.feat_tiles + 1) / 2 : (p.feat_tiles + p.mh - 1) / p.mh;
   const int v[13] = {p.splits, p.token_tiles, p.ng, p.n_g, p.mh, p.kc, p.stages, p.tma3d, feat_ctas,
-                     p.splits > 1 ? p.token_tiles * feat_ctas * p.splits : p.grid_x, p.acc_bufs, p.pair ? 1 : 0,
+                     p.splits > 1 && !p.lsplit ? p.token_tiles * feat_ctas * p.splits : p.grid_x, p.acc_bufs,
+                     p.pair ? 1 : 0,
                      p.bmt};
   for (int i = 0; i < 13; ++i) out[i] = v[i];
   return KVE_OK;

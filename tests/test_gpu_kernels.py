@@ -5,6 +5,7 @@ fp32 kernels within 1e-5 relative of an fp64/fp32 reference; bf16 attention
 within the 2e-2 absolute tolerance the task states for bf16 logits.
 """
 
+import ctypes
 import hashlib
 
 import numpy as np
@@ -493,6 +494,55 @@ def test_gemm_launch_shapes_give_identical_bits(cuda_device):
         L.check(lib.kve_gemm_force_shape(0, 0, 0))
         L.check(lib.kve_gemm_force_pair(0))
         L.check(lib.kve_gemm_force_rows(0))
+
+
+def test_gemm_split_k_inside_one_cta_gives_identical_bits(cuda_device):
+    """Split-K computed inside one CTA (one TMEM accumulator per k-range, summed in
+    the epilogue; the default for prompt-sized batches) reproduces the cluster
+    reduction bit for bit, for every epilogue and both output types, and a
+    prompt-sized batch's rows equal the same rows computed in a decode-sized batch
+    (which splits over a cluster)."""
+    lib = L.load()
+    g = torch.Generator(device=cuda_device).manual_seed(21)
+    # (m, n, k, epilogue, forced split factor or 0 for the (n, k) rule)
+    cases = [(64, 896, 4864, L.EPI_RESIDUAL, 0), (300, 2048, 11008, L.EPI_RESIDUAL, 0),
+             (2100, 896, 4864, L.EPI_RESIDUAL, 0), (2100, 2048, 11008, L.EPI_STORE, 0),
+             (17, 1000, 2048, L.EPI_BIAS, 3), (200, 1024, 1024, L.EPI_SILU_MUL, 4),
+             (100, 512, 4096, L.EPI_STORE, 8), (130, 768, 1536, L.EPI_RESIDUAL, 5)]
+    try:
+        for m, n, k, epi, fs in cases:
+            x = torch.randn(m, k, device=cuda_device, generator=g).to(torch.bfloat16)
+            w = (torch.randn(n, k, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+            n_out = n // 2 if epi == L.EPI_SILU_MUL else n
+            bias = torch.randn(n, device=cuda_device, generator=g) if epi == L.EPI_BIAS else None
+            res0 = torch.randn(m, n_out, device=cuda_device, generator=g).to(torch.bfloat16)
+            L.check(lib.kve_gemm_force_splits(fs))
+            info = (ctypes.c_int * 13)()
+            L.check(lib.kve_gemm_plan_info(m, n, k, info))
+            assert info[0] > 1, (m, n, k, "expected a split-K plan")
+            for out_dtype in (torch.bfloat16, torch.float32):
+                if epi == L.EPI_RESIDUAL and out_dtype != torch.bfloat16:
+                    continue
+
+                def run():
+                    out = res0.clone() if epi == L.EPI_RESIDUAL else None
+                    return ops.gemm(x, w, epilogue=epi, bias=bias, residual=out, out=out, out_dtype=out_dtype)
+
+                L.check(lib.kve_gemm_force_local_split(1))  # over a cluster
+                ref = run()
+                L.check(lib.kve_gemm_force_local_split(2))  # inside one CTA
+                got = run()
+                assert torch.equal(got, ref), (m, n, k, epi, fs, out_dtype)
+                L.check(lib.kve_gemm_force_local_split(0))  # the rule (inside one CTA from m = 2048)
+                assert torch.equal(run(), ref), (m, n, k, epi, fs, out_dtype)
+                if m >= 2048 and out_dtype == torch.bfloat16:
+                    full = ops.gemm(x, w, epilogue=L.EPI_STORE, out_dtype=torch.float32)
+                    for lo, hi in ((0, 64), (1000, 1320), (2093, 2100)):
+                        part = ops.gemm(x[lo:hi].contiguous(), w, epilogue=L.EPI_STORE, out_dtype=torch.float32)
+                        assert torch.equal(part, full[lo:hi]), (m, n, k, lo, hi)
+    finally:
+        L.check(lib.kve_gemm_force_local_split(0))
+        L.check(lib.kve_gemm_force_splits(0))
 
 
 def test_gemm_repeatable_and_no_workspace(cuda_device):
