@@ -414,7 +414,7 @@ __device__ __forceinline__ void splitk_exchange(const TcArgs& a, uint8_t* smem, 
       // Peers write into this CTA's drained stage buffers: wait until every CTA of
       // the cluster has finished its main loop (and, in later rounds, its reads).
       cluster_sync();
-      const int my_lo = (int)((long long)rank * ch / S), my_hi = (int)((long long)(rank + 1) * ch / S);
+      const int my_lo = (int)rank * ch / S, my_hi = ((int)rank + 1) * ch / S;  // 32-bit: ch <= 512, S <= 8
       if (epi) {
         // Both warpgroups drain alternate 32-token chunks; owner u's tokens
         // [lo_u, hi_u) are contiguous rows of pout.
@@ -437,7 +437,7 @@ __device__ __forceinline__ void splitk_exchange(const TcArgs& a, uint8_t* smem, 
           if (u == (int)rank) {
             mbar_expect_tx(smem_u32(recv_bar), (uint32_t)(S - 1) * (uint32_t)(my_hi - my_lo) * BM * 4);
           } else {
-            const int lo = (int)((long long)u * ch / S), hi = (int)((long long)(u + 1) * ch / S);
+            const int lo = u * ch / S, hi = (u + 1) * ch / S;
             if (hi > lo)
               bulk_copy_to_peer(map_to(smem_u32(recv + (size_t)rank * slm * BM), (uint32_t)u),
                                 smem_u32(pout + (size_t)lo * BM), (uint32_t)(hi - lo) * BM * 4,
@@ -503,7 +503,7 @@ __device__ __forceinline__ void splitk_direct(const TcArgs& a, uint8_t* smem, ui
   const int S = a.splits;
   const uint32_t rank = cluster_rank();
   float* pout = reinterpret_cast<float*>(smem);  // [mt][128] this CTA's partial, token-major
-  const int my_lo = (int)((long long)rank * a.mt / S), my_hi = (int)((long long)(rank + 1) * a.mt / S);
+  const int my_lo = (int)rank * a.mt / S, my_hi = ((int)rank + 1) * a.mt / S;  // 32-bit: mt <= 512, S <= 8
   const int tid = (int)threadIdx.x - 64;  // epilogue thread 0 .. 255
   const int fq = tid & 31;                 // features 4 fq .. 4 fq + 3 of the tile
   const int tsub = tid >> 5;               // token offset within a pass of 8
@@ -822,7 +822,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     if (epi && CS > 1 && egrp < kSumGroupsP) {
       const int ch0 = min(a.rch, a.mt);
       const uint32_t rk = cluster_rank();
-      const int lo = (int)((long long)rk * ch0 / a.splits), hi = (int)((long long)(rk + 1) * ch0 / a.splits);
+      const int lo = (int)rk * ch0 / a.splits, hi = ((int)rk + 1) * ch0 / a.splits;
       const int t0 = egrp * kRows;
       if (t0 < hi - lo) E::load_res(a, tok0 + lo + t0, min(kRows, hi - lo - t0), col0, etid, res_first);
     }
