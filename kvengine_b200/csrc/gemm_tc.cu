@@ -695,13 +695,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       next_stage(r, chunk, rlo, rhi);
     }
   }
+  // After a timeout anywhere in this launch, later CTAs skip their work instead
+  // of each waiting out the limit again. The flag is read before the dependency
+  // wait, so its latency overlaps the previous kernel's tail instead of delaying
+  // the first loads (the CTAs whose timeout it reports run alongside this one; a
+  // timeout of an earlier kernel is seen by the launches after this one).
+  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
   // Everything else touches global memory only after the previous kernel has
   // completed.
   grid_dep_wait();
   grid_dep_launch();
-  // After a timeout anywhere in this launch, later CTAs skip their work instead
-  // of each waiting out the limit again.
-  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
   const int n_iter = aborted ? 0 : n_stages_work;
 
   if (warp == 0) {
@@ -990,11 +993,11 @@ gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap map_w, const __gri
       load_w(sa, it * a.kc, tile_feat0(blockIdx.x), fb);
     }
   }
+  // After a timeout anywhere in this launch every CTA that starts later skips
+  // all of its tiles (read before the dependency wait, as in gemm_tc_kernel).
+  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
   grid_dep_wait();
   grid_dep_launch();
-  // After a timeout anywhere in this launch every CTA that starts later skips
-  // all of its tiles.
-  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
   const int tile_first = aborted ? n_tiles : (int)blockIdx.x;
   const int tile_step = (int)gridDim.x;
 
@@ -1302,9 +1305,10 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_cons
       load_w(sa, it * a.kc, tile_feat0(pair_idx), lead_full + 8u * it);
     }
   }
+  // Read before the dependency wait, as in gemm_tc_kernel.
+  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
   grid_dep_wait();
   grid_dep_launch();
-  const bool aborted = a.status && *reinterpret_cast<volatile int*>(a.status) == KVE_ERR_TIMEOUT;
   const int tile_first = aborted ? n_tiles : pair_idx;
   const int tile_step = (int)(gridDim.x >> 1);
 
