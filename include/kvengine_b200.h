@@ -194,9 +194,9 @@ int kve_gemm_force_shape(int token_tiles, int weight_halves, int k_chunks);
 int kve_gemm_force_splits(int splits);
 
 /* Tuning and test hook (no kvengine counterpart): whether later tcgen05 GEMMs
- * without split-K run as CTA pairs (2-CTA MMA on 256-row tiles): 0 = the cost
- * model's choice, 1 = never, 2 = wherever the shape allows. Results are
- * bit-identical either way. */
+ * without split-K, or with split-K inside the CTA, run as CTA pairs (2-CTA MMA on
+ * 256-row tiles): 0 = the cost model's choice, 1 = never, 2 = wherever the shape
+ * allows. Results are bit-identical either way. */
 int kve_gemm_force_pair(int mode);
 
 /* Tuning and test hook (no kvengine counterpart): whether later tcgen05 GEMMs
@@ -207,9 +207,9 @@ int kve_gemm_force_pair(int mode);
 int kve_gemm_force_rows(int rows);
 
 /* Tuning and test hook (no kvengine counterpart): whether later tcgen05 GEMMs
- * with split-K compute all of a tile's k-ranges in one CTA (one TMEM accumulator
- * per range, summed in the epilogue) instead of over a cluster of CTAs that
- * exchange their partials: 0 = for prompt-sized batches (m >= 2048, the
+ * with split-K compute all of a tile's k-ranges in one CTA or CTA pair (one TMEM
+ * accumulator per range, summed in the epilogue) instead of over a cluster of CTAs
+ * that exchange their partials: 0 = for prompt-sized batches (m >= 2048, the
  * default), 1 = never, 2 = wherever the shape allows. The ranges and the order
  * of their sum are the same either way, so results are bit-identical. */
 int kve_gemm_force_local_split(int mode);

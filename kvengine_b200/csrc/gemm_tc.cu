@@ -615,8 +615,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   // buffers (offset 0) and the output staging (offset stg_off).
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tok0 = blockIdx.x * a.mt;
-  const int feat0 = blockIdx.y * BMT * MH;
+  // LSP grids run the feature tiles fastest: the CTAs of a wave share a few token
+  // tiles and all the weights, which stay in L2, so each activation row comes from
+  // DRAM once (prompt-sized activations overflow L2: 186 MB for the 3B down).
+  const int tok0 = (LSP ? blockIdx.y : blockIdx.x) * a.mt;
+  const int feat0 = (LSP ? blockIdx.x : blockIdx.y) * BMT * MH;
   // Split-K: k-range r is k-blocks [range_lo(r), range_lo(r + 1)). Over a cluster
   // (CS CTAs) this CTA computes range blockIdx.z; with lsplit it computes all LS
   // ranges itself, range r into its own TMEM accumulator, and sums them in the
@@ -1224,9 +1227,12 @@ __device__ __forceinline__ uint32_t umma_idesc_pair(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)((2 * BM) >> 4) << 24);
 }
 
-template <int MODE, bool BF, int NG>
+// LSP (a.lsplit): split-K inside the pair, as in gemm_tc_kernel - every tile's
+// a.splits k-ranges accumulate into their own TMEM accumulators (one buffer).
+template <int MODE, bool BF, int NG, bool LSP = false>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, TcArgs a) {
+  static_assert(!LSP || NG == 1, "in-CTA split-K pair tiles are one token group");
   using E = Epi<MODE, BF>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1244,8 +1250,23 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_cons
   const bool leader = rank == 0;
   const int half_n = a.n_g >> 1;                             // tokens of a group held by each CTA
   const int n_tiles = a.token_tiles * a.feat_ctas;           // pair tiles of 256 weight rows
-  const int n_stages_work = (a.k_blocks + a.kc - 1) / a.kc;
-  const int acc_cols = a.mt;
+  // k-range r = k-blocks [range_lo(r), range_lo(r + 1)); one range without LSP.
+  const int LS = LSP ? a.splits : 1;
+  auto range_lo = [&](int r) { return LSP ? r * a.k_blocks / a.splits : (r ? a.k_blocks : 0); };
+  int n_stages_work = (range_lo(1) + a.kc - 1) / a.kc;  // per tile
+  if constexpr (LSP)
+    for (int r = 1; r < LS; ++r) n_stages_work += (range_lo(r + 1) - range_lo(r) + a.kc - 1) / a.kc;
+  // Walk to the next stage of a tile: `chunk` is its first k-block, in range r = [rlo, rhi).
+  auto next_stage = [&](int& r, int& chunk, int& rlo, int& rhi) {
+    chunk += a.kc;
+    if (LSP && chunk >= rhi) {
+      ++r;
+      rlo = chunk = rhi;
+      rhi = range_lo(r + 1);
+    }
+  };
+  const int kb1_0 = range_lo(1);
+  const int acc_cols = a.mt * LS;
   uint32_t tmem_cols = 32;
   while ((int)tmem_cols < a.acc_bufs * acc_cols) tmem_cols <<= 1;
 
@@ -1277,8 +1298,12 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_cons
   const uint32_t lead_acc_empty = map_to(smem_u32(acc_empty), 0);
   const uint32_t peer_empty = map_to(smem_u32(empty), rank ^ 1u);
   const uint32_t peer_acc_full = map_to(smem_u32(acc_full), rank ^ 1u);
-  auto tile_tok0 = [&](int t) { return (t % a.token_tiles) * a.mt; };
-  auto tile_feat0 = [&](int t) { return (t / a.token_tiles) * 2 * BM + (int)rank * BM; };  // this CTA's rows
+  // Tile t: token tiles fastest (the pairs of a round share the weight tiles), or
+  // with LSP feature tiles fastest (they share the token tiles, as in gemm_tc_kernel).
+  auto tile_tok0 = [&](int t) { return (LSP ? t / a.feat_ctas : t % a.token_tiles) * a.mt; };
+  auto tile_feat0 = [&](int t) {  // this CTA's rows
+    return (LSP ? t % a.feat_ctas : t / a.token_tiles) * 2 * BM + (int)rank * BM;
+  };
   // Stage layout: weights [kc][128][64], then per token group this CTA's half
   // [kc][n_g / 2][64] (SW128 K-major slabs).
   auto load_w = [&](uint8_t* dst, int chunk, int feat0, uint32_t fb) {
@@ -1300,9 +1325,11 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_cons
     prefetch_map(&map_w);
     prefetch_map(&map_x);
     uint8_t* sa = smem;
+    int r = 0, chunk = 0, rlo = 0, rhi = kb1_0;
     for (int it = 0; it < pre; ++it, sa += a.stage_bytes) {
       if (leader) mbar_add_tx(smem_u32(&full[it]), 2 * a.w_bytes);
-      load_w(sa, it * a.kc, tile_feat0(pair_idx), lead_full + 8u * it);
+      load_w(sa, chunk, tile_feat0(pair_idx), lead_full + 8u * it);
+      next_stage(r, chunk, rlo, rhi);
     }
   }
   // Read before the dependency wait, as in gemm_tc_kernel.
@@ -1321,7 +1348,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_cons
       bool ok = true;
       for (int tile = tile_first, ti = 0; ok && tile < n_tiles; tile += tile_step, ++ti) {
         const int tok0 = tile_tok0(tile), feat0 = tile_feat0(tile);
-        int chunk = 0;
+        int r = 0, chunk = 0, rlo = 0, rhi = kb1_0;
         for (int it = 0; it < n_stages_work; ++it) {
           if (issued >= a.stages && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, a.status)) {
             ok = false;
@@ -1336,7 +1363,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_cons
           }
           load_x(sa + a.w_bytes, chunk, tok0, fb);
           ++issued;
-          chunk += a.kc;
+          next_stage(r, chunk, rlo, rhi);
           if (++s == a.stages) {
             s = 0;
             ph ^= 1u;
@@ -1379,26 +1406,27 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_cons
           if (!mbar_wait(smem_u32(&acc_empty[ab]), (uint32_t)(use - 1) & 1u, a.status)) break;
           fence_after();
         }
-        const uint32_t tacc = tmem_base + (uint32_t)(ab * acc_cols);
-        int chunk = 0;
+        const uint32_t tacc0 = tmem_base + (uint32_t)(ab * acc_cols);
+        int r = 0, chunk = 0, rlo = 0, rhi = kb1_0;
         for (int it = 0; it < n_stages_work; ++it) {
           if (!mbar_wait(smem_u32(&full[s]), ph, a.status)) {
             ok = false;
             break;
           }
           fence_after();
-          const int nch = min(a.kc, a.k_blocks - chunk);
+          const int nch = min(a.kc, rhi - chunk);  // a range's partial last stage multiplies only its own chunks
+          const uint32_t tacc = tacc0 + (LSP ? (uint32_t)(r * a.mt) : 0u);
           for (int j = 0; j < nch; ++j) {
             const uint64_t ad = a0 + soff + j * a_chunk, bd = b0 + soff + j * b_chunk;
 #pragma unroll
             for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-              const uint32_t acc = (it > 0 || j > 0 || kk > 0) ? 1u : 0u;
+              const uint32_t acc = (chunk > rlo || j > 0 || kk > 0) ? 1u : 0u;
 #pragma unroll
               for (int g = 0; g < NG; ++g)
                 umma_bf16_pair(tacc + g * a.n_g, ad + kk * kstep, bd + g * grp_step + kk * kstep, idesc, acc);
             }
           }
-          chunk += a.kc;
+          next_stage(r, chunk, rlo, rhi);
           umma_commit_pair(smem_u32(&empty[s]));
           umma_commit_pair(peer_empty + 8u * s);
           if (++s == a.stages) {
@@ -1452,7 +1480,28 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_cons
           E::load_res(a, tok0 + c0, n, col0, etid, res);
         }
         float v[32];
-        tmem_load_cols(t_acc + c0, n, have, v);
+        if constexpr (!LSP) {
+          tmem_load_cols(t_acc + c0, n, have, v);
+        } else {
+          // The LS partials summed from zero in range order (as in gemm_tc_kernel).
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          for (int u = 0; u < LS; ++u) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (h == 1 && n <= 16) break;
+              float p[16];
+              if (have) {
+                tmem_ld16(t_acc + (uint32_t)(u * a.mt) + c0 + 16 * h, p);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) p[i] = 0.f;
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[16 * h + i] += p[i];
+            }
+          }
+        }
         E::template stage<32>(buf, 0, n, f_local, v, bias_f);
         epi_bar(egrp);
         E::copy_out(a, buf, tok0 + c0, n, col0, etid, res);
@@ -1546,7 +1595,26 @@ GemmKernel kernel_of() {
   else return gemm_tc_kernel<MODE, BF, NG, MH>;
 }
 
-// The in-CTA split-K kernel (one 128-row half, one token group).
+// The in-CTA split-K kernels (one token group): one-tile (one 128-row half) and CTA pairs.
+GemmKernel lsplit_pair_kernel_for(int mode, int out_dtype) {
+  const bool bf = out_dtype == KVE_BF16;
+  switch (mode) {
+    case KVE_EPI_STORE:
+      return bf ? gemm_tc_pair_kernel<KVE_EPI_STORE, true, 1, true> : gemm_tc_pair_kernel<KVE_EPI_STORE, false, 1, true>;
+    case KVE_EPI_BIAS:
+      return bf ? gemm_tc_pair_kernel<KVE_EPI_BIAS, true, 1, true> : gemm_tc_pair_kernel<KVE_EPI_BIAS, false, 1, true>;
+    case KVE_EPI_RESIDUAL:
+      return bf ? gemm_tc_pair_kernel<KVE_EPI_RESIDUAL, true, 1, true>
+                : gemm_tc_pair_kernel<KVE_EPI_RESIDUAL, false, 1, true>;
+    case KVE_EPI_SILU_MUL:
+      return bf ? gemm_tc_pair_kernel<KVE_EPI_SILU_MUL, true, 1, true>
+                : gemm_tc_pair_kernel<KVE_EPI_SILU_MUL, false, 1, true>;
+    case kEpiQkvRope:
+      return bf ? gemm_tc_pair_kernel<kEpiQkvRope, true, 1, true> : nullptr;
+    default:
+      return nullptr;
+  }
+}
 GemmKernel lsplit_kernel_for(int mode, int out_dtype) {
   const bool bf = out_dtype == KVE_BF16;
   switch (mode) {
@@ -1640,6 +1708,8 @@ void configure_kernel() {
               if (rk) cudaFuncSetAttribute(rk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
               GemmKernel lk = lsplit_kernel_for(mode, dt);
               if (lk) cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
+              GemmKernel lp = lsplit_pair_kernel_for(mode, dt);
+              if (lp) cudaFuncSetAttribute(lp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kSmemLimit - 512));
             }
           }
   });
@@ -1874,8 +1944,14 @@ std::atomic<int> g_force_local{0};
 // many tiles to spread over the SMs, one CTA can instead compute all S ranges of
 // its tile, range r into its own TMEM accumulator (S x mt <= 512 columns), and sum
 // them in the epilogue in the same order from the same zero start: the same bits
-// as the cluster reduction, without the exchange.
-void try_local_split(Plan& p, int m) {
+// as the cluster reduction, without the exchange. Where the features allow, the
+// tiles run on CTA pairs (2-CTA MMA, 256 weight rows; each SM stages half of the
+// tokens, so 85 instead of 64 FLOP per staged byte at 128 tokens), walked by the
+// resident pairs with one accumulator set per pair. Both forms run the feature
+// tiles fastest: 3B down over 8448 rows 0.56 ms over a cluster, 0.50 ms on one-CTA
+// tiles in token order (1.45 GB read from DRAM per launch), 0.41 ms on pairs in
+// feature order (0.52 GB).
+void try_local_split(Plan& p, int m, int row_bytes) {
   const int force = g_force_local.load();
   if (force == 1 || p.splits < 2 || !p.tma3d) return;
   if (force != 2 && m < kLargeM) return;
@@ -1904,6 +1980,27 @@ void try_local_split(Plan& p, int m) {
   p.rch = per;
   p.stg_off = 0;
   p.grid_x = p.token_tiles * p.feat_tiles;
+  // Pairs only for an even number of 128-row feature tiles: an odd one leaves half of
+  // every last pair tile idle (the 0.5B down, 7 tiles: 0.158 ms as pairs against
+  // 0.145-0.150 ms on one-CTA tiles over 8192 rows).
+  const int fp = g_force_pair.load();
+  if (fp == 1 || p.feat_tiles < 2 || (fp != 2 && p.feat_tiles % 2) || per < 32 || per % 16) return;
+  const size_t stg = persist_staging(row_bytes);
+  const int kc2 = chunks_for(1, per / 2, 1, true, kAvail - stg);
+  const uint32_t w2 = (uint32_t)(BM * BK * 2 * kc2);
+  const uint32_t sb2 = w2 + (uint32_t)(per / 2 * BK * 2 * kc2);
+  const int st2 = (int)std::min<size_t>(kMaxStages, (kAvail - stg) / sb2);
+  if (st2 < 2) return;
+  p.pair = true;
+  p.kc = kc2;
+  p.w_bytes = w2;
+  p.stage_bytes = sb2;
+  p.stages = st2;
+  p.stg_bytes = (int)stg;
+  const long long tiles = (long long)((p.feat_tiles + 1) / 2) * p.token_tiles;
+  const long long pairs = cluster_capacity()[2] / 2 > 0 ? cluster_capacity()[2] / 2 : 1;
+  const long long rounds = (tiles + pairs - 1) / pairs;
+  p.grid_x = (int)(2 * ((tiles + rounds - 1) / rounds));  // CTAs: two per pair
 }
 
 Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
@@ -2001,7 +2098,7 @@ Plan make_plan_uncached(int m, int n, int k, int row_bytes) {
       }
     }
   }
-  try_local_split(p, m);
+  try_local_split(p, m, row_bytes);
   return p;
 }
 
@@ -2101,7 +2198,7 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
                  (e.mode != KVE_EPI_RESIDUAL || (uintptr_t)e.residual % 16 == 0);
   const bool persist = p.stg_bytes > 0;
   GemmKernel kern = p.bmt == 64 ? rows64_kernel_for(e.mode, e.out_dtype)
-                  : p.lsplit ? lsplit_kernel_for(e.mode, e.out_dtype)
+                  : p.lsplit ? (p.pair ? lsplit_pair_kernel_for(e.mode, e.out_dtype) : lsplit_kernel_for(e.mode, e.out_dtype))
                   : p.pair ? pair_kernel_for(e.mode, e.out_dtype, p.ng) : kernel_for(e.mode, e.out_dtype, p.ng, p.mh, persist);
   if (!kern) return set_error(KVE_ERR_DTYPE, "kve_gemm(tcgen05): epilogue %d needs bf16 output", e.mode);
   CUtensorMap mw, mx;
@@ -2116,7 +2213,9 @@ int gemm_tc(const void* x, const void* w, int m, int n, int k, const EpiArgs& e,
   attr.val.clusterDim.y = 1;
   const int cl_splits = p.lsplit ? 1 : p.splits;  // CTAs of a cluster splitting K
   attr.val.clusterDim.z = cl_splits;
-  const dim3 grid = persist ? dim3(p.grid_x, 1, 1) : dim3(p.token_tiles, a.feat_ctas, cl_splits);
+  const dim3 grid = persist     ? dim3(p.grid_x, 1, 1)
+                    : p.lsplit ? dim3(a.feat_ctas, p.token_tiles, 1)  // feature tiles fastest
+                               : dim3(p.token_tiles, a.feat_ctas, cl_splits);
   cudaError_t err = launch_kernel_ex(kern, grid, dim3(kThreads),
                                      (size_t)p.stages * p.stage_bytes + p.stg_bytes + 1024 + 512, stream, &attr,
                                      (cl_splits > 1 || p.pair) ? 1 : 0, mw, mx, a);

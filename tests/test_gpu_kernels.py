@@ -497,11 +497,11 @@ def test_gemm_launch_shapes_give_identical_bits(cuda_device):
 
 
 def test_gemm_split_k_inside_one_cta_gives_identical_bits(cuda_device):
-    """Split-K computed inside one CTA (one TMEM accumulator per k-range, summed in
-    the epilogue; the default for prompt-sized batches) reproduces the cluster
-    reduction bit for bit, for every epilogue and both output types, and a
-    prompt-sized batch's rows equal the same rows computed in a decode-sized batch
-    (which splits over a cluster)."""
+    """Split-K computed inside one CTA or one CTA pair (one TMEM accumulator per
+    k-range, summed in the epilogue; the default for prompt-sized batches)
+    reproduces the cluster reduction bit for bit, for every epilogue and both
+    output types, and a prompt-sized batch's rows equal the same rows computed in a
+    decode-sized batch (which splits over a cluster)."""
     lib = L.load()
     g = torch.Generator(device=cuda_device).manual_seed(21)
     # (m, n, k, epilogue, forced split factor or 0 for the (n, k) rule)
@@ -530,9 +530,11 @@ def test_gemm_split_k_inside_one_cta_gives_identical_bits(cuda_device):
 
                 L.check(lib.kve_gemm_force_local_split(1))  # over a cluster
                 ref = run()
-                L.check(lib.kve_gemm_force_local_split(2))  # inside one CTA
-                got = run()
-                assert torch.equal(got, ref), (m, n, k, epi, fs, out_dtype)
+                L.check(lib.kve_gemm_force_local_split(2))  # inside one CTA / one CTA pair
+                for pair in (1, 2):  # one-CTA tiles only / CTA pairs wherever valid
+                    L.check(lib.kve_gemm_force_pair(pair))
+                    got = run()
+                    assert torch.equal(got, ref), (m, n, k, epi, fs, out_dtype, pair)
                 L.check(lib.kve_gemm_force_local_split(0))  # the rule (inside one CTA from m = 2048)
                 assert torch.equal(run(), ref), (m, n, k, epi, fs, out_dtype)
                 if m >= 2048 and out_dtype == torch.bfloat16:
@@ -543,6 +545,7 @@ def test_gemm_split_k_inside_one_cta_gives_identical_bits(cuda_device):
     finally:
         L.check(lib.kve_gemm_force_local_split(0))
         L.check(lib.kve_gemm_force_splits(0))
+        L.check(lib.kve_gemm_force_pair(0))
 
 
 def test_gemm_repeatable_and_no_workspace(cuda_device):
