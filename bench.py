@@ -537,8 +537,12 @@ def run_micro(args):
         # Config 4's decode attention: the draft pass (0.5B: 14 query / 2 kv heads, hd 64,
         # one row per sequence) and the verify pass (3B: 16 / 2 heads, hd 128, k + 1 = 5 rows),
         # 64 sequences at context 190, block size 16; 8 disjoint block sets, cycled.
-        for name, nq, nkv, hd, qlen in (("draft", 14, 2, 64, 1), ("verify", 16, 2, 128, 5)):
-            B, ctx_len, bs = 64, 190, 16
+        # Also the prompt pass (fused into the first verify: 128 prompt ids + k + 1 = 132 rows
+        # per sequence on the 3B; 128 on the draft), causal over its own rows.
+        for name, nq, nkv, hd, qlen, ctx_len in (("draft", 14, 2, 64, 1, 190), ("verify", 16, 2, 128, 5, 190),
+                                                  ("draft prompt", 14, 2, 64, 128, 128),
+                                                  ("verify prompt", 16, 2, 128, 132, 132)):
+            B, bs = 64, 16
             nbs = -(-ctx_len // bs)
             shape = (B * nbs * 8, bs, nkv, hd)
             dk = torch.randn(shape, device=dev).to(torch.bfloat16)  # timing only: any finite contents

@@ -214,6 +214,15 @@ int kve_gemm_force_rows(int rows);
  * of their sum are the same either way, so results are bit-identical. */
 int kve_gemm_force_local_split(int mode);
 
+/* Self-test of the device-side timeout path (no kvengine counterpart). Every
+ * spin-wait of this library is bounded (2 s) and, when it gives up, records
+ * KVE_ERR_TIMEOUT in *dev_status and lets its kernel return instead of hanging the
+ * GPU. This launches one thread that waits, through that same bounded mbarrier
+ * wait with its limit cut to limit_ns (0 .. 2e9), on a barrier nothing arrives
+ * at: afterwards *dev_status holds KVE_ERR_TIMEOUT (if it was 0) and the context
+ * is usable. */
+int kve_selftest_mbar_timeout(int* dev_status, int64_t limit_ns, cudaStream_t stream);
+
 /* The tcgen05 GEMM's launch plan for an [m, k] x [n, k]^T product with a bf16
  * output (no kvengine counterpart): out[0..12] = split-K factor, token tiles,
  * token groups per tile, tokens per group, weight halves, k-chunks per stage,

@@ -83,6 +83,7 @@ _SIGNATURES = {
     "kve_gemm_force_splits": (i32, [i32]),
     "kve_gemm_force_rows": (i32, [i32]),
     "kve_gemm_force_local_split": (i32, [i32]),
+    "kve_selftest_mbar_timeout": (i32, [vp, i64, vp]),
     "kve_gemm_plan_info": (i32, [i32, i32, i32, vp]),
     "kve_gemm_ex": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, i32, vp, sz, vp, i32, vp]),
     "kve_forward_gemm_ws_bytes": (sz, [C.POINTER(ModelT), i32, i32]),

@@ -7,6 +7,7 @@ within the 2e-2 absolute tolerance the task states for bf16 logits.
 
 import ctypes
 import hashlib
+import time
 
 import numpy as np
 import pytest
@@ -546,6 +547,50 @@ def test_gemm_split_k_inside_one_cta_gives_identical_bits(cuda_device):
         L.check(lib.kve_gemm_force_local_split(0))
         L.check(lib.kve_gemm_force_splits(0))
         L.check(lib.kve_gemm_force_pair(0))
+
+
+def test_bounded_wait_gives_up_and_context_survives(cuda_device):
+    """The device-side timeout path. A wait that can never complete (an mbarrier that
+    nothing arrives at, through the library's bounded wait with its limit cut to 50
+    ms) gives up, records KVE_ERR_TIMEOUT in the status word and lets its kernel
+    return; the context stays usable. GEMMs launched while the status word already
+    holds KVE_ERR_TIMEOUT (one-CTA tiles, a split-K cluster, CTA pairs) skip their
+    work and return at once instead of each waiting out the limit; their outputs
+    are not meaningful, and the status word keeps the first error."""
+    lib = L.load()
+    timeout = next(c for c, name in L.KVE_ERR.items() if name == "KVE_ERR_TIMEOUT")
+    stream = L.stream_handle(cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    L.check(lib.kve_selftest_mbar_timeout(status.data_ptr(), 50_000_000, stream))
+    torch.cuda.synchronize()
+    assert int(status.item()) == timeout
+    assert time.perf_counter() - t0 < 1.5  # the 50 ms limit, not the library's 2 s
+
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+
+    def check_gemm():
+        x = torch.randn(64, 896, device=cuda_device, generator=g).to(torch.bfloat16)
+        w = (torch.randn(1152, 896, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+        got = ops.gemm(x, w, out_dtype=torch.float32)
+        torch.testing.assert_close(got, x.float() @ w.float().t(), rtol=1e-4, atol=1e-3)
+
+    check_gemm()  # the context still computes correctly
+    flagged = torch.full((1,), timeout, dtype=torch.int32, device=cuda_device)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for m, n, k, epi in ((64, 1152, 896, L.EPI_BIAS), (64, 896, 4864, L.EPI_RESIDUAL),
+                         (320, 22016, 2048, L.EPI_SILU_MUL), (2100, 2048, 11008, L.EPI_RESIDUAL)):
+        x = torch.randn(m, k, device=cuda_device, generator=g).to(torch.bfloat16)
+        w = (torch.randn(n, k, device=cuda_device, generator=g) * 0.05).to(torch.bfloat16)
+        bias = torch.zeros(n, device=cuda_device) if epi == L.EPI_BIAS else None
+        res = torch.zeros(m, n, dtype=torch.bfloat16, device=cuda_device) if epi == L.EPI_RESIDUAL else None
+        ops.gemm(x, w, epilogue=epi, bias=bias, residual=res, out=res, status=flagged)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 1.5
+    assert int(flagged.item()) == timeout
+    check_gemm()
 
 
 def test_gemm_repeatable_and_no_workspace(cuda_device):
